@@ -1,0 +1,200 @@
+/*
+ * sc_b200.h -- C ABI of libsc_b200.so, the sm_100a kernels behind the
+ * tensor-parallel quantized decode path of shardcompute.
+ *
+ * Conventions
+ *   - Every entry point is extern "C", returns an int status (SC_OK = 0),
+ *     takes device pointers + sizes + a cudaStream_t, and keeps no reference
+ *     to any buffer after it returns.  Calls enqueue work on `stream` and do
+ *     not synchronise; they are safe to capture in a CUDA graph.
+ *   - Buffers are caller-owned.  Entry points that need scratch take a
+ *     `workspace` pointer and size; the matching *_workspace_bytes() query
+ *     gives the size.  Nothing here allocates device memory.
+ *   - fp16 tensors are passed as uint16_t*; dtype codes are SC_F16 / SC_F32.
+ *   - The weight format is MLX's group-wise affine format that the reference
+ *     stores in its shards: wq uint32 [rows, K*bits/32] with element j of a
+ *     word at bits [bits*j, bits*(j+1)); scales/biases fp16 [rows, K/group];
+ *     dequant w = scale*q + bias.
+ *   - sc_last_error() returns a thread-local message for the last failure.
+ *
+ * Reference interfaces replaced (paths inside Aarjav0210/shardcompute):
+ *   see the comment above each declaration.
+ */
+#ifndef SC_B200_H
+#define SC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_ABI_VERSION 1
+
+enum sc_status {
+  SC_OK = 0,
+  SC_ERR_SHAPE = 1,       /* maps to ValueError in the Python layer */
+  SC_ERR_CUDA = 2,        /* RuntimeError */
+  SC_ERR_NCCL = 3,        /* RuntimeError */
+  SC_ERR_TIMEOUT = 4,     /* TimeoutError */
+  SC_ERR_ARG = 5,         /* ValueError (null pointer, bad enum) */
+  SC_ERR_UNSUPPORTED = 6, /* NotImplementedError */
+  SC_ERR_WORKSPACE = 7    /* ValueError: workspace too small */
+};
+
+enum sc_dtype { SC_F16 = 0, SC_F32 = 1, SC_I32 = 2 };
+
+/* Epilogues of the fused quantized linear. */
+enum sc_epilogue {
+  SC_EPI_STORE = 0,    /* y = x.W^T (+ bias)                              */
+  SC_EPI_RESIDUAL = 1, /* y = residual + x.W^T (+ bias); y may alias it   */
+  SC_EPI_SWIGLU = 2    /* two segments: y = silu(x.W0^T) * (x.W1^T)       */
+};
+
+enum sc_reduce_op { SC_OP_SUM = 0, SC_OP_MAX = 1, SC_OP_MIN = 2, SC_OP_AVG = 3 };
+
+int sc_abi_version(void);
+const char* sc_status_name(int status);
+const char* sc_last_error(void);
+
+/* ------------------------------------------------------------------ K1 --
+ * Quantized linear: y[M, N] = x[M, K] . dequant(wq, scales, biases)^T + bias
+ * Replaces the mx.quantized_matmul(x, w, scales, biases, transpose=True,
+ * group_size, bits) calls of
+ *   parallel/quantized_linear.py:168-176  QuantizedColumnParallelLinear.forward
+ *   parallel/quantized_linear.py:206-214  QuantizedColumnParallelLinear.forward_sync
+ *   parallel/quantized_linear.py:435-443  QuantizedRowParallelLinear.forward (partial)
+ *   parallel/quantized_linear.py:472-480  QuantizedRowParallelLinear.forward_partial
+ * and the tied LM head matmul of parallel/transformer.py:565-569.
+ *   x: fp16 or fp32 [M, ldx]; bias: fp16 [N] or NULL; y: fp16 or fp32 [M, ldy].
+ *   bits in {4, 8}; group_size in {32, 64, 128}; K % group_size == 0.
+ *   Any M >= 1; M <= 16 runs as one weight pass per 16 rows of x.
+ */
+size_t sc_qlinear_workspace_bytes(int M, int K, int N, int bits);
+int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx,
+               const uint32_t* wq, const uint16_t* scales, const uint16_t* biases,
+               int N, int group_size, int bits, const uint16_t* bias,
+               void* y, int y_dtype, int ldy,
+               void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Device-side error word of the quantized-linear kernels: nonzero after a
+ * kernel gave up on a bounded wait (it then stops without touching the
+ * output).  Synchronises with the device; reset != 0 clears it.  No
+ * reference counterpart (the reference has no device code). */
+int sc_qgemv_device_error(int reset);
+
+/* Fused form used by the decode engine (no reference counterpart as one
+ * call; it fuses the reference's RMSNorm -> q/k/v or gate/up linears ->
+ * SiLU*mul, and linear -> residual add, parallel/transformer.py:240-252,
+ * parallel/mlp.py:239-245).
+ *   norm_weight: fp16 [K] or NULL; when set, each x row is RMS-normalised
+ *     (x / sqrt(mean(x^2) + eps) * w) before the product.
+ *   nseg segments (1..3) share x; for SC_EPI_STORE / SC_EPI_RESIDUAL their
+ *   rows are concatenated along N (y has sum(seg_rows) columns); for
+ *   SC_EPI_SWIGLU nseg must be 2 with equal rows and y = silu(y0) * y1.
+ *   residual: fp32 [M, ldr] (SC_EPI_RESIDUAL only). */
+int sc_qlinear_fused(const void* x, int x_dtype, int M, int K, int ldx,
+                     const uint16_t* norm_weight, float norm_eps,
+                     int nseg, const uint32_t* const* wq, const uint16_t* const* scales,
+                     const uint16_t* const* biases, const int* seg_rows,
+                     int group_size, int bits, const uint16_t* bias, int epilogue,
+                     void* y, int y_dtype, int ldy, const float* residual, int ldr,
+                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* ------------------------------------------------------------------ K3 --
+ * Vocab-split embedding gather.  Replaces QuantizedParallelEmbedding.forward
+ * before its all-reduce (parallel/embedding.py:322-356): local = id - v0,
+ * rows with id outside [v0, v1) are zero, others are dequantized exactly
+ * (fp16 of scale*q + bias, one rounding).  The table holds v1 - v0 rows.
+ * out: fp16 or fp32 [n, H]. */
+int sc_embed_gather_q(const int32_t* ids, int n, const uint32_t* wq, const uint16_t* scales,
+                      const uint16_t* biases, int vocab_start, int vocab_end, int H,
+                      int group_size, int bits, void* out, int out_dtype, cudaStream_t stream);
+/* fp16-table variant of the same masked gather (vocab-split fp16 table). */
+int sc_embed_gather_f16(const int32_t* ids, int n, const uint16_t* table, int vocab_start,
+                        int vocab_end, int H, void* out, int out_dtype, cudaStream_t stream);
+
+/* mx.dequantize of a whole table (QuantizedParallelEmbedding.dequantize_weight,
+ * parallel/embedding.py:369-379): out fp16 [rows, K]. */
+int sc_dequantize(const uint32_t* wq, const uint16_t* scales, const uint16_t* biases,
+                  int rows, int K, int group_size, int bits, uint16_t* out, cudaStream_t stream);
+/* Group-wise affine quantization (the mx.quantize calls of
+ * parallel/quantized_linear.py:116,353 and parallel/embedding.py:303):
+ * per group bias = min, scale = (max - min) / (2^bits - 1), both rounded to
+ * fp16, q = clamp(rint((w - bias) / scale)).  w: fp16 [rows, K]. */
+int sc_quantize(const uint16_t* w, int rows, int K, int group_size, int bits,
+                uint32_t* wq, uint16_t* scales, uint16_t* biases, cudaStream_t stream);
+
+/* ------------------------------------------------------------------ K4 --
+ * RoPE + KV append.  Replaces RoPE.__call__ and the KV concatenation of
+ * ParallelAttention.forward (parallel/attention.py:421-433).
+ *   qkv: fp32 [B*S, (Hq + 2*Hkv) * hd], per token the q heads, then k, then v.
+ *   *pos (device int32): cache length before this call; token s of every
+ *   sequence goes to position *pos + s (all sequences share one length).
+ *   Positions at or past Lmax / max_pos are not written.
+ *   cos_tab/sin_tab: fp32 [max_pos, hd/2].
+ *   q_out: fp32 [B*S, Hq*hd]; k_cache/v_cache: fp16 [B, Hkv, Lmax, hd]. */
+int sc_rope_append(const float* qkv, int B, int S, int Hq, int Hkv, int hd,
+                   const int32_t* pos, const float* cos_tab, const float* sin_tab, int max_pos,
+                   float* q_out, uint16_t* k_cache, uint16_t* v_cache, int Lmax,
+                   cudaStream_t stream);
+
+/* Split-KV GQA flash-decode over the preallocated cache.  Replaces
+ * parallel/attention.py:436-466 (GQA repeat, q.k^T*scale, causal mask,
+ * softmax, @v).  Query s of sequence b sees keys [0, min(*pos + s, Lmax-1)].
+ *   q: fp32 [B*S, Hq*hd]; out: fp16 or fp32 [B*S, Hq*hd]. */
+size_t sc_flash_decode_workspace_bytes(int B, int S, int Hq, int hd, int splits);
+int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                    const int32_t* pos, int B, int S, int Hq, int Hkv, int hd, int Lmax,
+                    float scale, int splits, void* out, int out_dtype,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* ------------------------------------------------------------------ K5 --
+ * RMSNorm (parallel/transformer.py:46-61): y = x / sqrt(mean(x^2)+eps) * w. */
+int sc_rmsnorm(const void* x, int x_dtype, int M, int H, const uint16_t* w, float eps,
+               void* y, int y_dtype, cudaStream_t stream);
+/* silu(gate) * up (parallel/mlp.py:161-162,245). */
+int sc_silu_mul(const void* gate, const void* up, int in_dtype, size_t n, void* out,
+                int out_dtype, cudaStream_t stream);
+/* y = a + b elementwise (residual adds, parallel/transformer.py:246,252). */
+int sc_add(const void* a, int a_dtype, const void* b, int b_dtype, size_t n, void* y,
+           int y_dtype, cudaStream_t stream);
+
+/* ------------------------------------------------------------------ K7 --
+ * Greedy token (worker/executor.py:276-278) over vocab-split logits.
+ * sc_argmax: per row of logits fp32 [M, ldl] (N columns) the max value and
+ * its lowest index, plus index_offset, into val[M] / idx[M].
+ * sc_argmax_merge: picks, per row, the best of `world` (val, idx) candidates
+ * laid out [world, M] (largest value, lowest index on ties) and writes the
+ * token to token_out[M]; when pos != NULL it also adds pos_advance to *pos. */
+size_t sc_argmax_workspace_bytes(int M, int N);
+int sc_argmax(const float* logits, int M, int N, int ldl, int index_offset,
+              float* val, int32_t* idx, void* workspace, size_t workspace_bytes,
+              cudaStream_t stream);
+int sc_argmax_merge(const float* vals, const int32_t* idxs, int M, int world,
+                    int32_t* token_out, int32_t* pos, int pos_advance, cudaStream_t stream);
+
+/* ------------------------------------------------------------ collectives --
+ * NCCL over NVLink in place of the TCP ring collectives of
+ * collectives/all_reduce.py:58-193 and collectives/all_gather.py:54-162
+ * (Communicator.all_reduce / all_gather / broadcast,
+ * collectives/communicator.py:259-507).  `comm` is an opaque handle. */
+int sc_comm_unique_id(void* uid_out, size_t uid_bytes);
+int sc_comm_init(const void* uid, size_t uid_bytes, int world, int rank, void** comm_out);
+int sc_comm_destroy(void* comm);
+int sc_comm_abort(void* comm);
+/* Non-blocking health check: *async_error = NCCL's asynchronous error code. */
+int sc_comm_poll(void* comm, int* async_error);
+int sc_allreduce(const void* send, void* recv, size_t count, int dtype, int op, void* comm,
+                 cudaStream_t stream);
+int sc_allgather(const void* send, void* recv, size_t count_per_rank, int dtype, void* comm,
+                 cudaStream_t stream);
+int sc_broadcast(const void* send, void* recv, size_t count, int dtype, int root, void* comm,
+                 cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SC_B200_H */

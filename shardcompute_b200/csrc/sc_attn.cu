@@ -1,0 +1,272 @@
+// K4: RoPE + KV-cache append, and split-KV GQA flash-decode.
+//
+// KV cache layout (per layer, per rank): fp16 [B, Hkv, Lmax, hd], preallocated
+// once; token positions come from a device counter so one captured CUDA graph
+// serves every decode step.
+//
+// Flash-decode: grid (splits, Hkv, B*S).  A CTA owns one KV head and the G =
+// Hq/Hkv query heads that share it (GQA packed: K/V are read once for the
+// whole group, never repeated), and a contiguous range of keys.  Inside the
+// CTA, 4 warps interleave over key steps; a key row (hd fp16) is spread over
+// hd/8 lanes with one 16-byte load each, so a warp covers 32*8/hd keys per
+// step.  Each lane group keeps an online-softmax state (max, sum, o[8]) per
+// query head; the states are merged in shared memory and written as one
+// (max, sum, o[hd]) partial per split, which a second kernel merges.
+#include <algorithm>
+
+#include "sc_common.cuh"
+
+namespace sc {
+
+__global__ void rope_append_kernel(const float* __restrict__ qkv, int S, int Hq, int Hkv, int hd,
+                                   const int32_t* __restrict__ pos_ptr, const float* __restrict__ cos_tab,
+                                   const float* __restrict__ sin_tab, int max_pos, float* __restrict__ q_out,
+                                   __half* __restrict__ kc, __half* __restrict__ vc, int Lmax) {
+  const int tok = blockIdx.x;  // b*S + s
+  const int b = tok / S, s = tok % S;
+  const int pos = *pos_ptr + s;
+  const int half = hd / 2;
+  const int width = (Hq + 2 * Hkv) * hd;
+  const float* src = qkv + (size_t)tok * width;
+  const bool pos_ok = pos >= 0 && pos < max_pos && pos < Lmax;
+  const int items = (Hq + Hkv) * half + Hkv * hd;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    if (it < (Hq + Hkv) * half) {
+      const int h = it / half, d = it % half;
+      const float x1 = src[h * hd + d], x2 = src[h * hd + d + half];
+      const float c = pos_ok ? cos_tab[(size_t)pos * half + d] : 1.f;
+      const float sn = pos_ok ? sin_tab[(size_t)pos * half + d] : 0.f;
+      // x*cos + rotate_half(x)*sin, rotate_half = [-x2, x1], products unfused
+      const float o1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, sn));
+      const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+      if (h < Hq) {
+        q_out[(size_t)tok * Hq * hd + h * hd + d] = o1;
+        q_out[(size_t)tok * Hq * hd + h * hd + d + half] = o2;
+      } else if (pos_ok) {
+        const int kh = h - Hq;
+        __half* dst = kc + (((size_t)b * Hkv + kh) * Lmax + pos) * hd;
+        dst[d] = __float2half_rn(o1);
+        dst[d + half] = __float2half_rn(o2);
+      }
+    } else if (pos_ok) {
+      const int r = it - (Hq + Hkv) * half;
+      const int vh = r / hd, d = r % hd;
+      vc[(((size_t)b * Hkv + vh) * Lmax + pos) * hd + d] = __float2half_rn(src[(Hq + Hkv) * hd + vh * hd + d]);
+    }
+  }
+}
+
+constexpr int FD_WARPS = 4;
+
+template <int HD, int G, typename OT>
+__global__ void __launch_bounds__(FD_WARPS * 32)
+flash_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
+                    const int32_t* __restrict__ pos_ptr, int S, int Hq, int Hkv, int Lmax, float scale,
+                    int splits, float* __restrict__ part, OT* __restrict__ out) {
+  constexpr int LPK = HD / 8;    // lanes per key
+  constexpr int KPS = 32 / LPK;  // keys per warp step
+  const int split = blockIdx.x, kvh = blockIdx.y, tok = blockIdx.z;
+  const int b = tok / S, s = tok % S;
+  // keys visible to this query, never past the cache (a position beyond
+  // Lmax was not appended by sc_rope_append either)
+  const int L = min(*pos_ptr + s + 1, Lmax);
+  const int chunk = (L + splits - 1) / splits;
+  const int k_beg = split * chunk;
+  const int k_end = min(L, k_beg + chunk);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / LPK, dl = lane % LPK;
+  const int d0 = dl * 8;
+
+  float qr[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float* qp = q + (size_t)tok * Hq * HD + (size_t)(kvh * G + g) * HD + d0;
+    const float4 a = *reinterpret_cast<const float4*>(qp);
+    const float4 c = *reinterpret_cast<const float4*>(qp + 4);
+    qr[g][0] = a.x; qr[g][1] = a.y; qr[g][2] = a.z; qr[g][3] = a.w;
+    qr[g][4] = c.x; qr[g][5] = c.y; qr[g][6] = c.z; qr[g][7] = c.w;
+  }
+  float m[G], l[G], o[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
+  }
+  const __half* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  const __half* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+
+  for (int k0 = k_beg + warp * KPS; k0 < k_end; k0 += FD_WARPS * KPS) {
+    const int key = k0 + sub;
+    const bool valid = key < k_end;
+    uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
+    if (valid) {
+      kv4 = *reinterpret_cast<const uint4*>(kbase + (size_t)key * HD + d0);
+      vv4 = *reinterpret_cast<const uint4*>(vbase + (size_t)key * HD + d0);
+    }
+    float kf[8], vf[8];
+    {
+      const uint32_t kw[4] = {kv4.x, kv4.y, kv4.z, kv4.w};
+      const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __half22float2(u32_as_h2(kw[i]));
+        const float2 c = __half22float2(u32_as_h2(vw[i]));
+        kf[2 * i] = a.x; kf[2 * i + 1] = a.y;
+        vf[2 * i] = c.x; vf[2 * i + 1] = c.y;
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot = fmaf(qr[g][i], kf[i], dot);
+#pragma unroll
+      for (int off = LPK / 2; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      if (valid) {
+        const float sc = dot * scale;
+        const float mn = fmaxf(m[g], sc);
+        const float corr = expf(m[g] - mn);
+        const float pr = expf(sc - mn);
+        l[g] = l[g] * corr + pr;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[g][i] = fmaf(pr, vf[i], o[g][i] * corr);
+        m[g] = mn;
+      }
+    }
+  }
+
+  // merge the FD_WARPS*KPS lane-group states
+  __shared__ float sm_m[FD_WARPS * KPS][G], sm_l[FD_WARPS * KPS][G];
+  __shared__ float sm_o[FD_WARPS * KPS][G][HD];
+  const int grp = warp * KPS + sub;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (dl == 0) {
+      sm_m[grp][g] = m[g];
+      sm_l[grp][g] = l[g];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sm_o[grp][g][d0 + i] = o[g][i];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * HD; e += FD_WARPS * 32) {
+    const int g = e / HD, d = e % HD;
+    float M = -INFINITY;
+    for (int r = 0; r < FD_WARPS * KPS; ++r) M = fmaxf(M, sm_m[r][g]);
+    float Ls = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int r = 0; r < FD_WARPS * KPS; ++r) {
+        const float w = expf(sm_m[r][g] - M);
+        Ls = fmaf(sm_l[r][g], w, Ls);
+        O = fmaf(sm_o[r][g][d], w, O);
+      }
+    }
+    const int qh = kvh * G + g;
+    if (splits == 1) {
+      out[(size_t)tok * Hq * HD + (size_t)qh * HD + d] = from_f32<OT>(O / Ls);
+    } else {
+      float* pp = part + (((size_t)tok * Hq + qh) * splits + split) * (HD + 2);
+      pp[2 + d] = O;
+      if (d == 0) {
+        pp[0] = M;
+        pp[1] = Ls;
+      }
+    }
+  }
+}
+
+template <int HD, typename OT>
+__global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq, int splits, OT* __restrict__ out) {
+  const int qh = blockIdx.x, tok = blockIdx.y;
+  const float* pp = part + ((size_t)tok * Hq + qh) * splits * (HD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, pp[s * (HD + 2)]);
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float Ls = 0.f, O = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float* q = pp + s * (HD + 2);
+      const float w = q[0] == -INFINITY ? 0.f : expf(q[0] - M);
+      Ls = fmaf(q[1], w, Ls);
+      O = fmaf(q[2 + d], w, O);
+    }
+    out[(size_t)tok * Hq * HD + (size_t)qh * HD + d] = from_f32<OT>(O / Ls);
+  }
+}
+
+template <int HD, int G, typename OT>
+static int launch_fd(const float* q, const __half* kc, const __half* vc, const int32_t* pos, int B, int S, int Hq,
+                     int Hkv, int Lmax, float scale, int splits, float* part, OT* out, cudaStream_t stream) {
+  dim3 grid(splits, Hkv, B * S);
+  flash_decode_kernel<HD, G, OT><<<grid, FD_WARPS * 32, 0, stream>>>(q, kc, vc, pos, S, Hq, Hkv, Lmax, scale, splits,
+                                                                    part, out);
+  int st = check_launch("flash_decode");
+  if (st != SC_OK || splits == 1) return st;
+  flash_decode_merge_kernel<HD, OT><<<dim3(Hq, B * S), HD, 0, stream>>>(part, Hq, splits, out);
+  return check_launch("flash_decode_merge");
+}
+
+template <int HD, typename OT>
+static int dispatch_g(int G, const float* q, const __half* kc, const __half* vc, const int32_t* pos, int B, int S,
+                      int Hq, int Hkv, int Lmax, float scale, int splits, float* part, OT* out, cudaStream_t stream) {
+  switch (G) {
+    case 1: return launch_fd<HD, 1, OT>(q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, out, stream);
+    case 2: return launch_fd<HD, 2, OT>(q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, out, stream);
+    case 4: return launch_fd<HD, 4, OT>(q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, out, stream);
+    case 8: return launch_fd<HD, 8, OT>(q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, out, stream);
+  }
+  set_error("flash_decode: GQA group %d unsupported (1, 2, 4, 8)", G);
+  return SC_ERR_UNSUPPORTED;
+}
+
+}  // namespace sc
+
+extern "C" {
+
+int sc_rope_append(const float* qkv, int B, int S, int Hq, int Hkv, int hd, const int32_t* pos,
+                   const float* cos_tab, const float* sin_tab, int max_pos, float* q_out, uint16_t* k_cache,
+                   uint16_t* v_cache, int Lmax, cudaStream_t stream) {
+  SC_REQUIRE(hd > 0 && hd % 2 == 0, SC_ERR_SHAPE, "rope_append: head_dim must be even");
+  SC_REQUIRE(Hq > 0 && Hkv > 0 && B > 0 && S > 0, SC_ERR_SHAPE, "rope_append: empty shape");
+  SC_REQUIRE(qkv && pos && cos_tab && sin_tab && q_out && k_cache && v_cache, SC_ERR_ARG,
+             "rope_append: null pointer");
+  sc::rope_append_kernel<<<B * S, 256, 0, stream>>>(qkv, S, Hq, Hkv, hd, pos, cos_tab, sin_tab, max_pos, q_out,
+                                                    (__half*)k_cache, (__half*)v_cache, Lmax);
+  return sc::check_launch("rope_append");
+}
+
+size_t sc_flash_decode_workspace_bytes(int B, int S, int Hq, int hd, int splits) {
+  if (splits <= 1) return 0;
+  return (size_t)B * S * Hq * splits * (hd + 2) * sizeof(float);
+}
+
+int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos, int B,
+                    int S, int Hq, int Hkv, int hd, int Lmax, float scale, int splits, void* out, int out_dtype,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  SC_REQUIRE(hd == 64 || hd == 128, SC_ERR_UNSUPPORTED, "flash_decode: head_dim %d unsupported (64, 128)", hd);
+  SC_REQUIRE(Hkv > 0 && Hq % Hkv == 0, SC_ERR_SHAPE, "flash_decode: Hq=%d not a multiple of Hkv=%d", Hq, Hkv);
+  SC_REQUIRE(B > 0 && S > 0 && splits >= 1 && splits <= 1024, SC_ERR_SHAPE, "flash_decode: bad B/S/splits");
+  SC_REQUIRE(q && k_cache && v_cache && pos && out, SC_ERR_ARG, "flash_decode: null pointer");
+  SC_REQUIRE(out_dtype == SC_F16 || out_dtype == SC_F32, SC_ERR_ARG, "flash_decode: out dtype");
+  const size_t need = sc_flash_decode_workspace_bytes(B, S, Hq, hd, splits);
+  SC_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), SC_ERR_WORKSPACE,
+             "flash_decode: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
+  const int G = Hq / Hkv;
+  const __half* kc = (const __half*)k_cache;
+  const __half* vc = (const __half*)v_cache;
+  float* part = (float*)workspace;
+  if (hd == 128) {
+    if (out_dtype == SC_F16)
+      return sc::dispatch_g<128, __half>(G, q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, (__half*)out,
+                                         stream);
+    return sc::dispatch_g<128, float>(G, q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, (float*)out,
+                                      stream);
+  }
+  if (out_dtype == SC_F16)
+    return sc::dispatch_g<64, __half>(G, q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, (__half*)out,
+                                      stream);
+  return sc::dispatch_g<64, float>(G, q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, (float*)out, stream);
+}
+
+}  // extern "C"

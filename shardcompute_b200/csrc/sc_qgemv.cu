@@ -1,0 +1,1206 @@
+// K1: group-wise affine 4/8-bit dequant-GEMV for decode (M <= 16 per pass).
+//
+// y[m, n] = sum_k x[m, k] * w_hat[n, k],  w_hat = fp16(scale*q + bias) (exact,
+// one rounding), fp32 accumulation on the tensor cores (mma.m16n8k16).
+//
+// Layout read (unchanged MLX format of the reference's shards):
+//   wq     uint32 [N, K*bits/32], row n contiguous
+//   scales fp16   [N, K/group]
+//   biases fp16   [N, K/group]
+//
+// Vocabulary: a "chunk" is 16 consecutive uint32 words (64 B) of one weight
+// row; a "tile" is 16 weight rows.  Lane (g = lane/4, t = lane%4) of a warp
+// dequantises words [4t, 4t+4) of a chunk for tile rows g and g+8 into the A
+// registers of mma.m16n8k16; the activation x is the B operand, staged once
+// per CTA in shared memory in exactly the permuted k order the A registers
+// come out in, so no shuffle is needed.  fp16 dequantisation is
+// fma.rn.f16x2(q, scale, bias): bit-identical to the oracle's dequantize.
+//
+// Two kernels:
+//   * qgemv_tma_kernel (main path): warp-specialised TMA pipeline, below.
+//   * qgemv_kernel (fallback for shapes the tensor maps cannot describe:
+//     K*bits/32 not a multiple of 32 words, K/group not a multiple of 8,
+//     unaligned bases, segments not multiples of 16 rows): 128-bit
+//     non-allocating loads straight from HBM into registers.
+// Both split K across CTAs (grid.y) when x's K-slice does not fit in shared
+// memory or there are too few tiles for the SMs; fp32 partials then go to a
+// caller-provided workspace (summed by a second kernel), or, for an in-place
+// fp32 residual epilogue, are added atomically.
+#include <stdarg.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "sc_common.cuh"
+
+namespace sc {
+
+constexpr int QG_WARPS = 8;
+constexpr int QG_THREADS = QG_WARPS * 32;
+constexpr int QG_MAX_SEG = 3;
+constexpr int QG_XS_MAX = 96 * 1024;  // shared-memory budget for the staged x slice (fallback)
+
+struct QSeg {
+  const uint32_t* wq;
+  const uint16_t* s;
+  const uint16_t* b;
+  int rows;
+};
+
+struct QGemvParams {
+  const void* x;
+  int ldx;
+  int M;   // rows of x in this pass (<= 16)
+  int K;
+  const uint16_t* norm_w;
+  float eps;
+  QSeg seg[QG_MAX_SEG];
+  int nseg;
+  int N;   // output columns: sum of segment rows (or rows of one segment for SwiGLU)
+  int group;
+  const uint16_t* bias;
+  void* y;
+  int ldy;
+  const float* residual;
+  int ldr;
+  float* partial;        // [nacc][splits][M][N] when splits > 1
+  int splits;
+  int chunks_per_split;  // chunk count of each K split
+  int tiles;             // ceil(N / 16)
+  int lg_group;          // log2(group)
+};
+
+template <int BITS>
+struct QTraits;
+template <>
+struct QTraits<4> {
+  static constexpr int PF = 8;    // codes per word
+  static constexpr int NMMA = 8;  // mma per chunk per 16-row tile
+  static constexpr int KPC = 128; // k values per chunk
+};
+template <>
+struct QTraits<8> {
+  static constexpr int PF = 4;
+  static constexpr int NMMA = 4;
+  static constexpr int KPC = 64;
+};
+
+// Shared-memory slot (in halves) of x[m][k] for a K-slice starting at k0.
+// Row (kc_local, t) holds M * NMMA * 4 halves plus 8 halves of padding.
+template <int BITS>
+__device__ __forceinline__ int xslot(int kl, int m, int M) {
+  using T = QTraits<BITS>;
+  const int w = kl / T::PF, e = kl % T::PF;
+  const int kc = w >> 4, t = (w >> 2) & 3, j = w & 3;
+  int i, h;
+  if (BITS == 4) {
+    const int p = e & 3, hi = e >> 2;
+    i = 2 * j + (p >> 1);
+    h = 2 * (p & 1) + hi;
+  } else {
+    const int p = e & 1, hi = e >> 1;
+    i = j;
+    h = 2 * p + hi;
+  }
+  const int rowlen = M * T::NMMA * 4 + 8;
+  return (kc * 4 + t) * rowlen + (m * T::NMMA + i) * 4 + h;
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_x(const void* x, size_t idx) {
+  return to_f32<T>(reinterpret_cast<const T*>(x)[idx]);
+}
+
+// Stage x (optionally RMS-normalised) for chunks [kc0, kc1) into `xs`.
+// Threads [0, nthreads) of the CTA take part; `s_rms` holds 16 floats.
+template <int BITS, bool NORM, typename XT>
+__device__ __forceinline__ void stage_x(const QGemvParams& p, __half* xs, float* s_rms, int kc0, int kc1, int tid,
+                                        int nthreads, int bar_id) {
+  using TR = QTraits<BITS>;
+  const int M = p.M;
+  const int rowlen = M * TR::NMMA * 4 + 8;
+  const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
+  if (NORM) {
+    for (int m = warp; m < M; m += nwarps) {
+      float ss = 0.f;
+      for (int k = lane; k < p.K; k += 32) {
+        const float v = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
+        ss = fmaf(v, v, ss);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) s_rms[m] = sqrtf(ss / (float)p.K + p.eps);
+    }
+    named_bar_sync(bar_id, nthreads);
+  }
+  const int nkc = kc1 - kc0;
+  const int k0 = kc0 * TR::KPC;
+  const int span = nkc * TR::KPC;
+  for (int idx = tid; idx < span * M; idx += nthreads) {
+    const int m = idx / span, kl = idx % span;
+    const int k = k0 + kl;
+    float v = 0.f;
+    if (k < p.K) {
+      v = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
+      if (NORM) v = (v / s_rms[m]) * __half2float(__ushort_as_half(p.norm_w[k]));
+    }
+    xs[xslot<BITS>(kl, m, M)] = __float2half_rn(v);
+  }
+  // zero the padding halves so no uninitialised value is ever read
+  for (int r = tid; r < nkc * 4; r += nthreads)
+    for (int h = M * TR::NMMA * 4; h < rowlen; ++h) xs[r * rowlen + h] = __float2half_rn(0.f);
+  named_bar_sync(bar_id, nthreads);
+}
+
+// Epilogue of one output element (row, col) of a tile, from its summed
+// accumulators v[NACC].
+template <int EPI, typename YT>
+__device__ __forceinline__ void epilogue(const QGemvParams& p, int split, bool atomic_out, int row, int col,
+                                         const float* v) {
+  constexpr bool DUAL = (EPI == SC_EPI_SWIGLU);
+  if (atomic_out) {
+    // split-K into an fp32 output that already holds the residual
+    float add = v[0];
+    if (split == 0 && p.bias) add += __half2float(__ushort_as_half(p.bias[row]));
+    atomicAdd(reinterpret_cast<float*>(p.y) + (size_t)col * p.ldy + row, add);
+    return;
+  }
+  if (p.splits > 1) {
+    p.partial[(((size_t)0 * p.splits + split) * p.M + col) * p.N + row] = v[0];
+    if (DUAL) p.partial[(((size_t)1 * p.splits + split) * p.M + col) * p.N + row] = v[DUAL ? 1 : 0];
+    return;
+  }
+  float out;
+  if (DUAL) {
+    out = silu_f32(v[0]) * v[DUAL ? 1 : 0];
+  } else {
+    out = v[0];
+    if (p.bias) out += __half2float(__ushort_as_half(p.bias[row]));
+    if (EPI == SC_EPI_RESIDUAL) out += p.residual[(size_t)col * p.ldr + row];
+  }
+  reinterpret_cast<YT*>(p.y)[(size_t)col * p.ldy + row] = from_f32<YT>(out);
+}
+
+// ---------------------------------------------------------------------------
+// Fallback: direct 128-bit loads from HBM into registers.  A CTA (8 warps)
+// owns a tile at a time; its warps split the tile's chunks along K (warp w
+// takes chunks w, w+8, ...) and the partial tiles are summed through shared
+// memory.
+template <int BITS, int MT, int EPI, bool NORM, typename XT, typename YT>
+__global__ void __launch_bounds__(QG_THREADS)
+qgemv_kernel(const QGemvParams p) {
+  using TR = QTraits<BITS>;
+  constexpr int NMMA = TR::NMMA;
+  constexpr bool DUAL = (EPI == SC_EPI_SWIGLU);
+  constexpr int NACC = DUAL ? 2 : 1;
+  constexpr int UNR = DUAL ? 2 : 4;
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ float s_rms[16];
+  const int M = p.M;
+  const int rowlen = M * NMMA * 4 + 8;  // halves
+  const int split = blockIdx.y;
+  const int kc0 = split * p.chunks_per_split;
+  const int KW = p.K / TR::PF;
+  const int KC = (KW + 15) / 16;
+  const int kc1 = min(KC, kc0 + p.chunks_per_split);
+  const int nkc = kc1 - kc0;
+  __half* xs = reinterpret_cast<__half*>(smem_raw);
+  float* red = reinterpret_cast<float*>(smem_raw + (size_t)nkc * 4 * rowlen * sizeof(__half));
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  stage_x<BITS, NORM, XT>(p, xs, s_rms, kc0, kc1, tid, QG_THREADS, 0);
+
+  const int gsize = p.group;
+  const int KG = p.K / gsize;
+
+  for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+    const int n0 = tile * 16;
+    // resolve the two rows of this lane to (segment pointer, local row)
+    const uint32_t* wrow[NACC][2];
+    const uint16_t* srow[NACC][2];
+    const uint16_t* brow[NACC][2];
+    bool rvalid[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int n = n0 + g + 8 * h;
+      rvalid[h] = n < p.N;
+      int sidx = 0, local = n;
+      if (!DUAL) {
+#pragma unroll
+        for (int s = 0; s < QG_MAX_SEG - 1; ++s)
+          if (s + 1 < p.nseg && local >= p.seg[sidx].rows) { local -= p.seg[sidx].rows; ++sidx; }
+      }
+      if (!rvalid[h]) local = 0;
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+        const QSeg& sg = p.seg[DUAL ? a : sidx];
+        wrow[a][h] = sg.wq + (size_t)local * KW;
+        srow[a][h] = sg.s + (size_t)local * KG;
+        brow[a][h] = sg.b + (size_t)local * KG;
+      }
+    }
+
+    float acc[NACC][MT][4];
+#pragma unroll
+    for (int a = 0; a < NACC; ++a)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[a][mt][r] = 0.f;
+
+    for (int base = kc0 + warp; base < kc1; base += QG_WARPS * UNR) {
+      uint4 wv[UNR][NACC][2];
+      uint32_t sb[UNR][NACC][2];  // (scale | bias << 16) per row
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int kc = base + u * QG_WARPS;
+        const int word = kc * 16 + 4 * t;
+        const bool kval = (kc < kc1) && (word < KW);
+        const int gi = kval ? (word * TR::PF) / gsize : 0;
+#pragma unroll
+        for (int a = 0; a < NACC; ++a)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (kval && rvalid[h]) {
+              wv[u][a][h] = ldg_stream_v4(wrow[a][h] + word);
+              sb[u][a][h] = (uint32_t)ldg_u16(srow[a][h] + gi) | ((uint32_t)ldg_u16(brow[a][h] + gi) << 16);
+            } else {
+              wv[u][a][h] = make_uint4(0, 0, 0, 0);
+              sb[u][a][h] = 0u;  // scale = bias = 0 -> w_hat = 0
+            }
+          }
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int kc = base + u * QG_WARPS;
+        if (kc >= kc1) break;
+        uint32_t bf[MT][NMMA][2];
+        const int kcl = kc - kc0;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const int m = min(mt * 8 + g, M - 1);
+          const uint4* src = reinterpret_cast<const uint4*>(xs + (kcl * 4 + t) * rowlen + m * NMMA * 4);
+#pragma unroll
+          for (int q = 0; q < NMMA / 2; ++q) {
+            const uint4 v = src[q];
+            bf[mt][2 * q][0] = v.x;
+            bf[mt][2 * q][1] = v.y;
+            bf[mt][2 * q + 1][0] = v.z;
+            bf[mt][2 * q + 1][1] = v.w;
+          }
+        }
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          const __half2 s0 = __half2half2(__ushort_as_half((uint16_t)(sb[u][a][0] & 0xffffu)));
+          const __half2 b0 = __half2half2(__ushort_as_half((uint16_t)(sb[u][a][0] >> 16)));
+          const __half2 s1 = __half2half2(__ushort_as_half((uint16_t)(sb[u][a][1] & 0xffffu)));
+          const __half2 b1 = __half2half2(__ushort_as_half((uint16_t)(sb[u][a][1] >> 16)));
+          const uint32_t w0[4] = {wv[u][a][0].x, wv[u][a][0].y, wv[u][a][0].z, wv[u][a][0].w};
+          const uint32_t w1[4] = {wv[u][a][1].x, wv[u][a][1].y, wv[u][a][1].z, wv[u][a][1].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (BITS == 4) {
+              __half2 P0[4], P1[4];
+              unpack_u4(w0[j], P0);
+              unpack_u4(w1[j], P1);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                P0[q] = hfma2_rn(P0[q], s0, b0);
+                P1[q] = hfma2_rn(P1[q], s1, b1);
+              }
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const int i = 2 * j + hh;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                  mma_16816(acc[a][mt], h2_as_u32(P0[2 * hh]), h2_as_u32(P1[2 * hh]),
+                            h2_as_u32(P0[2 * hh + 1]), h2_as_u32(P1[2 * hh + 1]), bf[mt][i][0],
+                            bf[mt][i][1]);
+              }
+            } else {
+              __half2 P0[2], P1[2];
+              unpack_u8(w0[j], P0);
+              unpack_u8(w1[j], P1);
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                P0[q] = hfma2_rn(P0[q], s0, b0);
+                P1[q] = hfma2_rn(P1[q], s1, b1);
+              }
+#pragma unroll
+              for (int mt = 0; mt < MT; ++mt)
+                mma_16816(acc[a][mt], h2_as_u32(P0[0]), h2_as_u32(P1[0]), h2_as_u32(P0[1]),
+                          h2_as_u32(P1[1]), bf[mt][j][0], bf[mt][j][1]);
+            }
+          }
+        }
+      }
+    }
+
+    // ---- cross-warp reduction of the tile ----
+    constexpr int RPL = NACC * MT * 4;  // floats per lane per warp
+#pragma unroll
+    for (int a = 0; a < NACC; ++a)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) red[(warp * 32 + lane) * RPL + (a * MT + mt) * 4 + r] = acc[a][mt][r];
+    __syncthreads();
+    for (int e = tid; e < 32 * MT * 4; e += QG_THREADS) {
+      const int l = e & 31, rr = e >> 5;  // rr = mt*4 + r
+      const int mt = rr >> 2, r = rr & 3;
+      const int row = n0 + (l >> 2) + 8 * (r >> 1);
+      const int col = mt * 8 + 2 * (l & 3) + (r & 1);
+      if (row >= p.N || col >= M) continue;
+      float v[NACC];
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+        float sacc = 0.f;
+#pragma unroll
+        for (int w = 0; w < QG_WARPS; ++w) sacc += red[(w * 32 + l) * RPL + (a * MT + mt) * 4 + r];
+        v[a] = sacc;
+      }
+      epilogue<EPI, YT>(p, split, false, row, col, v);
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Warp-specialised TMA pipeline (the main decode path).
+//
+// One producer warp streams each tile's K-range into a ring of NST
+// shared-memory stages with tensor-map TMA: per stage ONE
+// cp.async.bulk.tensor brings 16 rows x (cps*16) packed words (a 3-D box,
+// 128-byte swizzled), and one each brings the matching 16 x (groups) fp16
+// scales and biases (swizzled to their row width).  All complete on the
+// stage's "full" mbarrier by byte count; a TMA copy has a fixed issue cost,
+// so a stage is a few large boxes rather than many row copies.  Sixteen
+// consumer warps wait on "full", dequantise from shared memory exactly as the
+// fallback does from registers, feed mma.m16n8k16 and release the stage on
+// its "empty" mbarrier, so the producer runs up to NST stages ahead.  Tile
+// rows are read in a permuted order (mma row m <-> tile row tile_row(m)) so
+// the 128-bit shared loads of one quarter-warp hit different swizzle phases
+// and never conflict.  Every wait is bounded in time; on timeout the CTA
+// stops, drains its in-flight copies and records an error readable through
+// sc_qgemv_device_error().
+constexpr int TC_NCW = 16;  // consumer warps
+constexpr int TC_THREADS = (TC_NCW + 1) * 32;
+constexpr int TC_MAX_NST = 8;
+constexpr uint64_t TC_WAIT_NS = 2000000000ull;  // 2 s
+
+static __device__ int g_qgemv_error = 0;
+
+struct TmaGeo {
+  int cps;          // chunks (16 words) per stage
+  int nblk;         // 32-word blocks per stage (cps / 2)
+  int ngs;          // scale groups per stage (box width)
+  int nst;          // ring depth
+  int wset_bytes;   // bytes of one weight set's packed-word box (16 * nblk * 128)
+  int sset_bytes;   // bytes of one scales (or biases) box slot, 1 KB aligned
+  int stage_bytes;  // bytes of one stage (all sets)
+  int ring_off;     // byte offset of the ring in dynamic shared memory (1 KB aligned)
+  int red_off;      // byte offset of the reduction buffer
+  int bar_off;      // byte offset of the mbarriers
+  int atomic_out;   // split-K partials added atomically into y (in-place residual)
+  int row_swz;      // 1: box lines ordered (block, row) with row-dependent swizzle
+  int s_swz;        // scale-box swizzle mask: 0 none, 1 (32 B), 3 (64 B), 7 (128 B)
+};
+
+struct TmaMaps {
+  CUtensorMap w[QG_MAX_SEG];
+  CUtensorMap s[QG_MAX_SEG];
+  CUtensorMap b[QG_MAX_SEG];
+};
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// tile row read by mma row m (0..15): quarter-warps pair rows 4 apart
+__device__ __forceinline__ int tile_row(int m) { return ((m & 7) >> 1) + 4 * (m & 1) + (m & 8); }
+
+// segment of a tile (segments are multiples of 16 rows except the last)
+__device__ __forceinline__ int tile_segment(const QGemvParams& p, int n0, int* base) {
+  int sidx = 0, b = 0;
+#pragma unroll
+  for (int s = 0; s < QG_MAX_SEG - 1; ++s)
+    if (s + 1 < p.nseg && n0 >= b + p.seg[sidx].rows) { b += p.seg[sidx].rows; ++sidx; }
+  *base = b;
+  return sidx;
+}
+
+template <int BITS, int MT, int EPI, bool NORM, typename XT, typename YT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ TmaMaps maps) {
+  using TR = QTraits<BITS>;
+  constexpr int NMMA = TR::NMMA;
+  constexpr bool DUAL = (EPI == SC_EPI_SWIGLU);
+  constexpr int NACC = DUAL ? 2 : 1;
+  constexpr int NA = DUAL ? 2 : 4;  // independent accumulators per weight set
+  constexpr int RPL = NACC * MT * 4;
+  constexpr int NC = TC_NCW * 32;
+
+  extern __shared__ __align__(128) unsigned char smem_tma[];
+  __shared__ int s_abort;
+  __shared__ float s_rms[16];
+
+  const int M = p.M;
+  const int rowlen = M * NMMA * 4 + 8;
+  const int split = blockIdx.y;
+  const int kc0 = split * p.chunks_per_split;
+  const int KW = p.K / TR::PF;
+  const int KC = (KW + 15) / 16;
+  const int kc1 = min(KC, kc0 + p.chunks_per_split);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  // swizzled TMA boxes need 1024-byte aligned shared addresses
+  unsigned char* sbase = smem_tma + ((1024 - (smem_u32(smem_tma) & 1023)) & 1023);
+
+  __half* xs = reinterpret_cast<__half*>(sbase);
+  unsigned char* ring = sbase + geo.ring_off;
+  float* red = reinterpret_cast<float*>(sbase + geo.red_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + geo.bar_off);
+  uint64_t* empty = full + TC_MAX_NST;
+
+  if (tid == 0) {
+    for (int s = 0; s < geo.nst; ++s) {
+      mbar_init(&full[s], 1);  // one expect_tx arrival; completion by the copies' bytes
+      mbar_init(&empty[s], TC_NCW);
+    }
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == TC_NCW) {
+    // ============================ producer ============================
+    if (lane == 0) {
+      uint32_t it = 0;
+      const uint32_t tx = (uint32_t)(NACC * (geo.wset_bytes + 2 * 16 * geo.ngs * 2));
+      for (int tile = blockIdx.x; tile < p.tiles && !s_abort; tile += gridDim.x) {
+        const int n0 = tile * 16;
+        int sbase_row = 0;
+        const int sidx = DUAL ? 0 : tile_segment(p, n0, &sbase_row);
+        const int row0 = n0 - sbase_row;
+        for (int kcs = kc0; kcs < kc1; kcs += geo.cps) {
+          const int s = it % geo.nst;
+          const uint32_t ph = (it / geo.nst) & 1;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1, &s_abort, TC_WAIT_NS)) break;
+          unsigned char* st = ring + (size_t)s * geo.stage_bytes;
+          const int blk0 = kcs / 2;                // 32-word blocks
+          const int g0 = kcs * TR::KPC / p.group;  // scale groups
+          mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+          for (int a = 0; a < NACC; ++a) {
+            const int mi = DUAL ? a : sidx;
+            unsigned char* wd = st + a * geo.wset_bytes;
+            if (geo.row_swz)
+              tma_load_3d(wd, &maps.w[mi], 0, row0, blk0, &full[s]);
+            else
+              tma_load_3d(wd, &maps.w[mi], 0, blk0, row0, &full[s]);
+            unsigned char* sd = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
+            tma_load_2d(sd, &maps.s[mi], g0, row0, &full[s]);
+            tma_load_2d(sd + geo.sset_bytes, &maps.b[mi], g0, row0, &full[s]);
+          }
+          ++it;
+        }
+      }
+      if (s_abort) {
+        // drain: let every issued stage land before the CTA can exit
+        for (uint32_t k = (it > (uint32_t)geo.nst ? it - geo.nst : 0); k < it; ++k) {
+          int dummy = 0;
+          mbar_wait_bounded(&full[k % geo.nst], (k / geo.nst) & 1, (volatile int*)&dummy, TC_WAIT_NS / 4);
+        }
+        atomicExch(&g_qgemv_error, 1);
+      }
+    }
+    return;
+  }
+
+  // ============================ consumers ============================
+  const int g = lane >> 2, t = lane & 3;
+  stage_x<BITS, NORM, XT>(p, xs, s_rms, kc0, kc1, tid, NC, 1);
+
+  // Work items of a stage: NACC weight sets x nch chunks; warp w takes items
+  // w and w + TC_NCW.  When the stage is full and holds exactly two items per
+  // warp (the planned shape), an item's chunk and set are fixed per warp, so
+  // its shared-memory offsets are computed once here; the rows g+8 sit at a
+  // constant stride from rows g (the swizzle phase repeats every 8 rows).
+  // Rows past N and blocks past K arrive zero-filled from TMA (scale = bias =
+  // 0 makes w_hat = 0), so the loop needs no bounds tests.
+  const int pr0 = tile_row(g);  // tile row of mma row g (mma row g+8 -> pr0 + 8)
+  const int lgG = p.lg_group;
+  const int w_r8 = geo.row_swz ? 1024 : 8 * geo.nblk * 128;
+  const int s_r8 = 16 * geo.ngs;
+  int xm[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) xm[mt] = min(mt * 8 + g, M - 1) * NMMA * 4;
+
+  auto woff = [&](int c) -> int {  // packed-word box offset of (chunk c, row pr0, unit t)
+    const int u = ((c & 1) << 2) | t;
+    if (geo.row_swz) return (c >> 1) * 2048 + pr0 * 128 + ((u ^ (pr0 & 7)) << 4);
+    const int l = pr0 * geo.nblk + (c >> 1);
+    return l * 128 + ((u ^ (l & 7)) << 4);
+  };
+  auto soff = [&](int c) -> int {  // scales box offset of (row pr0, group of chunk c / lane t)
+    const int gi = ((c * 16 + 4 * t) * TR::PF) >> lgG;
+    const int lo = pr0 * geo.ngs * 2 + gi * 2;
+    return lo ^ (((lo >> 7) & geo.s_swz) << 4);
+  };
+  const bool fast_shape = NACC * geo.cps == 2 * TC_NCW;
+  int fw[2], fs[2], fx[2];  // per fast-path item: word / scale / x offsets
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int c = DUAL ? warp : warp + j * TC_NCW;
+    const int aset = DUAL ? j : 0;
+    fw[j] = aset * geo.wset_bytes + woff(c);
+    fs[j] = NACC * geo.wset_bytes + (aset * 2) * geo.sset_bytes + soff(c);
+    fx[j] = (c * 4 + t) * rowlen;
+  }
+
+  struct Item {
+    uint4 w0, w1;
+    uint32_t sb0, sb1;
+    uint32_t bf[MT][NMMA][2];
+  };
+  auto load_item = [&](Item& d, const unsigned char* st, const __half* xst, int wo, int so, int xo) {
+    d.w0 = *reinterpret_cast<const uint4*>(st + wo);
+    d.w1 = *reinterpret_cast<const uint4*>(st + wo + w_r8);
+    d.sb0 = (uint32_t)*reinterpret_cast<const uint16_t*>(st + so) |
+            ((uint32_t)*reinterpret_cast<const uint16_t*>(st + so + geo.sset_bytes) << 16);
+    d.sb1 = (uint32_t)*reinterpret_cast<const uint16_t*>(st + so + s_r8) |
+            ((uint32_t)*reinterpret_cast<const uint16_t*>(st + so + s_r8 + geo.sset_bytes) << 16);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint4* src = reinterpret_cast<const uint4*>(xst + xo + xm[mt]);
+#pragma unroll
+      for (int q = 0; q < NMMA / 2; ++q) {
+        const uint4 v = src[q];
+        d.bf[mt][2 * q][0] = v.x;
+        d.bf[mt][2 * q][1] = v.y;
+        d.bf[mt][2 * q + 1][0] = v.z;
+        d.bf[mt][2 * q + 1][1] = v.w;
+      }
+    }
+  };
+  float acc[NACC][NA][MT][4];
+  auto compute_item = [&](const Item& d, int aset) {
+    const __half2 s0 = __half2half2(__ushort_as_half((uint16_t)(d.sb0 & 0xffffu)));
+    const __half2 b0 = __half2half2(__ushort_as_half((uint16_t)(d.sb0 >> 16)));
+    const __half2 s1 = __half2half2(__ushort_as_half((uint16_t)(d.sb1 & 0xffffu)));
+    const __half2 b1 = __half2half2(__ushort_as_half((uint16_t)(d.sb1 >> 16)));
+    const uint32_t w0[4] = {d.w0.x, d.w0.y, d.w0.z, d.w0.w};
+    const uint32_t w1[4] = {d.w1.x, d.w1.y, d.w1.z, d.w1.w};
+#pragma unroll
+    for (int aa = 0; aa < NACC; ++aa) {
+      if (NACC == 2 && aa != aset) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (BITS == 4) {
+          __half2 P0[4], P1[4];
+          unpack_u4(w0[j], P0);
+          unpack_u4(w1[j], P1);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            P0[q] = hfma2_rn(P0[q], s0, b0);
+            P1[q] = hfma2_rn(P1[q], s1, b1);
+          }
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int i = 2 * j + hh;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+              mma_16816(acc[aa][i % NA][mt], h2_as_u32(P0[2 * hh]), h2_as_u32(P1[2 * hh]),
+                        h2_as_u32(P0[2 * hh + 1]), h2_as_u32(P1[2 * hh + 1]), d.bf[mt][i][0], d.bf[mt][i][1]);
+          }
+        } else {
+          __half2 P0[2], P1[2];
+          unpack_u8(w0[j], P0);
+          unpack_u8(w1[j], P1);
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            P0[q] = hfma2_rn(P0[q], s0, b0);
+            P1[q] = hfma2_rn(P1[q], s1, b1);
+          }
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+            mma_16816(acc[aa][j % NA][mt], h2_as_u32(P0[0]), h2_as_u32(P1[0]), h2_as_u32(P0[1]),
+                      h2_as_u32(P1[1]), d.bf[mt][j][0], d.bf[mt][j][1]);
+        }
+      }
+    }
+  };
+
+  int s = 0;
+  uint32_t ph = 0;
+  int rbuf = 0;
+  bool aborted = false;
+  for (int tile = blockIdx.x; tile < p.tiles && !aborted; tile += gridDim.x) {
+    const int n0 = tile * 16;
+#pragma unroll
+    for (int a = 0; a < NACC; ++a)
+#pragma unroll
+      for (int q = 0; q < NA; ++q)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[a][q][mt][r] = 0.f;
+
+    for (int kcs = kc0; kcs < kc1; kcs += geo.cps) {
+      if (!mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS)) { aborted = true; break; }
+      const unsigned char* st = ring + (size_t)s * geo.stage_bytes;
+      const __half* xst = xs + (kcs - kc0) * 4 * rowlen;
+      const int nch = min(kc1 - kcs, geo.cps);
+      if (fast_shape && nch == geo.cps) {
+        if (MT == 1) {
+          // both items in flight before either is computed
+          Item da, db;
+          load_item(da, st, xst, fw[0], fs[0], fx[0]);
+          load_item(db, st, xst, fw[1], fs[1], fx[1]);
+          compute_item(da, 0);
+          compute_item(db, DUAL ? 1 : 0);
+        } else {
+          Item da;
+          load_item(da, st, xst, fw[0], fs[0], fx[0]);
+          compute_item(da, 0);
+          load_item(da, st, xst, fw[1], fs[1], fx[1]);
+          compute_item(da, DUAL ? 1 : 0);
+        }
+      } else {
+        for (int i = warp; i < NACC * nch; i += TC_NCW) {
+          const int aset = (NACC == 2 && i >= nch) ? 1 : 0;
+          const int c = i - aset * nch;
+          Item da;
+          load_item(da, st, xst, aset * geo.wset_bytes + woff(c),
+                    NACC * geo.wset_bytes + (aset * 2) * geo.sset_bytes + soff(c), (c * 4 + t) * rowlen);
+          compute_item(da, aset);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == geo.nst) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+    if (aborted) break;
+
+    // ---- cross-warp reduction and epilogue (consumer warps only) ----
+    // red is double-buffered by tile, so one barrier per tile suffices: the
+    // next-but-one tile's writes come after every thread passed the next
+    // tile's barrier, i.e. after these reads.
+    float* rb = red + rbuf * (TC_NCW * 32 * RPL);
+    rbuf ^= 1;
+#pragma unroll
+    for (int a = 0; a < NACC; ++a)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float v = 0.f;
+#pragma unroll
+          for (int q = 0; q < NA; ++q) v += acc[a][q][mt][r];
+          rb[(warp * 32 + lane) * RPL + (a * MT + mt) * 4 + r] = v;
+        }
+    named_bar_sync(1, NC);
+    for (int e = tid; e < 32 * MT * 4; e += NC) {
+      const int l = e & 31, rr = e >> 5;
+      const int mt = rr >> 2, r = rr & 3;
+      const int row = n0 + tile_row((l >> 2) + 8 * (r >> 1));
+      const int col = mt * 8 + 2 * (l & 3) + (r & 1);
+      if (row >= p.N || col >= M) continue;
+      float v[NACC];
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+        float sacc = 0.f;
+#pragma unroll
+        for (int w = 0; w < TC_NCW; ++w) sacc += rb[(w * 32 + l) * RPL + (a * MT + mt) * 4 + r];
+        v[a] = sacc;
+      }
+      epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, col, v);
+    }
+  }
+  if (aborted && lane == 0) atomicExch(&g_qgemv_error, 1);
+}
+
+template <int EPI, typename YT>
+__global__ void qgemv_splitk_reduce(const QGemvParams p) {
+  const size_t total = (size_t)p.M * p.N;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int col = (int)(e / p.N), row = (int)(e % p.N);
+    float v[2] = {0.f, 0.f};
+    const int nacc = (EPI == SC_EPI_SWIGLU) ? 2 : 1;
+    for (int a = 0; a < nacc; ++a)
+      for (int s = 0; s < p.splits; ++s) v[a] += p.partial[(((size_t)a * p.splits + s) * p.M + col) * p.N + row];
+    float out;
+    if (EPI == SC_EPI_SWIGLU) {
+      out = silu_f32(v[0]) * v[1];
+    } else {
+      out = v[0];
+      if (p.bias) out += __half2float(__ushort_as_half(p.bias[row]));
+      if (EPI == SC_EPI_RESIDUAL) out += p.residual[(size_t)col * p.ldr + row];
+    }
+    reinterpret_cast<YT*>(p.y)[(size_t)col * p.ldy + row] = from_f32<YT>(out);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+struct SplitPlan {
+  int splits;
+  int chunks_per_split;
+  int tiles;
+};
+
+static int kpc_of(int bits) { return bits == 4 ? 128 : 64; }
+static int nmma_of(int bits) { return bits == 4 ? 8 : 4; }
+
+static size_t xs_bytes(int bits, int M, int nkc) {
+  const size_t rowlen = (size_t)M * nmma_of(bits) * 4 + 8;
+  return (size_t)nkc * 4 * rowlen * 2;
+}
+
+static size_t smem_bytes(int bits, int M, int nkc, int nacc, int MT) {
+  return xs_bytes(bits, M, nkc) + (size_t)QG_WARPS * 32 * nacc * MT * 4 * 4;
+}
+
+// Direct-load kernel plan (fallback path).
+static SplitPlan plan_splits(int M, int K, int N, int bits, int nacc) {
+  SplitPlan sp;
+  const int KC = (K / (32 / bits) + 15) / 16;
+  sp.tiles = (N + 15) / 16;
+  const int MT = M > 8 ? 2 : 1;
+  int splits = 1;
+  while (splits < KC && smem_bytes(bits, M, (KC + splits - 1) / splits, nacc, MT) > (size_t)QG_XS_MAX) ++splits;
+  const int want = 2 * sm_count();
+  while (sp.tiles * splits < want && (KC + splits) / (splits + 1) >= QG_WARPS) ++splits;
+  sp.chunks_per_split = (KC + splits - 1) / splits;
+  sp.splits = (KC + sp.chunks_per_split - 1) / sp.chunks_per_split;
+  return sp;
+}
+
+// ---- TMA pipeline plan
+constexpr size_t TC_SMEM_BUDGET = 220 * 1024;
+constexpr size_t TC_XS_BUDGET = 64 * 1024;
+constexpr int TC_STAGE_CHUNKS = 32;  // 16 rows x 32 chunks x 64 B = 32 KB of packed words per stage
+
+struct TmaPlan {
+  bool ok;
+  SplitPlan sp;
+  TmaGeo geo;
+  size_t smem;
+  int grid_x;
+};
+
+static int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+// Chunk granularity of stages and splits: whole 32-word blocks, and a scale
+// box whose width (groups) is a multiple of 8 (16 bytes).
+static int tma_unit(int bits, int group) { return std::max(2, 8 * group / kpc_of(bits)); }
+
+// Tuning knobs read once from the environment (0 / unset = built-in choice):
+// SC_QGEMV_CPS chunks per stage, SC_QGEMV_NST ring depth, SC_QGEMV_PATH=ldg
+// forces the direct-load kernel.
+struct Knobs {
+  int cps = 0, nst = 0, ldg = 0;
+  Knobs() {
+    if (const char* e = getenv("SC_QGEMV_CPS")) cps = atoi(e);
+    if (const char* e = getenv("SC_QGEMV_NST")) nst = atoi(e);
+    if (const char* e = getenv("SC_QGEMV_PATH")) ldg = strcmp(e, "ldg") == 0;
+  }
+};
+static const Knobs& knobs() {
+  static Knobs k;
+  return k;
+}
+
+static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int MT) {
+  TmaPlan tp{};
+  tp.ok = false;
+  const int KW = K / (32 / bits);
+  const int KC = (KW + 15) / 16;
+  const int KG = K / group;
+  if (KW % 32 || KG % 8) return tp;  // boxes must tile a row exactly; 16-byte scale rows
+  const int U = tma_unit(bits, group);
+  const int nsm = sm_count();
+  SplitPlan sp;
+  sp.tiles = (N + 15) / 16;
+  int splits = 1;
+  auto cps_of = [&](int s) { return round_up((KC + s - 1) / s, U); };
+  while (cps_of(splits) > U && xs_bytes(bits, M, cps_of(splits)) > TC_XS_BUDGET) ++splits;
+  // more splits when there are too few tiles for the SMs (keep >= TC_NCW chunks per split)
+  while (sp.tiles * splits < nsm && cps_of(splits + 1) >= TC_NCW) ++splits;
+  sp.chunks_per_split = cps_of(splits);
+  sp.splits = (KC + sp.chunks_per_split - 1) / sp.chunks_per_split;
+  TmaGeo geo{};
+  int cps = knobs().cps > 0 ? knobs().cps : TC_STAGE_CHUNKS / nacc;
+  while (cps > U && cps * kpc_of(bits) / group * 2 > 128) cps /= 2;  // scale-box row <= 128 B (swizzle span)
+  cps = std::min(cps, sp.chunks_per_split);
+  cps = std::max(U, cps / U * U);
+  geo.cps = cps;
+  geo.nblk = cps / 2;
+  geo.ngs = cps * kpc_of(bits) / group;
+  {
+    const int rowb = geo.ngs * 2;
+    geo.s_swz = rowb == 128 ? 7 : rowb == 64 ? 3 : rowb == 32 ? 1 : 0;
+  }
+  geo.wset_bytes = 16 * geo.nblk * 128;
+  geo.sset_bytes = round_up(16 * geo.ngs * 2, 1024);
+  geo.stage_bytes = nacc * (geo.wset_bytes + 2 * geo.sset_bytes);
+  geo.ring_off = round_up((int)xs_bytes(bits, M, sp.chunks_per_split), 1024);
+  const int red_bytes = 2 * TC_NCW * 32 * nacc * MT * 4 * 4;  // double-buffered by tile
+  const size_t fixed = geo.ring_off + red_bytes + 2 * TC_MAX_NST * 8 + 1024 /* base alignment */ + 64;
+  if (fixed >= TC_SMEM_BUDGET) return tp;
+  int nst = (int)std::min<size_t>(TC_MAX_NST, (TC_SMEM_BUDGET - fixed) / geo.stage_bytes);
+  if (knobs().nst > 0) nst = std::min(nst, knobs().nst);
+  if (nst < 2) return tp;
+  geo.nst = nst;
+  geo.red_off = geo.ring_off + nst * geo.stage_bytes;
+  geo.bar_off = round_up(geo.red_off + red_bytes, 16);
+  geo.atomic_out = 0;
+  geo.row_swz = 1;
+  tp.smem = geo.bar_off + 2 * TC_MAX_NST * 8 + 1024;
+  tp.sp = sp;
+  tp.geo = geo;
+  tp.grid_x = std::max(1, std::min(sp.tiles, (nsm + sp.splits - 1) / sp.splits));
+  tp.ok = true;
+  return tp;
+}
+
+// ---- tensor maps (driver entry point fetched through the runtime)
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// mode: 1 = (word, row, block) dims with row-dependent swizzle, 0 = (word, block, row)
+static bool encode_wmap(CUtensorMap* m, const uint32_t* wq, int rows, int KW, int nblk, int mode) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3], es[3] = {1, 1, 1};
+  if (mode) {
+    dims[0] = 32; dims[1] = (cuuint64_t)rows; dims[2] = (cuuint64_t)(KW / 32);
+    strides[0] = (cuuint64_t)KW * 4; strides[1] = 128;
+    box[0] = 32; box[1] = 16; box[2] = (cuuint32_t)nblk;
+  } else {
+    dims[0] = 32; dims[1] = (cuuint64_t)(KW / 32); dims[2] = (cuuint64_t)rows;
+    strides[0] = 128; strides[1] = (cuuint64_t)KW * 4;
+    box[0] = 32; box[1] = (cuuint32_t)nblk; box[2] = 16;
+  }
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint32_t*>(wq), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool encode_smap(CUtensorMap* m, const uint16_t* s, int rows, int KG, int ngs, int swz_mask) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)KG, (cuuint64_t)rows}, strides[1] = {(cuuint64_t)KG * 2};
+  cuuint32_t box[2] = {(cuuint32_t)ngs, 16}, es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(s), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swz_mask == 7   ? CU_TENSOR_MAP_SWIZZLE_128B
+            : swz_mask == 3 ? CU_TENSOR_MAP_SWIZZLE_64B
+            : swz_mask == 1 ? CU_TENSOR_MAP_SWIZZLE_32B
+                            : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Encode every segment's maps; prefers the row-swizzled layout, falls back to
+// the block-major one if the driver rejects non-monotonic strides.
+static bool encode_maps(const QGemvParams& p, int bits, int nacc, TmaGeo* geo, TmaMaps* maps) {
+  static int mode_ok = -1;  // -1 unknown, 1 row-swizzled works, 0 use block-major
+  const int KW = p.K / (32 / bits), KG = p.K / p.group;
+  const int nmaps = nacc == 2 ? 2 : p.nseg;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int mode = (mode_ok == 0 || pass == 1) ? 0 : 1;
+    bool ok = true;
+    for (int s = 0; s < nmaps && ok; ++s) {
+      const QSeg& sg = p.seg[s];
+      ok = encode_wmap(&maps->w[s], sg.wq, sg.rows, KW, geo->nblk, mode) &&
+           encode_smap(&maps->s[s], sg.s, sg.rows, KG, geo->ngs, geo->s_swz) &&
+           encode_smap(&maps->b[s], sg.b, sg.rows, KG, geo->ngs, geo->s_swz);
+    }
+    if (ok) {
+      if (mode_ok < 0) mode_ok = mode;
+      geo->row_swz = mode;
+      return true;
+    }
+    if (mode == 0) return false;
+    mode_ok = 0;
+  }
+  return false;
+}
+
+template <int BITS, int MT, int EPI, bool NORM, typename XT, typename YT>
+static int launch_qgemv(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, cudaStream_t stream) {
+  const int nacc = (EPI == SC_EPI_SWIGLU) ? 2 : 1;
+  if (tp) {
+    auto kern = qgemv_tma_kernel<BITS, MT, EPI, NORM, XT, YT>;
+    static bool configured = false;
+    if (!configured) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM_BUDGET);
+      configured = true;
+    }
+    dim3 grid(tp->grid_x, p.splits);
+    kern<<<grid, TC_THREADS, tp->smem, stream>>>(p, tp->geo, *maps);
+    int st = check_launch("qgemv_tma");
+    if (st != SC_OK || p.splits == 1 || tp->geo.atomic_out) return st;
+  } else {
+    auto kern = qgemv_kernel<BITS, MT, EPI, NORM, XT, YT>;
+    const size_t smem = smem_bytes(BITS, p.M, p.chunks_per_split, nacc, MT);
+    static bool configured = false;
+    if (!configured) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      configured = true;
+    }
+    int nb = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, QG_THREADS, smem);
+    const int slots = std::max(1, std::max(nb, 1) * sm_count() / p.splits);
+    const int per_cta = (p.tiles + slots - 1) / slots;
+    dim3 grid((p.tiles + per_cta - 1) / per_cta, p.splits);
+    kern<<<grid, QG_THREADS, smem, stream>>>(p);
+    int st = check_launch("qgemv");
+    if (st != SC_OK || p.splits == 1) return st;
+  }
+  const size_t total = (size_t)p.M * p.N;
+  const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)4 * sm_count());
+  qgemv_splitk_reduce<EPI, YT><<<rb, 256, 0, stream>>>(p);
+  return check_launch("qgemv_splitk_reduce");
+}
+
+template <int BITS, int MT, int EPI, bool NORM>
+static int dispatch_types(QGemvParams& p, const TmaPlan* tp, const TmaMaps* mp, int x_dtype, int y_dtype,
+                          cudaStream_t stream) {
+  if (x_dtype == SC_F16 && y_dtype == SC_F16) return launch_qgemv<BITS, MT, EPI, NORM, __half, __half>(p, tp, mp, stream);
+  if (x_dtype == SC_F16 && y_dtype == SC_F32) return launch_qgemv<BITS, MT, EPI, NORM, __half, float>(p, tp, mp, stream);
+  if (x_dtype == SC_F32 && y_dtype == SC_F16) return launch_qgemv<BITS, MT, EPI, NORM, float, __half>(p, tp, mp, stream);
+  if (x_dtype == SC_F32 && y_dtype == SC_F32) return launch_qgemv<BITS, MT, EPI, NORM, float, float>(p, tp, mp, stream);
+  set_error("qlinear: unsupported dtype pair x=%d y=%d", x_dtype, y_dtype);
+  return SC_ERR_ARG;
+}
+
+template <int BITS, int MT, int EPI>
+static int dispatch_norm(QGemvParams& p, const TmaPlan* tp, const TmaMaps* mp, int x_dtype, int y_dtype,
+                         cudaStream_t stream) {
+  if (p.norm_w) return dispatch_types<BITS, MT, EPI, true>(p, tp, mp, x_dtype, y_dtype, stream);
+  return dispatch_types<BITS, MT, EPI, false>(p, tp, mp, x_dtype, y_dtype, stream);
+}
+
+template <int BITS, int MT>
+static int dispatch_epi(QGemvParams& p, const TmaPlan* tp, const TmaMaps* mp, int epi, int x_dtype, int y_dtype,
+                        cudaStream_t stream) {
+  switch (epi) {
+    case SC_EPI_STORE: return dispatch_norm<BITS, MT, SC_EPI_STORE>(p, tp, mp, x_dtype, y_dtype, stream);
+    case SC_EPI_RESIDUAL: return dispatch_norm<BITS, MT, SC_EPI_RESIDUAL>(p, tp, mp, x_dtype, y_dtype, stream);
+    case SC_EPI_SWIGLU: return dispatch_norm<BITS, MT, SC_EPI_SWIGLU>(p, tp, mp, x_dtype, y_dtype, stream);
+  }
+  set_error("qlinear: unknown epilogue %d", epi);
+  return SC_ERR_ARG;
+}
+
+// Which kernel a pass uses, and its split plan.  Shared by the launcher and
+// the workspace-size query so both always agree.
+struct PassPlan {
+  bool tma;
+  TmaPlan tp;
+  SplitPlan sp;
+};
+
+static bool aligned(const void* ptr, size_t a) { return ((uintptr_t)ptr % a) == 0; }
+
+static PassPlan plan_pass(int mb, int K, int N, int bits, int group, int nacc, bool tma_ok, bool atomic_ok) {
+  PassPlan pp{};
+  const int MT = mb > 8 ? 2 : 1;
+  if (tma_ok && !knobs().ldg) {
+    pp.tp = plan_tma(mb, K, N, bits, group, nacc, MT);
+    if (pp.tp.ok) {
+      pp.tma = true;
+      pp.sp = pp.tp.sp;
+      if (atomic_ok && pp.sp.splits > 1) pp.tp.geo.atomic_out = 1;
+      return pp;
+    }
+  }
+  pp.tma = false;
+  pp.sp = plan_splits(mb, K, N, bits, nacc);
+  return pp;
+}
+
+static size_t pass_workspace(const PassPlan& pp, int mb, int N, int nacc) {
+  if (pp.sp.splits <= 1 || (pp.tma && pp.tp.geo.atomic_out)) return 0;
+  return (size_t)nacc * pp.sp.splits * mb * N * sizeof(float);
+}
+
+static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_w, float eps,
+                       int nseg, const uint32_t* const* wq, const uint16_t* const* scales,
+                       const uint16_t* const* biases, const int* seg_rows, int group, int bits,
+                       const uint16_t* bias, int epi, void* y, int y_dtype, int ldy, const float* residual,
+                       int ldr, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  SC_REQUIRE(x && y && wq && scales && biases && seg_rows, SC_ERR_ARG, "qlinear: null pointer argument");
+  SC_REQUIRE(bits == 4 || bits == 8, SC_ERR_SHAPE, "qlinear: bits must be 4 or 8 (got %d)", bits);
+  SC_REQUIRE(group == 32 || group == 64 || group == 128, SC_ERR_SHAPE,
+             "qlinear: group_size must be 32, 64 or 128 (got %d)", group);
+  SC_REQUIRE(M >= 1 && K >= 1, SC_ERR_SHAPE, "qlinear: M=%d K=%d must be positive", M, K);
+  SC_REQUIRE(K % group == 0, SC_ERR_SHAPE, "qlinear: K=%d not a multiple of group_size=%d", K, group);
+  SC_REQUIRE(ldx >= K && ldy >= 1, SC_ERR_SHAPE, "qlinear: bad leading dimensions");
+  SC_REQUIRE(nseg >= 1 && nseg <= QG_MAX_SEG, SC_ERR_SHAPE, "qlinear: 1..3 weight segments (got %d)", nseg);
+  SC_REQUIRE(epi != SC_EPI_RESIDUAL || residual, SC_ERR_ARG, "qlinear: residual epilogue needs residual");
+  SC_REQUIRE(epi != SC_EPI_SWIGLU || (nseg == 2 && seg_rows[0] == seg_rows[1]), SC_ERR_SHAPE,
+             "qlinear: SwiGLU needs two segments of equal rows");
+  SC_REQUIRE(x_dtype == SC_F16 || x_dtype == SC_F32, SC_ERR_ARG, "qlinear: x dtype");
+  SC_REQUIRE(y_dtype == SC_F16 || y_dtype == SC_F32, SC_ERR_ARG, "qlinear: y dtype");
+  SC_REQUIRE(epi != SC_EPI_SWIGLU || !bias, SC_ERR_UNSUPPORTED, "qlinear: bias with SwiGLU epilogue");
+
+  QGemvParams p{};
+  p.K = K;
+  p.ldx = ldx;
+  p.norm_w = norm_w;
+  p.eps = eps;
+  p.nseg = nseg;
+  int N = 0;
+  bool tma_ok = true;
+  for (int s = 0; s < nseg; ++s) {
+    SC_REQUIRE(wq[s] && scales[s] && biases[s], SC_ERR_ARG, "qlinear: null weight segment %d", s);
+    SC_REQUIRE(seg_rows[s] >= 0, SC_ERR_SHAPE, "qlinear: negative rows");
+    p.seg[s] = QSeg{wq[s], scales[s], biases[s], seg_rows[s]};
+    N += seg_rows[s];
+    // tensor maps need 16-byte bases; a 16-row tile must not straddle two segments
+    tma_ok = tma_ok && aligned(wq[s], 16) && aligned(scales[s], 16) && aligned(biases[s], 16) &&
+             seg_rows[s] > 0 && (s + 1 == nseg || seg_rows[s] % 16 == 0 || epi == SC_EPI_SWIGLU);
+  }
+  if (epi == SC_EPI_SWIGLU) N = seg_rows[0];
+  SC_REQUIRE(ldy >= N, SC_ERR_SHAPE, "qlinear: ldy=%d < N=%d", ldy, N);
+  SC_REQUIRE(epi != SC_EPI_RESIDUAL || ldr >= N, SC_ERR_SHAPE, "qlinear: ldr=%d < N=%d", ldr, N);
+  if (N == 0) return SC_OK;
+  p.N = N;
+  p.group = group;
+  p.lg_group = group == 32 ? 5 : group == 64 ? 6 : 7;
+  p.bias = bias;
+  p.ldy = ldy;
+  p.ldr = ldr;
+  const int nacc = epi == SC_EPI_SWIGLU ? 2 : 1;
+  const size_t xsz = x_dtype == SC_F16 ? 2 : 4;
+  const size_t ysz = y_dtype == SC_F16 ? 2 : 4;
+  const bool atomic_ok = epi == SC_EPI_RESIDUAL && y_dtype == SC_F32 && (const void*)residual == (const void*)y &&
+                         ldr == ldy;
+
+  for (int m0 = 0; m0 < M; m0 += 16) {
+    const int mb = std::min(16, M - m0);
+    PassPlan pp = plan_pass(mb, K, N, bits, group, nacc, tma_ok, atomic_ok);
+    p.M = mb;
+    p.x = static_cast<const char*>(x) + (size_t)m0 * ldx * xsz;
+    p.y = static_cast<char*>(y) + (size_t)m0 * ldy * ysz;
+    p.residual = residual ? residual + (size_t)m0 * ldr : nullptr;
+    TmaMaps maps;
+    const TmaPlan* tp = nullptr;
+    if (pp.tma && encode_maps(p, bits, nacc, &pp.tp.geo, &maps)) {
+      tp = &pp.tp;
+    } else if (pp.tma) {
+      // tensor maps unavailable: plan this pass for the direct-load kernel
+      pp = plan_pass(mb, K, N, bits, group, nacc, false, false);
+    }
+    p.splits = pp.sp.splits;
+    p.chunks_per_split = pp.sp.chunks_per_split;
+    p.tiles = pp.sp.tiles;
+    const size_t need = pass_workspace(pp, mb, N, nacc);
+    if (need) {
+      SC_REQUIRE(ws && ws_bytes >= need, SC_ERR_WORKSPACE, "qlinear: workspace of %zu bytes needed (got %zu)", need,
+                 ws_bytes);
+      p.partial = static_cast<float*>(ws);
+    } else {
+      p.partial = nullptr;
+    }
+    int st;
+    if (bits == 4)
+      st = mb > 8 ? dispatch_epi<4, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
+                  : dispatch_epi<4, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
+    else
+      st = mb > 8 ? dispatch_epi<8, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
+                  : dispatch_epi<8, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
+    if (st != SC_OK) return st;
+  }
+  return SC_OK;
+}
+
+}  // namespace sc
+
+extern "C" {
+
+size_t sc_qlinear_workspace_bytes(int M, int K, int N, int bits) {
+  if (M < 1 || K < 1 || N < 1 || (bits != 4 && bits != 8)) return 0;
+  const int mb = M < 16 ? M : 16;
+  size_t best = 0;
+  // the widest plan over every pass size, kernel choice and group size
+  for (int mm = 1; mm <= mb; ++mm)
+    for (int group : {32, 64, 128})
+      for (int tma = 0; tma < 2; ++tma) {
+        if (K % group) continue;
+        sc::PassPlan pp = sc::plan_pass(mm, K, N, bits, group, 2, tma != 0, false);
+        best = std::max(best, sc::pass_workspace(pp, mm, N, 2));
+      }
+  return best;
+}
+
+int sc_qgemv_device_error(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, sc::g_qgemv_error, sizeof(int));
+  if (reset) {
+    const int z = 0;
+    cudaMemcpyToSymbol(sc::g_qgemv_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const uint32_t* wq, const uint16_t* scales,
+               const uint16_t* biases, int N, int group_size, int bits, const uint16_t* bias, void* y,
+               int y_dtype, int ldy, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const uint32_t* w[1] = {wq};
+  const uint16_t* s[1] = {scales};
+  const uint16_t* b[1] = {biases};
+  int rows[1] = {N};
+  return sc::run_qlinear(x, x_dtype, M, K, ldx, nullptr, 0.f, 1, w, s, b, rows, group_size, bits, bias,
+                         SC_EPI_STORE, y, y_dtype, ldy, nullptr, 0, workspace, workspace_bytes, stream);
+}
+
+int sc_qlinear_fused(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_weight,
+                     float norm_eps, int nseg, const uint32_t* const* wq, const uint16_t* const* scales,
+                     const uint16_t* const* biases, const int* seg_rows, int group_size, int bits,
+                     const uint16_t* bias, int epilogue, void* y, int y_dtype, int ldy, const float* residual,
+                     int ldr, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return sc::run_qlinear(x, x_dtype, M, K, ldx, norm_weight, norm_eps, nseg, wq, scales, biases, seg_rows,
+                         group_size, bits, bias, epilogue, y, y_dtype, ldy, residual, ldr, workspace,
+                         workspace_bytes, stream);
+}
+
+}  // extern "C"
