@@ -1,0 +1,432 @@
+"""Communicator: the reference's collective API on NCCL over NVLink.
+
+Drop-in for ``collectives/communicator.py`` of the reference (``Communicator``
+:52-603, ``ProcessGroup`` :606-648): same method names, arguments and
+semantics (all_reduce sum/mean/max/min, rank-ordered all_gather along any
+dim, start/wait_all_reduce, all_reduce_batch, reduce_scatter, broadcast,
+barrier, send/recv, stats).  The asyncio-TCP ring / WebSocket-relay
+transports of the reference (``collectives/all_reduce.py:58-193``,
+``all_gather.py:54-162``, ``point_to_point.py``, ``ws_relay.py``) are replaced
+by one NCCL communicator per process, created through ``libsc_b200.so``.
+
+Rendezvous: rank 0 creates the NCCL unique id and publishes it in a
+``torch.distributed`` store (a ``TCPStore`` at ``peer_infos[0]`` / the
+constructor's host and port, or the default store of an initialised process
+group).  Collectives are enqueued on the caller's current CUDA stream, so
+they order with the kernels around them and can be captured in CUDA graphs.
+``send``/``recv`` are control-plane transfers (small host tensors through the
+store), as the reference uses them only to move request metadata.
+
+``backend="gloo"`` runs the same host logic with ``torch.distributed`` on CPU
+tensors; it exists so the multi-rank host paths are testable without GPUs.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import datetime
+import logging
+import pickle
+import time
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional
+
+import torch
+
+logger = logging.getLogger(__name__)
+
+_OPS = {"sum": 0, "max": 1, "min": 2, "mean": 3}
+
+
+@dataclass
+class CommunicatorStats:
+    total_all_reduce_calls: int = 0
+    total_all_gather_calls: int = 0
+    total_all_reduce_time_ms: float = 0.0
+    total_all_gather_time_ms: float = 0.0
+    total_bytes_sent: int = 0
+    total_bytes_received: int = 0
+
+    def to_dict(self) -> Dict[str, Any]:
+        return {
+            "total_all_reduce_calls": self.total_all_reduce_calls,
+            "total_all_gather_calls": self.total_all_gather_calls,
+            "total_all_reduce_time_ms": self.total_all_reduce_time_ms,
+            "total_all_gather_time_ms": self.total_all_gather_time_ms,
+            "total_bytes_sent": self.total_bytes_sent,
+            "total_bytes_received": self.total_bytes_received,
+            "avg_all_reduce_time_ms": (self.total_all_reduce_time_ms / self.total_all_reduce_calls
+                                       if self.total_all_reduce_calls else 0),
+            "avg_all_gather_time_ms": (self.total_all_gather_time_ms / self.total_all_gather_calls
+                                       if self.total_all_gather_calls else 0),
+        }
+
+
+class Communicator:
+    """Collectives for tensor parallelism (one process per GPU)."""
+
+    def __init__(self, rank: int, world_size: int, host: str = "127.0.0.1", port: int = 9000,
+                 topology_type: str = "ring", backend: str = "nccl"):
+        if backend not in ("nccl", "gloo"):
+            raise ValueError(f"backend must be 'nccl' or 'gloo', got {backend}")
+        self.rank = rank
+        self.world_size = world_size
+        self.host = host
+        self.port = port
+        self.topology_type = topology_type  # accepted for compatibility; NCCL picks its own algorithm
+        self.backend = backend
+        self.stats = CommunicatorStats()
+        self._initialized = False
+        self._comm = None  # opaque sc_comm handle (nccl backend)
+        self._store = None
+        self._pg = None  # torch.distributed group (gloo backend)
+        self._pending: Dict[str, Any] = {}
+        self._ar_counter = 0
+        self._barrier_counter = 0
+        self._bcast_counter = 0
+        self._p2p_counter: Dict[tuple, int] = {}
+        self._comm_stream: Optional[torch.cuda.Stream] = None
+
+    # ------------------------------------------------------------ setup
+
+    @property
+    def is_initialized(self) -> bool:
+        return self._initialized
+
+    async def initialize(self, peer_infos: Optional[List[Any]] = None, timeout: float = 30.0, store=None):
+        """Rendezvous and create the communicator.
+
+        ``peer_infos`` (reference ``PeerInfo`` list) only supplies rank 0's
+        host/port for the store; ``store`` may be given directly instead.
+        """
+        self.initialize_sync(peer_infos=peer_infos, timeout=timeout, store=store)
+
+    def initialize_sync(self, peer_infos=None, timeout: float = 30.0, store=None):
+        if self._initialized:
+            logger.warning("Communicator already initialized")
+            return
+        import torch.distributed as dist
+
+        if store is None and dist.is_available() and dist.is_initialized():
+            store = dist.distributed_c10d._get_default_store()
+        if store is None:
+            host, port = self.host, self.port
+            if peer_infos:
+                p0 = peer_infos[0]
+                host = getattr(p0, "host", host)
+                port = getattr(p0, "port", port)
+            store = dist.TCPStore(host, port, self.world_size, self.rank == 0,
+                                  timeout=datetime.timedelta(seconds=timeout))
+        self._store = store
+        if self.backend == "gloo":
+            if not dist.is_initialized():
+                dist.init_process_group("gloo", store=store, rank=self.rank, world_size=self.world_size,
+                                        timeout=datetime.timedelta(seconds=timeout))
+            self._pg = dist.group.WORLD
+        else:
+            from .. import _lib as L
+
+            lib = L.load()
+            uid = (C.c_char * 128)()
+            key = "shardcompute_b200/nccl_uid"
+            if self.rank == 0:
+                L.check(lib.sc_comm_unique_id(uid, 128), "sc_comm_unique_id")
+                store.set(key, bytes(uid))
+            else:
+                store.wait([key], datetime.timedelta(seconds=timeout))
+                C.memmove(uid, store.get(key), 128)
+            handle = C.c_void_p()
+            L.check(lib.sc_comm_init(uid, 128, self.world_size, self.rank, C.byref(handle)), "sc_comm_init")
+            self._comm = handle
+            self._comm_stream = torch.cuda.Stream()
+        self._initialized = True
+
+    def _require(self):
+        if not self._initialized:
+            raise RuntimeError("Communicator not initialized")
+
+    def _device(self) -> torch.device:
+        return torch.device("cpu") if self.backend == "gloo" else torch.device("cuda", torch.cuda.current_device())
+
+    # ------------------------------------------------------------ raw NCCL (engine path)
+
+    def _dt(self, t: torch.Tensor) -> int:
+        from .. import _lib as L
+
+        return {torch.float16: L.SC_F16, torch.float32: L.SC_F32, torch.int32: L.SC_I32}[t.dtype]
+
+    def allreduce_into(self, send: torch.Tensor, recv: torch.Tensor, op: str = "sum") -> None:
+        """Enqueue an all-reduce of ``send`` into ``recv`` on the current stream (graph-capturable)."""
+        self._require()
+        if op not in _OPS:
+            raise ValueError(f"Unknown reduction op: {op}")
+        if self.world_size == 1:
+            if recv.data_ptr() != send.data_ptr():
+                recv.copy_(send)
+            return
+        if self.backend == "gloo":
+            import torch.distributed as dist
+
+            buf = send.clone()
+            dist.all_reduce(buf, op=_gloo_op(op), group=self._pg)
+            if op == "mean":
+                buf /= self.world_size
+            recv.copy_(buf)
+            return
+        from .. import _lib as L
+
+        L.call("sc_allreduce", send.data_ptr(), recv.data_ptr(), send.numel(), self._dt(send), _OPS[op],
+               self._comm, torch.cuda.current_stream(send.device).cuda_stream)
+
+    def allgather_into(self, send: torch.Tensor, recv: torch.Tensor) -> None:
+        """Enqueue an all-gather: ``recv`` is ``[world, *send.shape]`` contiguous."""
+        self._require()
+        if self.world_size == 1:
+            recv.view_as(send).copy_(send)
+            return
+        if self.backend == "gloo":
+            import torch.distributed as dist
+
+            parts = [torch.empty_like(send) for _ in range(self.world_size)]
+            dist.all_gather(parts, send.contiguous(), group=self._pg)
+            recv.copy_(torch.stack(parts))
+            return
+        from .. import _lib as L
+
+        L.call("sc_allgather", send.data_ptr(), recv.data_ptr(), send.numel(), self._dt(send), self._comm,
+               torch.cuda.current_stream(send.device).cuda_stream)
+
+    # ------------------------------------------------------------ reference API
+
+    def _reduce_tensor(self, tensor: torch.Tensor, op: str) -> torch.Tensor:
+        if op not in _OPS:
+            raise ValueError(f"Unknown reduction op: {op}")
+        src = tensor.contiguous()
+        out = torch.empty_like(src)
+        self.allreduce_into(src, out, op)
+        return out
+
+    async def all_reduce(self, tensor: torch.Tensor, op: str = "sum") -> torch.Tensor:
+        self._require()
+        t0 = time.perf_counter()
+        out = self._reduce_tensor(tensor, op)
+        self.stats.total_all_reduce_calls += 1
+        self.stats.total_all_reduce_time_ms += (time.perf_counter() - t0) * 1000
+        nb = tensor.numel() * tensor.element_size() * (self.world_size - 1) * 2 // max(self.world_size, 1)
+        self.stats.total_bytes_sent += nb
+        self.stats.total_bytes_received += nb
+        return out
+
+    def start_all_reduce(self, tensor: torch.Tensor, op: str = "sum") -> str:
+        """Non-blocking all-reduce on the comm stream; the id is redeemed by wait_all_reduce."""
+        self._require()
+        self._ar_counter += 1
+        op_id = f"ar_{self.rank}_{self._ar_counter}"
+        if self.backend == "gloo" or self.world_size == 1:
+            self._pending[op_id] = (self._reduce_tensor(tensor, op), None, time.perf_counter())
+            return op_id
+        cur = torch.cuda.current_stream(tensor.device)
+        src = tensor.contiguous()
+        out = torch.empty_like(src)
+        self._comm_stream.wait_stream(cur)
+        with torch.cuda.stream(self._comm_stream):
+            self.allreduce_into(src, out, op)
+            ev = torch.cuda.Event()
+            ev.record(self._comm_stream)
+        src.record_stream(self._comm_stream)
+        out.record_stream(self._comm_stream)
+        self._pending[op_id] = (out, ev, time.perf_counter())
+        return op_id
+
+    async def wait_all_reduce(self, op_id: str) -> torch.Tensor:
+        if op_id not in self._pending:
+            raise ValueError(f"Unknown all-reduce operation ID: {op_id}")
+        out, ev, t0 = self._pending.pop(op_id)
+        if ev is not None:
+            torch.cuda.current_stream(out.device).wait_event(ev)
+        self.stats.total_all_reduce_calls += 1
+        self.stats.total_all_reduce_time_ms += (time.perf_counter() - t0) * 1000
+        return out
+
+    async def all_reduce_batch(self, tensors: List[torch.Tensor], op: str = "sum") -> List[torch.Tensor]:
+        """One all-reduce over the concatenation of ``tensors`` (counted as one call)."""
+        self._require()
+        if not tensors:
+            return []
+        if len(tensors) == 1:
+            return [await self.all_reduce(tensors[0], op)]
+        dtype = tensors[0].dtype
+        if any(t.dtype != dtype for t in tensors):
+            raise ValueError("All tensors must have same dtype for batched all-reduce")
+        red = await self.all_reduce(torch.cat([t.reshape(-1) for t in tensors]), op)
+        outs, off = [], 0
+        for t in tensors:
+            outs.append(red[off:off + t.numel()].view(t.shape))
+            off += t.numel()
+        return outs
+
+    async def all_gather(self, tensor: torch.Tensor, dim: int = -1) -> torch.Tensor:
+        """Rank-ordered concatenation along ``dim`` (reference all_gather.py:90-162)."""
+        self._require()
+        if self.world_size == 1:
+            return tensor
+        t0 = time.perf_counter()
+        src = tensor.contiguous()
+        buf = torch.empty((self.world_size, *src.shape), dtype=src.dtype, device=src.device)
+        self.allgather_into(src, buf)
+        d = dim if dim >= 0 else src.dim() + dim
+        out = torch.cat(list(buf.unbind(0)), dim=d)
+        self.stats.total_all_gather_calls += 1
+        self.stats.total_all_gather_time_ms += (time.perf_counter() - t0) * 1000
+        nb = src.numel() * src.element_size() * (self.world_size - 1)
+        self.stats.total_bytes_sent += nb
+        self.stats.total_bytes_received += nb
+        return out
+
+    async def reduce_scatter(self, tensor: torch.Tensor, op: str = "sum", dim: int = -1) -> torch.Tensor:
+        """Reduce across ranks; return this rank's 1/N slice along ``dim``."""
+        self._require()
+        red = self._reduce_tensor(tensor, op)
+        d = dim if dim >= 0 else red.dim() + dim
+        return red.chunk(self.world_size, dim=d)[self.rank].contiguous()
+
+    async def broadcast(self, tensor: Optional[torch.Tensor], root: int = 0) -> torch.Tensor:
+        """Root's tensor on every rank; non-roots may pass None (shape/dtype travel via the store)."""
+        self._require()
+        self._bcast_counter += 1
+        key = f"shardcompute_b200/bcast/{self._bcast_counter}"
+        if self.rank == root:
+            if tensor is None:
+                raise ValueError("Root must provide tensor for broadcast")
+            if self.world_size > 1:
+                self._store.set(key, pickle.dumps((tuple(tensor.shape), str(tensor.dtype))))
+            src = tensor.contiguous()
+        else:
+            self._store.wait([key], datetime.timedelta(seconds=60))
+            shape, dt = pickle.loads(self._store.get(key))
+            src = torch.empty(shape, dtype=getattr(torch, dt.split(".")[-1]), device=self._device())
+        if self.world_size == 1:
+            return src
+        if self.backend == "gloo":
+            import torch.distributed as dist
+
+            dist.broadcast(src, src=root, group=self._pg)
+            return src
+        from .. import _lib as L
+
+        L.call("sc_broadcast", src.data_ptr(), src.data_ptr(), src.numel(), self._dt(src), root, self._comm,
+               torch.cuda.current_stream(src.device).cuda_stream)
+        return src
+
+    async def barrier(self):
+        self._require()
+        self._barrier_counter += 1
+        dev = self._device()
+        t = torch.tensor([float(self._barrier_counter)], dtype=torch.float32, device=dev)
+        await self.all_reduce(t, op="sum")
+        if dev.type == "cuda":
+            torch.cuda.current_stream(dev).synchronize()
+
+    async def send(self, tensor: torch.Tensor, dest: int):
+        """Point-to-point send of a small tensor through the store (control plane)."""
+        self._require()
+        if dest == self.rank or not 0 <= dest < self.world_size:
+            raise ValueError(f"Invalid destination rank: {dest}")
+        n = self._p2p_counter.get((self.rank, dest), 0) + 1
+        self._p2p_counter[(self.rank, dest)] = n
+        key = f"shardcompute_b200/p2p/{self.rank}->{dest}/{n}"
+        self._store.set(key, pickle.dumps((tuple(tensor.shape), str(tensor.dtype),
+                                           tensor.detach().cpu().contiguous().numpy().tobytes())))
+
+    async def recv(self, source: int) -> torch.Tensor:
+        self._require()
+        if source == self.rank or not 0 <= source < self.world_size:
+            raise ValueError(f"Invalid source rank: {source}")
+        import numpy as np
+
+        n = self._p2p_counter.get((source, self.rank), 0) + 1
+        self._p2p_counter[(source, self.rank)] = n
+        key = f"shardcompute_b200/p2p/{source}->{self.rank}/{n}"
+        self._store.wait([key], datetime.timedelta(seconds=60))
+        shape, dt, raw = pickle.loads(self._store.get(key))
+        t = torch.from_numpy(np.frombuffer(bytearray(raw), dtype=_np_dtype(dt)).reshape(shape).copy())
+        return t.to(self._device())
+
+    def flush_peers(self):
+        """NCCL keeps no per-peer receive queues; nothing to discard."""
+        return None
+
+    def get_stats(self) -> Dict[str, Any]:
+        return self.stats.to_dict()
+
+    def reset_stats(self):
+        self.stats = CommunicatorStats()
+
+    # ------------------------------------------------------------ failure handling
+
+    def poll(self) -> int:
+        """NCCL asynchronous error code (0 = healthy); never blocks."""
+        if self.backend != "nccl" or self._comm is None:
+            return 0
+        from .. import _lib as L
+
+        err = C.c_int(0)
+        L.check(L.load().sc_comm_poll(self._comm, C.byref(err)), "sc_comm_poll")
+        return err.value
+
+    def abort(self):
+        """Tear the communicator down without waiting for peers (unblocks a rank stuck on a dead peer)."""
+        if self.backend == "nccl" and self._comm is not None:
+            from .. import _lib as L
+
+            L.load().sc_comm_abort(self._comm)
+            self._comm = None
+        self._initialized = False
+
+    async def shutdown(self):
+        self.shutdown_sync()
+
+    def shutdown_sync(self):
+        if self.backend == "nccl" and self._comm is not None:
+            from .. import _lib as L
+
+            torch.cuda.synchronize()
+            L.check(L.load().sc_comm_destroy(self._comm), "sc_comm_destroy")
+            self._comm = None
+        self._initialized = False
+
+
+def _gloo_op(op: str):
+    import torch.distributed as dist
+
+    if op not in _OPS:
+        raise ValueError(f"Unknown reduction op: {op}")
+    return {"sum": dist.ReduceOp.SUM, "mean": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX,
+            "min": dist.ReduceOp.MIN}[op]
+
+
+def _np_dtype(torch_dtype_str: str):
+    import numpy as np
+
+    name = torch_dtype_str.split(".")[-1]
+    return {"float16": np.float16, "float32": np.float32, "float64": np.float64, "int32": np.int32,
+            "int64": np.int64, "uint8": np.uint8}[name]
+
+
+class ProcessGroup:
+    """Subgroup wrapper; like the reference it proxies the full communicator."""
+
+    def __init__(self, ranks: List[int], local_rank: int, comm: Communicator):
+        self.ranks = ranks
+        self.local_rank = local_rank
+        self.size = len(ranks)
+        self.comm = comm
+        self.group_to_global = {i: r for i, r in enumerate(ranks)}
+        self.global_to_group = {r: i for i, r in enumerate(ranks)}
+        self.group_rank = self.global_to_group[local_rank]
+
+    async def all_reduce(self, tensor: torch.Tensor, op: str = "sum") -> torch.Tensor:
+        return await self.comm.all_reduce(tensor, op)
+
+    async def all_gather(self, tensor: torch.Tensor, dim: int = -1) -> torch.Tensor:
+        return await self.comm.all_gather(tensor, dim)
