@@ -1,0 +1,337 @@
+#!/usr/bin/env python
+"""Decode throughput of the tensor-parallel 4-bit Llama-3-8B path on B200.
+
+Workload (default): Llama-3-8B shapes (hidden 4096, 32 layers, 32 q / 8 kv
+heads, ffn 14336, vocab 128256, RoPE theta 5e5), random-init N(0, 0.02)
+weights quantized 4-bit g64 on the GPU, tied embedding/LM head, batch 1, KV
+cache pre-filled by a 2048-token random prompt, greedy decode.  One *step* is
+one decode token for the whole batch: embedding, 32 layers, LM head, argmax,
+all captured in one CUDA graph.  Per step every rank streams its whole weight
+shard (4.5 GB at TP1), far more than the 126 MB L2, so no L2 flush is needed.
+
+``python bench.py --gpus N --steps K --warmup W``; for N > 1 it runs under
+torchrun (one process per GPU, tensor parallel, NCCL for the data path, gloo
+for timing control).  Rank 0 prints one JSON line.
+
+``--impl reference`` times the CPU stand-in of the reference's MLX CPU decode
+(torch fp32 on all host threads; MLX is not installed) on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+if HERE not in sys.path:
+    sys.path.insert(0, HERE)
+
+MODELS = {
+    "llama3-8b": dict(vocab_size=128256, hidden_size=4096, num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
+                      intermediate_size=14336, max_position_embeddings=8192, rms_norm_eps=1e-5, rope_theta=5e5,
+                      tie_word_embeddings=True),
+    "tinyllama": dict(vocab_size=32000, hidden_size=2048, num_hidden_layers=22, num_attention_heads=32, num_key_value_heads=4,
+                      intermediate_size=5632, max_position_embeddings=2048, rms_norm_eps=1e-5, rope_theta=1e4,
+                      tie_word_embeddings=True),
+    "llama3-70b": dict(vocab_size=128256, hidden_size=8192, num_hidden_layers=80, num_attention_heads=64, num_key_value_heads=8,
+                       intermediate_size=28672, max_position_embeddings=8192, rms_norm_eps=1e-5, rope_theta=5e5,
+                       tie_word_embeddings=True),
+}
+METRIC = "decode tok/s bs1 Llama-3-8B 4-bit at TP 1/2/4/8; dequant-GEMV HBM GB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", choices=sorted(MODELS), default="llama3-8b")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--bits", type=int, default=4, choices=[4, 8])
+    ap.add_argument("--group", type=int, default=64)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        sel = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            sel = ["-i", uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"]
+        except Exception:
+            pass
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"] + sel, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- reference arm
+
+def cpu_sample(args, world: int, budget_s: float):
+    """Time the CPU stand-in of the reference decode; returns (tok/s, threads, description)."""
+    from oracle.cpu_decode import CpuDecodeSample, DecodeShape
+
+    m = MODELS[args.model]
+    sh = DecodeShape(hidden=m["hidden_size"], layers=m["num_hidden_layers"], heads=m["num_attention_heads"],
+                     kv_heads=m["num_key_value_heads"],
+                     ffn=m["intermediate_size"], vocab=m["vocab_size"], bits=args.bits, group=args.group,
+                     ctx=args.ctx, batch=args.batch, world=world)
+    s = CpuDecodeSample(sh)
+    t1 = s.time_samples(1)
+    n = max(1, min(64, int(budget_s / max(t1, 1e-3))))
+    sec = s.time_samples(n)
+    desc = (f"{n} samples of 1/{sh.layers} token (one decoder layer + 1/{sh.layers} of the tied head) at "
+            f"ctx {sh.ctx}, batch {sh.batch}, TP shard 1/{world}; torch fp32 on {s.threads} threads; tok/s = "
+            f"batch / ({sh.layers} x s/sample)")
+    return s.tokens_per_s(sec), s.threads, desc, s, sec
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    from oracle.cpu_decode import CpuDecodeSample, DecodeShape
+
+    m = MODELS[args.model]
+    sh = DecodeShape(hidden=m["hidden_size"], layers=m["num_hidden_layers"], heads=m["num_attention_heads"],
+                     kv_heads=m["num_key_value_heads"], ffn=m["intermediate_size"], vocab=m["vocab_size"],
+                     bits=args.bits, group=args.group, ctx=args.ctx, batch=args.batch, world=world)
+    s = CpuDecodeSample(sh)
+    threads = s.threads
+    desc = (f"each step = 1/{sh.layers} token (one decoder layer + 1/{sh.layers} of the tied head) at ctx {sh.ctx}, "
+            f"batch {sh.batch}, TP shard 1/{world}, torch fp32 on {threads} threads; tok/s = batch / "
+            f"({sh.layers} x s/step)")
+    for _ in range(args.warmup):
+        s.run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        s.run()
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    tok_s = s.tokens_per_s(sec)
+    line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, world),
+            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "MLX (the reference's CPU backend) is not installed; the oracle's torch-fp32 restatement of the "
+                    "same per-token work is timed instead"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args, world: int):
+    return {"workload": f"cfg3 {args.model} {args.bits}-bit g{args.group} decode, batch {args.batch}, "
+                        f"KV prefilled to {args.ctx}, TP{world}",
+            "model": args.model, "global_batch": args.batch, "ctx": args.ctx, "bits": args.bits,
+            "group": args.group, "parallelism": f"tp{world}",
+            "l2": "no flush: every step streams the rank's full weight shard (> 126 MB L2)"}
+
+
+# ---------------------------------------------------------------- our arm
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.gpus != world and world > 1:
+        print(f"--gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+        return 2
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if args.warmup < 3:
+        print("--warmup must be >= 3", file=sys.stderr)
+        return 2
+
+    import torch.distributed as dist
+
+    from shardcompute_b200 import _lib
+    from shardcompute_b200.collectives import Communicator
+    from shardcompute_b200.model.config import ModelConfig
+    from shardcompute_b200.parallel.decode_engine import DecodeEngine
+    from shardcompute_b200.parallel.weights import RankWeights
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300))
+        comm = Communicator(rank, world, backend="nccl")
+        comm.initialize_sync(timeout=300)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+
+    cfg = ModelConfig.from_dict(MODELS[args.model])
+    weights = RankWeights.synthetic(cfg, world, rank, bits=args.bits, group=args.group, device=dev, seed=0)
+    B = args.batch
+    n_replays = 1 + 2 * (args.warmup + args.steps) + args.steps + 8
+    eng = DecodeEngine(weights, comm, max_batch=B, max_seq=args.ctx + n_replays + 16, device=dev)
+    gen = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, cfg.vocab_size, (B, args.ctx), generator=gen, dtype=torch.int64).to(torch.int32)
+    eng.reset()
+    eng.prefill(prompt.to(dev))
+    # one eager step: count this library's launches per step
+    c0 = _lib.load().sc_launch_count()
+    eng.decode_step()
+    torch.cuda.synchronize(dev)
+    launches_per_step = int(_lib.load().sc_launch_count() - c0)
+    eng.capture()
+
+    # ---- timed region: K graph replays, inputs resident on the device
+    for _ in range(args.warmup):
+        eng.replay()
+    barrier()
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)  # graph replays launch on the current stream
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.replay()
+    e1.record(stream)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    ms_step = ms / args.steps
+    value = B * args.steps / (ms / 1e3)
+
+    # ---- end to end: host token in (pinned), device step, host token out, each step
+    host_in = torch.zeros(B, dtype=torch.int32).pin_memory()
+    host_out = torch.zeros(B, dtype=torch.int32).pin_memory()
+    host_out.copy_(eng.tok[:B])
+    for _ in range(3):
+        host_in.copy_(host_out)
+        eng.decode_host(host_in, host_out)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_in.copy_(host_out)
+        eng.decode_host(host_in, host_out)
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = {"value": B * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": host_in.numel() * 4,
+           "d2h_bytes_per_step": host_out.numel() * 4,
+           "path": "DecodeEngine.decode_host: pinned ids -> device, graph step, sampled ids -> pinned host, sync"}
+
+    # ---- roofline of the dominant kernel (dequant-GEMV): event pairs around every GEMV of a step
+    eng.capture_probe()
+    eng.replay_probe()
+    g_ms, g_bytes, g_n = 0.0, 0, 0
+    for _ in range(args.steps):
+        a, b, n = eng.replay_probe()
+        g_ms += a
+        g_bytes += b
+        g_n += n
+    peak, peak_kind = load_peaks()
+    achieved = g_bytes / (g_ms / 1e3) / 1e9
+    gemv_share = g_ms / args.steps / ms_step
+    roofline = {"bound": "hbm", "kernel": "qgemv_tma (fused RMSNorm/dequant-GEMV/epilogue)", "achieved": achieved,
+                "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None, "launches_per_step": g_n // args.steps,
+                "algorithmic_bytes_per_step": g_bytes // args.steps, "ms_per_step": g_ms / args.steps,
+                "share_of_step": gemv_share}
+    step_bytes = g_bytes / args.steps + eng.kv_bytes_per_step()
+    roofline["step_bytes"] = step_bytes
+    roofline["step_frac"] = step_bytes / (ms_step / 1e3) / 1e9 / peak
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tok_s, threads, desc, _, _ = cpu_sample(args, world, args.cpu_seconds)
+        cpu = {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f16", "weights": f"u{args.bits} g{args.group} affine",
+                "data": "synthetic (random-init N(0,0.02) weights, uniform random prompt ids)",
+                "config": workload_config(args, world), "clocks": clk, "e2e": e2e,
+                "gpu_launches": launches_per_step * args.steps, "roofline": roofline, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    eng.graph = None
+    eng._probe_graph = None
+    if comm is not None:
+        comm.shutdown_sync()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -58,6 +58,10 @@ enum sc_reduce_op { SC_OP_SUM = 0, SC_OP_MAX = 1, SC_OP_MIN = 2, SC_OP_AVG = 3 }
 int sc_abi_version(void);
 const char* sc_status_name(int status);
 const char* sc_last_error(void);
+/* Number of kernels this library has enqueued in this process (a kernel
+ * inside a captured CUDA graph counts once, at capture).  Instrumentation
+ * for benchmarks; no counterpart in the reference. */
+unsigned long long sc_launch_count(void);
 
 /* ------------------------------------------------------------------ K1 --
  * Quantized linear: y[M, N] = x[M, K] . dequant(wq, scales, biases)^T + bias

@@ -32,6 +32,7 @@ SIGNATURES = {
     "sc_abi_version": (_i, []),
     "sc_status_name": (C.c_char_p, [_i]),
     "sc_last_error": (C.c_char_p, []),
+    "sc_launch_count": (C.c_ulonglong, []),
     "sc_qlinear_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "sc_qgemv_device_error": (_i, [_i]),
     "sc_qlinear": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),

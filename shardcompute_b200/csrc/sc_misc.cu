@@ -1,5 +1,6 @@
 // K5 / K7 and the ABI plumbing: RMSNorm, SiLU*mul, add, greedy argmax over
 // vocab-split logits, status strings and the thread-local error message.
+#include <atomic>
 #include <stdarg.h>
 #include <stdio.h>
 #include <climits>
@@ -19,12 +20,16 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+// Kernels enqueued by this library (each successful check follows exactly one launch).
+static std::atomic<unsigned long long> g_launches{0};
+
 int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
     return SC_ERR_CUDA;
   }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return SC_OK;
 }
 
@@ -177,6 +182,8 @@ const char* sc_status_name(int status) {
 }
 
 const char* sc_last_error(void) { return sc::g_err; }
+
+unsigned long long sc_launch_count(void) { return sc::g_launches.load(std::memory_order_relaxed); }
 
 int sc_rmsnorm(const void* x, int x_dtype, int M, int H, const uint16_t* w, float eps, void* y, int y_dtype,
                cudaStream_t stream) {

@@ -1,0 +1,372 @@
+"""Fused per-rank forward of the tensor-parallel quantized decoder.
+
+This is the hot path behind ``ParallelTransformer.forward`` /
+``ParallelExecutor.generate`` (reference parallel/transformer.py:516-577,
+worker/executor.py:229-325), re-laid for B200:
+
+* one step = embedding gather (K3) -> per layer [RMSNorm+q|k|v GEMV (K1) ->
+  RoPE+KV append (K4) -> split-KV flash-decode (K4) -> o GEMV + residual (K1)
+  -> RMSNorm+gate|up GEMV with SiLU*mul (K1) -> down GEMV + residual (K1)] ->
+  RMSNorm+tied LM-head GEMV (K1) -> argmax (K7);
+* TP > 1: the embedding and the two row-parallel outputs per layer are
+  all-reduced with NCCL; rank 0 folds the residual into its partial so the
+  all-reduce output *is* the new hidden state; greedy sampling gathers only
+  (max, index) per rank instead of the vocab-split logits;
+* the residual stream is fp32, GEMV inputs fp16, KV cache fp16
+  ``[L, 2, B, Hkv/TP, Lmax, hd]``, preallocated;
+* positions and token ids live in device buffers, so one decode step is
+  captured once in a CUDA graph and replayed; each replay reads the token the
+  previous replay wrote and advances the position counter on the device.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from .. import _lib as L
+from .. import ops
+from ..model.config import ModelConfig
+from .weights import RankWeights
+
+
+def rope_table(head_dim: int, length: int, base: float):
+    """fp32 cos/sin ``[length, head_dim/2]`` computed as the reference does
+    (inv_freq = 1 / base**(arange(0, hd, 2)/hd), angles = outer(t, inv_freq);
+    parallel/attention.py:56-92)."""
+    inv = (np.float32(1.0) / (np.float32(base) ** (np.arange(0, head_dim, 2, dtype=np.float32)
+                                                    / np.float32(head_dim)))).astype(np.float32)
+    ang = np.outer(np.arange(length, dtype=np.float32), inv).astype(np.float32)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+class DecodeEngine:
+    """One rank's decoder state: weights, KV cache, buffers, captured step."""
+
+    def __init__(self, weights: RankWeights, comm=None, max_batch: int = 1, max_seq: int = 2048,
+                 device: Optional[torch.device] = None, attn_splits: Optional[int] = None):
+        cfg: ModelConfig = weights.cfg
+        self.cfg = cfg
+        self.w = weights
+        self.comm = comm
+        self.world = weights.world
+        self.rank = weights.rank
+        if self.world > 1 and comm is None:
+            raise RuntimeError("Communicator required for tensor parallelism (world_size > 1)")
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        dev = self.device
+        self.B = max_batch
+        self.Lmax = max_seq
+        self.H = cfg.hidden_size
+        self.hd = cfg.head_dim
+        self.Hq = cfg.num_heads // self.world
+        self.Hkv = cfg.kv_heads // self.world
+        self.F = cfg.intermediate_size // self.world
+        self.Vl = cfg.vocab_size // self.world
+        self.bits, self.group = weights.bits, weights.group
+        self.eps = cfg.rms_norm_eps
+        nl = cfg.num_layers
+        self.kv = torch.zeros(nl, 2, self.B, self.Hkv, self.Lmax, self.hd, dtype=torch.float16, device=dev)
+        cos, sin = rope_table(self.hd, self.Lmax, cfg.rope_theta)
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.host_pos = 0  # host mirror of pos: bounds every step against the cache length
+        self.tok = torch.zeros(self.B, dtype=torch.int32, device=dev)  # decode input / sampled output
+        if attn_splits is None:
+            attn_splits = max(1, min(64, math.ceil(2 * 148 / max(1, self.Hkv * self.B)), math.ceil(self.Lmax / 64)))
+        self.splits = attn_splits
+        self._bufs = {}
+        self._probe: Optional[list] = None  # (start, end, bytes) per GEMV while instrumenting
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self._graph_stream: Optional[torch.cuda.Stream] = None
+        # decode scratch: fixed for the engine's lifetime (a captured graph keeps its address)
+        self.workspace = torch.empty(self._workspace_bytes(self.B, 1), dtype=torch.uint8, device=dev)
+        self._ws = self.workspace
+
+    # ------------------------------------------------------------ buffers
+
+    def _workspace_bytes(self, B: int, S: int) -> int:
+        M = B * S
+        qkvN = (self.Hq + 2 * self.Hkv) * self.hd
+        need = [ops.qlinear_workspace_bytes(M, self.H, qkvN, self.bits),
+                ops.qlinear_workspace_bytes(M, self.Hq * self.hd, self.H, self.bits),
+                ops.qlinear_workspace_bytes(M, self.H, self.F, self.bits) * 2,
+                ops.qlinear_workspace_bytes(M, self.F, self.H, self.bits),
+                ops.qlinear_workspace_bytes(M, self.H, self.Vl, self.bits),
+                ops.flash_decode_workspace_bytes(B, S, self.Hq, self.hd, self.splits if S == 1 else 1),
+                ops.argmax_workspace_bytes(B, self.Vl)]
+        return max(max(need), 1 << 16)
+
+    def _use_workspace(self, B: int, S: int):
+        """Select scratch for a (B, S) pass: the decode workspace when it is
+        big enough, else a transient one (prefill), never the captured one resized."""
+        need = self._workspace_bytes(B, S)
+        if need <= self.workspace.numel():
+            self._ws = self.workspace
+        else:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+
+    def _buffers(self, B: int, S: int):
+        key = (B, S)
+        if key in self._bufs:
+            return self._bufs[key]
+        dev, M = self.device, B * S
+        b = {
+            "ids": torch.zeros(M, dtype=torch.int32, device=dev),
+            "h": torch.zeros(M, self.H, dtype=torch.float32, device=dev),
+            "part": torch.zeros(M, self.H, dtype=torch.float32, device=dev),
+            "qkv": torch.zeros(M, (self.Hq + 2 * self.Hkv) * self.hd, dtype=torch.float32, device=dev),
+            "q": torch.zeros(M, self.Hq * self.hd, dtype=torch.float32, device=dev),
+            "attn": torch.zeros(M, self.Hq * self.hd, dtype=torch.float16, device=dev),
+            "act": torch.zeros(M, self.F, dtype=torch.float16, device=dev),
+            "hlast": torch.zeros(B, self.H, dtype=torch.float32, device=dev),
+            "logits": torch.zeros(B, self.Vl, dtype=torch.float32, device=dev),
+            "val": torch.zeros(B, dtype=torch.float32, device=dev),
+            "idx": torch.zeros(B, dtype=torch.int32, device=dev),
+            "gval": torch.zeros(self.world, B, dtype=torch.float32, device=dev),
+            "gidx": torch.zeros(self.world, B, dtype=torch.int32, device=dev),
+        }
+        if S > 1 and S * B > 64:  # prefill buffers are transient; keep only decode-sized ones cached
+            return b
+        self._bufs[key] = b
+        return b
+
+    # ------------------------------------------------------------ kernels of one step
+
+    def _qlin(self, x, segs, out, epilogue=L.SC_EPI_STORE, norm=None, residual=None):
+        """Fused GEMV through the C ABI with the engine's workspace."""
+        n = len(segs)
+        import ctypes as C
+
+        M, K = x.shape
+        rows = [int(s[0].shape[0]) for s in segs]
+        N = rows[0] if epilogue == L.SC_EPI_SWIGLU else sum(rows)
+        W = (C.c_void_p * n)(*[s[0].data_ptr() for s in segs])
+        Sp = (C.c_void_p * n)(*[s[1].data_ptr() for s in segs])
+        Bp = (C.c_void_p * n)(*[s[2].data_ptr() for s in segs])
+        R = (C.c_int * n)(*rows)
+        if self._probe is not None:
+            ev0 = torch.cuda.Event(enable_timing=True, external=True)
+            ev1 = torch.cuda.Event(enable_timing=True, external=True)
+            ev0.record()
+        L.call("sc_qlinear_fused", x.data_ptr(), ops._dt(x), M, K, K,
+               None if norm is None else norm.data_ptr(), float(self.eps), n,
+               C.cast(W, L._pp), C.cast(Sp, L._pp), C.cast(Bp, L._pp), R, self.group, self.bits, None, epilogue,
+               out.data_ptr(), ops._dt(out), N, None if residual is None else residual.data_ptr(),
+               N if residual is not None else 0, self._ws.data_ptr(), self._ws.numel(),
+               ops.stream_handle(self.device))
+        if self._probe is not None:
+            ev1.record()
+            # algorithmic bytes: packed words + fp16 scale/bias of every segment,
+            # the activations in, the norm weight, the outputs (and residual) once
+            nbytes = (sum(r * K * self.bits // 8 + r * (K // self.group) * 4 for r in rows) +
+                      M * K * x.element_size() + (0 if norm is None else K * 2) +
+                      M * N * out.element_size() + (M * N * residual.element_size() if residual is not None else 0))
+            self._probe.append((ev0, ev1, nbytes))
+
+    def _allreduce(self, send, recv):
+        if self.world == 1:
+            if send.data_ptr() != recv.data_ptr():
+                recv.copy_(send)
+            return
+        self.comm.allreduce_into(send, recv, "sum")
+
+    def _layers(self, bf, B: int, S: int, hidden: Optional[List[torch.Tensor]] = None):
+        """Embedding + all layers for M = B*S tokens at positions pos..pos+S-1."""
+        w, M = self.w, B * S
+        h = bf["h"]
+        ops.embed_gather_q(bf["ids"], *w.embed, w.vocab_start, w.vocab_end, self.H, self.group, self.bits,
+                           out=h)
+        self._allreduce(h, h)
+        if hidden is not None:
+            hidden.append(h.clone())
+        splits = self.splits if S == 1 else 1
+        for i, lw in enumerate(w.layers):
+            kc, vc = self.kv[i, 0], self.kv[i, 1]
+            self._qlin(h, [lw.q, lw.k, lw.v], bf["qkv"], norm=lw.ln1)
+            ops.rope_append(bf["qkv"], B, S, self.Hq, self.Hkv, self.hd, self.pos, self.cos, self.sin, bf["q"], kc, vc)
+            ops.flash_decode(bf["q"], kc, vc, self.pos, B, S, self.Hq, self.Hkv, self.hd, splits, bf["attn"],
+                             workspace=self._ws)
+            self._row_out(bf["attn"], lw.o, h, bf["part"])
+            self._qlin(h, [lw.gate, lw.up], bf["act"], epilogue=L.SC_EPI_SWIGLU, norm=lw.ln2)
+            self._row_out(bf["act"], lw.down, h, bf["part"])
+            if hidden is not None:
+                hidden.append(h.clone())
+
+    def _row_out(self, x, tri, h, part):
+        """Row-parallel linear + residual.  TP=1: h += x.W^T in place.  TP>1:
+        rank 0 writes h + x.W^T, others x.W^T, and the all-reduce of those
+        partials lands in h (the residual is added exactly once)."""
+        if self.world == 1:
+            self._qlin(x, [tri], h, epilogue=L.SC_EPI_RESIDUAL, residual=h)
+            return
+        if self.rank == 0:
+            self._qlin(x, [tri], part, epilogue=L.SC_EPI_RESIDUAL, residual=h)
+        else:
+            self._qlin(x, [tri], part)
+        self._allreduce(part, h)
+
+    def _sample(self, bf, hlast, B: int, advance: int):
+        """Tied LM head on the last position of each sequence + greedy argmax."""
+        w = self.w
+        self._qlin(hlast, [w.embed], bf["logits"], norm=w.norm)
+        ops.argmax(bf["logits"], index_offset=w.vocab_start, val=bf["val"], idx=bf["idx"])
+        if self.world > 1:
+            self.comm.allgather_into(bf["val"], bf["gval"])
+            self.comm.allgather_into(bf["idx"], bf["gidx"])
+            ops.argmax_merge(bf["gval"], bf["gidx"], self.world, self.tok[:B], self.pos, advance)
+        else:
+            ops.argmax_merge(bf["val"].view(1, B), bf["idx"].view(1, B), 1, self.tok[:B], self.pos, advance)
+
+    # ------------------------------------------------------------ public steps
+
+    def reset(self):
+        self.pos.zero_()
+        self.host_pos = 0
+
+    def _advance(self, n: int):
+        if self.host_pos + n > self.Lmax:
+            raise ValueError(f"KV cache full: position {self.host_pos} + {n} exceeds max_seq {self.Lmax}")
+        self.host_pos += n
+
+    def kv_bytes_per_step(self) -> int:
+        """KV-cache bytes one decode step reads at the current length (all layers)."""
+        return self.cfg.num_layers * 2 * self.B * self.Hkv * self.host_pos * self.hd * 2
+
+    def prefill(self, input_ids: torch.Tensor):
+        """Run the prompt ``[B, S]`` through the model; the first generated
+        token lands in ``self.tok`` and the position counter advances by S."""
+        B, S = input_ids.shape
+        if B > self.B:
+            raise ValueError(f"batch {B} > engine max_batch {self.B}")
+        self._advance(S)
+        bf = self._buffers(B, S)
+        self._use_workspace(B, S)
+        bf["ids"].copy_(input_ids.reshape(-1).to(torch.int32), non_blocking=True)
+        self._layers(bf, B, S)
+        hl = bf["h"].view(B, S, self.H)[:, -1] if S > 1 else bf["h"]
+        bf["hlast"][:B].copy_(hl)
+        self._sample(bf, bf["hlast"][:B], B, S)
+
+    def decode_step(self):
+        """One greedy step for the engine's full batch (eager)."""
+        self._advance(1)
+        B = self.B
+        bf = self._buffers(B, 1)
+        self._ws = self.workspace
+        bf["ids"].copy_(self.tok[:B])
+        self._layers(bf, B, 1)
+        self._sample(bf, bf["h"], B, 1)
+
+    def capture(self):
+        """Capture decode_step in a CUDA graph (after one eager warm-up)."""
+        self._graph_stream = torch.cuda.Stream(device=self.device)
+        self._graph_stream.wait_stream(torch.cuda.current_stream(self.device))
+        pos0 = self.pos.clone()
+        tok0 = self.tok.clone()
+        hp0 = self.host_pos
+        with torch.cuda.stream(self._graph_stream):
+            self.decode_step()  # warm-up: plans, tensor maps, lazy module loads
+        torch.cuda.current_stream(self.device).wait_stream(self._graph_stream)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self._graph_stream):
+            self.decode_step()
+        torch.cuda.synchronize(self.device)
+        self.host_pos = hp0
+        # the eager warm-up advanced the position and wrote one cache slot that
+        # the next real step overwrites; put the position and token back
+        self.pos.copy_(pos0)
+        self.tok.copy_(tok0)
+        return self.graph
+
+    def capture_probe(self):
+        """Capture a second copy of the decode step with a CUDA event pair
+        around every dequant-GEMV launch; ``replay_probe`` then returns the
+        summed GEMV device time and algorithmic bytes of one step."""
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        self._probe = []
+        g = torch.cuda.CUDAGraph()
+        hp0 = self.host_pos
+        try:
+            with torch.cuda.graph(g, stream=stream):
+                self.decode_step()
+        finally:
+            probe, self._probe = self._probe, None
+            self.host_pos = hp0
+        torch.cuda.synchronize(self.device)
+        self._probe_graph, self._probe_events = g, probe
+        return g
+
+    def replay_probe(self):
+        """Replay the instrumented step; returns (gemv_ms, gemv_bytes, launches)."""
+        self._advance(1)
+        self._probe_graph.replay()
+        torch.cuda.synchronize(self.device)
+        ms = sum(a.elapsed_time(b) for a, b, _ in self._probe_events)
+        return ms, sum(n for _, _, n in self._probe_events), len(self._probe_events)
+
+    def decode_host(self, tokens: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """One greedy step driven from host memory: copy ``tokens`` (pinned
+        int32 [B]) to the device, replay the step, copy the sampled tokens
+        back into ``out`` (pinned int32 [B]) and wait for them."""
+        self.tok[: tokens.numel()].copy_(tokens, non_blocking=True)
+        self.replay()
+        out.copy_(self.tok[: out.numel()], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out
+
+    def replay(self):
+        if self.graph is None:
+            self.capture()
+        self._advance(1)
+        self.graph.replay()
+
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, stop_tokens=(), use_graph: bool = True):
+        """Greedy generation: prefill, then one token per step, each read back
+        to the host (the reference's per-token stop check,
+        worker/executor.py:308-313)."""
+        self.reset()
+        self.prefill(input_ids)
+        B = input_ids.shape[0]
+        out = []
+        host_tok = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        for t in range(max_new_tokens):
+            host_tok.copy_(self.tok[:B], non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            out.append(host_tok.clone())
+            if int(host_tok[0]) in stop_tokens or t == max_new_tokens - 1:
+                break
+            if use_graph and B == self.B:
+                self.replay()
+            else:
+                self.decode_step()
+        return torch.stack(out, dim=1)
+
+    def forward_logits(self, input_ids: torch.Tensor, return_hidden: bool = False):
+        """Full forward of ``[B, S]`` ids at the current position (cache
+        updated): logits for every position, gathered over the vocab split
+        (``ParallelTransformer.forward`` semantics), optionally with the hidden
+        state after the embedding and after each layer."""
+        B, S = input_ids.shape
+        self._advance(S)
+        bf = self._buffers(B, S)
+        self._use_workspace(B, S)
+        bf["ids"].copy_(input_ids.reshape(-1).to(torch.int32))
+        hidden = [] if return_hidden else None
+        self._layers(bf, B, S, hidden)
+        logits = torch.empty(B * S, self.Vl, dtype=torch.float32, device=self.device)
+        self._qlin(bf["h"], [self.w.embed], logits, norm=self.w.norm)
+        if self.world > 1:
+            g = torch.empty(self.world, B * S, self.Vl, dtype=torch.float32, device=self.device)
+            self.comm.allgather_into(logits, g)
+            logits = g.permute(1, 0, 2).reshape(B * S, self.world * self.Vl)
+        with torch.no_grad():
+            self.pos += S
+        logits = logits.view(B, S, -1)
+        return (logits, hidden) if return_hidden else logits
