@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--group", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: build this many decoder layers instead of the model's")
     return ap.parse_args()
 
 
@@ -189,7 +191,8 @@ def run_reference(args, rank: int, world: int):
 
 
 def workload_config(args, world: int):
-    return {"workload": f"cfg3 {args.model} {args.bits}-bit g{args.group} decode, batch {args.batch}, "
+    extra = {"layers": args.layers, "note": "profiling case: reduced layer count"} if args.layers else {}
+    return {**extra, "workload": f"cfg3 {args.model} {args.bits}-bit g{args.group} decode, batch {args.batch}, "
                         f"KV prefilled to {args.ctx}, TP{world}",
             "model": args.model, "global_batch": args.batch, "ctx": args.ctx, "bits": args.bits,
             "group": args.group, "parallelism": f"tp{world}",
@@ -238,7 +241,10 @@ def main():
         if world > 1:
             dist.barrier()
 
-    cfg = ModelConfig.from_dict(MODELS[args.model])
+    mdict = dict(MODELS[args.model])
+    if args.layers:
+        mdict["num_hidden_layers"] = args.layers
+    cfg = ModelConfig.from_dict(mdict)
     weights = RankWeights.synthetic(cfg, world, rank, bits=args.bits, group=args.group, device=dev, seed=0)
     B = args.batch
     n_replays = 1 + 2 * (args.warmup + args.steps) + args.steps + 8
@@ -262,10 +268,12 @@ def main():
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream(dev)  # graph replays launch on the current stream
+    torch.cuda.nvtx.range_push("timed")
     e0.record(stream)
     for _ in range(args.steps):
         eng.replay()
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1))
     clk = clocks.stop()
