@@ -22,6 +22,8 @@ __global__ void rope_append_kernel(const float* __restrict__ qkv, int S, int Hq,
                                    const int32_t* __restrict__ pos_ptr, const float* __restrict__ cos_tab,
                                    const float* __restrict__ sin_tab, int max_pos, float* __restrict__ q_out,
                                    __half* __restrict__ kc, __half* __restrict__ vc, int Lmax) {
+  pdl_trigger();
+  pdl_wait();
   const int tok = blockIdx.x;  // b*S + s
   const int b = tok / S, s = tok % S;
   const int pos = *pos_ptr + s;
@@ -63,6 +65,8 @@ __global__ void __launch_bounds__(FD_WARPS * 32)
 flash_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
                     const int32_t* __restrict__ pos_ptr, int S, int Hq, int Hkv, int Lmax, float scale,
                     int splits, float* __restrict__ part, OT* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int LPK = HD / 8;    // lanes per key
   constexpr int KPS = 32 / LPK;  // keys per warp step
   const int split = blockIdx.x, kvh = blockIdx.y, tok = blockIdx.z;
@@ -179,6 +183,8 @@ flash_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc, 
 
 template <int HD, typename OT>
 __global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq, int splits, OT* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int qh = blockIdx.x, tok = blockIdx.y;
   const float* pp = part + ((size_t)tok * Hq + qh) * splits * (HD + 2);
   float M = -INFINITY;
@@ -199,11 +205,11 @@ template <int HD, int G, typename OT>
 static int launch_fd(const float* q, const __half* kc, const __half* vc, const int32_t* pos, int B, int S, int Hq,
                      int Hkv, int Lmax, float scale, int splits, float* part, OT* out, cudaStream_t stream) {
   dim3 grid(splits, Hkv, B * S);
-  flash_decode_kernel<HD, G, OT><<<grid, FD_WARPS * 32, 0, stream>>>(q, kc, vc, pos, S, Hq, Hkv, Lmax, scale, splits,
+  ::sc::launch(flash_decode_kernel<HD, G, OT>, grid, FD_WARPS * 32, 0, stream, q, kc, vc, pos, S, Hq, Hkv, Lmax, scale, splits,
                                                                     part, out);
   int st = check_launch("flash_decode");
   if (st != SC_OK || splits == 1) return st;
-  flash_decode_merge_kernel<HD, OT><<<dim3(Hq, B * S), HD, 0, stream>>>(part, Hq, splits, out);
+  ::sc::launch(flash_decode_merge_kernel<HD, OT>, dim3(Hq, B * S), HD, 0, stream, part, Hq, splits, out);
   return check_launch("flash_decode_merge");
 }
 
@@ -231,7 +237,7 @@ int sc_rope_append(const float* qkv, int B, int S, int Hq, int Hkv, int hd, cons
   SC_REQUIRE(Hq > 0 && Hkv > 0 && B > 0 && S > 0, SC_ERR_SHAPE, "rope_append: empty shape");
   SC_REQUIRE(qkv && pos && cos_tab && sin_tab && q_out && k_cache && v_cache, SC_ERR_ARG,
              "rope_append: null pointer");
-  sc::rope_append_kernel<<<B * S, 256, 0, stream>>>(qkv, S, Hq, Hkv, hd, pos, cos_tab, sin_tab, max_pos, q_out,
+  ::sc::launch(sc::rope_append_kernel, B * S, 256, 0, stream, qkv, S, Hq, Hkv, hd, pos, cos_tab, sin_tab, max_pos, q_out,
                                                     (__half*)k_cache, (__half*)v_cache, Lmax);
   return sc::check_launch("rope_append");
 }

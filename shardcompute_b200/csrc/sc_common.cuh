@@ -6,6 +6,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 #include <stdio.h>
 
 #include "../../include/sc_b200.h"
@@ -17,6 +20,43 @@ void set_error(const char* fmt, ...);
 
 // Returns SC_OK or SC_ERR_CUDA (with the launch error recorded).
 int check_launch(const char* what);
+int check_launch(const char* what, cudaError_t launch_status);
+
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with programmatic stream serialisation, so it may be scheduled while its
+// predecessor in the stream is still running (hiding the launch gap and the
+// predecessor's tail).  Each kernel therefore (1) executes pdl_wait() in
+// every CTA before it reads anything a predecessor writes or writes anything
+// a predecessor reads -- griddepcontrol.wait returns once every prerequisite
+// grid has completed and its memory is visible -- and (2) signals
+// pdl_trigger() as soon as its own CTAs are all resident, letting the next
+// kernel's CTAs take SMs as they free up.  Only reads of data no kernel of the
+// step writes (weights, scales, biases) may precede pdl_wait().  Without the
+// launch attribute both instructions are no-ops.  SC_PDL=0 disables it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+// Records a failed launch for the next check_launch() on this thread.
+void note_launch_status(cudaError_t e);
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  note_launch_status(e);
+  return e;
+}
 
 #define SC_REQUIRE(cond, code, ...)          \
   do {                                       \

@@ -61,6 +61,8 @@ template <int BITS, typename OT>
 __global__ void embed_gather_q_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ wq,
                                       const uint16_t* __restrict__ scales, const uint16_t* __restrict__ biases,
                                       int v0, int v1, int H, int group, OT* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PF = 32 / BITS;
   constexpr int VPS = 4 * PF;  // values per 16-byte slice
   const int row = blockIdx.x;
@@ -87,6 +89,8 @@ __global__ void embed_gather_q_kernel(const int32_t* __restrict__ ids, const uin
 template <typename OT>
 __global__ void embed_gather_f16_kernel(const int32_t* __restrict__ ids, const uint16_t* __restrict__ table,
                                         int v0, int v1, int H, OT* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const int id = ids[row];
   OT* o = out + (size_t)row * H;
@@ -109,6 +113,8 @@ template <int BITS>
 __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const uint16_t* __restrict__ scales,
                                   const uint16_t* __restrict__ biases, int rows, int K, int group,
                                   __half* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PF = 32 / BITS;
   constexpr int VPS = 4 * PF;
   const size_t nsl_row = K / VPS;
@@ -132,6 +138,8 @@ template <int BITS>
 __global__ void quantize_kernel(const __half* __restrict__ w, int rows, int K, int group,
                                 uint32_t* __restrict__ wq, uint16_t* __restrict__ scales,
                                 uint16_t* __restrict__ biases) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PF = 32 / BITS;
   constexpr int NB = (1 << BITS) - 1;
   const int KG = K / group;
@@ -194,17 +202,17 @@ int sc_embed_gather_q(const int32_t* ids, int n, const uint32_t* wq, const uint1
   const int threads = 128;
   if (bits == 4) {
     if (out_dtype == SC_F16)
-      sc::embed_gather_q_kernel<4, __half><<<n, threads, 0, stream>>>(ids, wq, scales, biases, vocab_start, vocab_end,
+      ::sc::launch(sc::embed_gather_q_kernel<4, __half>, n, threads, 0, stream, ids, wq, scales, biases, vocab_start, vocab_end,
                                                                       H, group_size, (__half*)out);
     else
-      sc::embed_gather_q_kernel<4, float><<<n, threads, 0, stream>>>(ids, wq, scales, biases, vocab_start, vocab_end,
+      ::sc::launch(sc::embed_gather_q_kernel<4, float>, n, threads, 0, stream, ids, wq, scales, biases, vocab_start, vocab_end,
                                                                      H, group_size, (float*)out);
   } else {
     if (out_dtype == SC_F16)
-      sc::embed_gather_q_kernel<8, __half><<<n, threads, 0, stream>>>(ids, wq, scales, biases, vocab_start, vocab_end,
+      ::sc::launch(sc::embed_gather_q_kernel<8, __half>, n, threads, 0, stream, ids, wq, scales, biases, vocab_start, vocab_end,
                                                                       H, group_size, (__half*)out);
     else
-      sc::embed_gather_q_kernel<8, float><<<n, threads, 0, stream>>>(ids, wq, scales, biases, vocab_start, vocab_end,
+      ::sc::launch(sc::embed_gather_q_kernel<8, float>, n, threads, 0, stream, ids, wq, scales, biases, vocab_start, vocab_end,
                                                                      H, group_size, (float*)out);
   }
   return sc::check_launch("embed_gather_q");
@@ -219,9 +227,9 @@ int sc_embed_gather_f16(const int32_t* ids, int n, const uint16_t* table, int vo
   SC_REQUIRE(ids && table && out, SC_ERR_ARG, "embed_gather_f16: null pointer");
   const int threads = std::min(256, std::max(32, ((H / 8) + 31) / 32 * 32));
   if (out_dtype == SC_F16)
-    sc::embed_gather_f16_kernel<__half><<<n, threads, 0, stream>>>(ids, table, vocab_start, vocab_end, H, (__half*)out);
+    ::sc::launch(sc::embed_gather_f16_kernel<__half>, n, threads, 0, stream, ids, table, vocab_start, vocab_end, H, (__half*)out);
   else
-    sc::embed_gather_f16_kernel<float><<<n, threads, 0, stream>>>(ids, table, vocab_start, vocab_end, H, (float*)out);
+    ::sc::launch(sc::embed_gather_f16_kernel<float>, n, threads, 0, stream, ids, table, vocab_start, vocab_end, H, (float*)out);
   return sc::check_launch("embed_gather_f16");
 }
 
@@ -236,9 +244,9 @@ int sc_dequantize(const uint32_t* wq, const uint16_t* scales, const uint16_t* bi
   SC_REQUIRE(wq && scales && biases && out, SC_ERR_ARG, "dequantize: null pointer");
   const int blocks = 4 * sc::sm_count();
   if (bits == 4)
-    sc::dequantize_kernel<4><<<blocks, 256, 0, stream>>>(wq, scales, biases, rows, K, group_size, (__half*)out);
+    ::sc::launch(sc::dequantize_kernel<4>, blocks, 256, 0, stream, wq, scales, biases, rows, K, group_size, (__half*)out);
   else
-    sc::dequantize_kernel<8><<<blocks, 256, 0, stream>>>(wq, scales, biases, rows, K, group_size, (__half*)out);
+    ::sc::launch(sc::dequantize_kernel<8>, blocks, 256, 0, stream, wq, scales, biases, rows, K, group_size, (__half*)out);
   return sc::check_launch("dequantize");
 }
 
@@ -253,9 +261,9 @@ int sc_quantize(const uint16_t* w, int rows, int K, int group_size, int bits, ui
   SC_REQUIRE(w && wq && scales && biases, SC_ERR_ARG, "quantize: null pointer");
   const int blocks = 8 * sc::sm_count();
   if (bits == 4)
-    sc::quantize_kernel<4><<<blocks, 256, 0, stream>>>((const __half*)w, rows, K, group_size, wq, scales, biases);
+    ::sc::launch(sc::quantize_kernel<4>, blocks, 256, 0, stream, (const __half*)w, rows, K, group_size, wq, scales, biases);
   else
-    sc::quantize_kernel<8><<<blocks, 256, 0, stream>>>((const __half*)w, rows, K, group_size, wq, scales, biases);
+    ::sc::launch(sc::quantize_kernel<8>, blocks, 256, 0, stream, (const __half*)w, rows, K, group_size, wq, scales, biases);
   return sc::check_launch("quantize");
 }
 

@@ -23,14 +23,33 @@ void set_error(const char* fmt, ...) {
 // Kernels enqueued by this library (each successful check follows exactly one launch).
 static std::atomic<unsigned long long> g_launches{0};
 
-int check_launch(const char* what) {
-  const cudaError_t e = cudaGetLastError();
+static thread_local cudaError_t g_launch_status = cudaSuccess;
+
+void note_launch_status(cudaError_t e) {
+  if (e != cudaSuccess && g_launch_status == cudaSuccess) g_launch_status = e;
+}
+
+int check_launch(const char* what, cudaError_t launch_status) {
+  const cudaError_t last = cudaGetLastError();  // also clears a sticky launch error
+  const cudaError_t noted = g_launch_status;
+  g_launch_status = cudaSuccess;
+  const cudaError_t e = launch_status != cudaSuccess ? launch_status : (noted != cudaSuccess ? noted : last);
   if (e != cudaSuccess) {
     set_error("%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
     return SC_ERR_CUDA;
   }
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return SC_OK;
+}
+
+int check_launch(const char* what) { return check_launch(what, cudaSuccess); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SC_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 template <typename T>
@@ -42,6 +61,8 @@ __device__ __forceinline__ float ldf(const void* p, size_t i) {
 template <typename XT, typename YT>
 __global__ void rmsnorm_kernel(const void* __restrict__ x, int H, const uint16_t* __restrict__ w, float eps,
                                void* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   float ss = 0.f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -70,12 +91,16 @@ __global__ void rmsnorm_kernel(const void* __restrict__ x, int H, const uint16_t
 
 template <typename IT, typename OT>
 __global__ void silu_mul_kernel(const void* __restrict__ g, const void* __restrict__ u, size_t n, void* __restrict__ o) {
+  pdl_trigger();
+  pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     reinterpret_cast<OT*>(o)[i] = from_f32<OT>(silu_f32(ldf<IT>(g, i)) * ldf<IT>(u, i));
 }
 
 template <typename AT, typename BT, typename YT>
 __global__ void add_kernel(const void* __restrict__ a, const void* __restrict__ b, size_t n, void* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     reinterpret_cast<YT*>(y)[i] = from_f32<YT>(ldf<AT>(a, i) + ldf<BT>(b, i));
 }
@@ -90,6 +115,8 @@ constexpr int AM_CHUNK = 4096;
 
 __global__ void argmax_partial_kernel(const float* __restrict__ logits, int N, int ldl, float* __restrict__ pv,
                                       int* __restrict__ pi, int nchunks) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x, row = blockIdx.y;
   const int beg = c * AM_CHUNK, end = min(N, beg + AM_CHUNK);
   float bv = -INFINITY;
@@ -118,6 +145,8 @@ __global__ void argmax_partial_kernel(const float* __restrict__ logits, int N, i
 
 __global__ void argmax_final_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int nchunks,
                                     int offset, float* __restrict__ val, int32_t* __restrict__ idx) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   float bv = -INFINITY;
   int bi = INT_MAX;
@@ -140,6 +169,8 @@ __global__ void argmax_final_kernel(const float* __restrict__ pv, const int* __r
 
 __global__ void argmax_merge_kernel(const float* __restrict__ vals, const int32_t* __restrict__ idxs, int M, int world,
                                     int32_t* __restrict__ tok, int32_t* __restrict__ pos, int adv) {
+  pdl_trigger();
+  pdl_wait();
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     float bv = -INFINITY;
     int bi = INT_MAX;
@@ -156,8 +187,8 @@ __global__ void argmax_merge_kernel(const float* __restrict__ vals, const int32_
 template <typename A, typename B>
 static int add_dispatch_y(const void* a, const void* b, size_t n, void* y, int yd, cudaStream_t st) {
   const int blocks = (int)std::min<size_t>((n + 255) / 256, 8 * (size_t)sm_count());
-  if (yd == SC_F16) add_kernel<A, B, __half><<<blocks, 256, 0, st>>>(a, b, n, y);
-  else add_kernel<A, B, float><<<blocks, 256, 0, st>>>(a, b, n, y);
+  if (yd == SC_F16) ::sc::launch(add_kernel<A, B, __half>, blocks, 256, 0, st, a, b, n, y);
+  else ::sc::launch(add_kernel<A, B, float>, blocks, 256, 0, st, a, b, n, y);
   return check_launch("add");
 }
 
@@ -191,10 +222,10 @@ int sc_rmsnorm(const void* x, int x_dtype, int M, int H, const uint16_t* w, floa
   if (M <= 0) return SC_OK;
   SC_REQUIRE(x && w && y, SC_ERR_ARG, "rmsnorm: null pointer");
   const int threads = std::min(1024, std::max(32, (H + 31) / 32 * 32 / 4));
-  if (x_dtype == SC_F32 && y_dtype == SC_F32) sc::rmsnorm_kernel<float, float><<<M, threads, 0, stream>>>(x, H, w, eps, y);
-  else if (x_dtype == SC_F32 && y_dtype == SC_F16) sc::rmsnorm_kernel<float, __half><<<M, threads, 0, stream>>>(x, H, w, eps, y);
-  else if (x_dtype == SC_F16 && y_dtype == SC_F32) sc::rmsnorm_kernel<__half, float><<<M, threads, 0, stream>>>(x, H, w, eps, y);
-  else if (x_dtype == SC_F16 && y_dtype == SC_F16) sc::rmsnorm_kernel<__half, __half><<<M, threads, 0, stream>>>(x, H, w, eps, y);
+  if (x_dtype == SC_F32 && y_dtype == SC_F32) ::sc::launch(sc::rmsnorm_kernel<float, float>, M, threads, 0, stream, x, H, w, eps, y);
+  else if (x_dtype == SC_F32 && y_dtype == SC_F16) ::sc::launch(sc::rmsnorm_kernel<float, __half>, M, threads, 0, stream, x, H, w, eps, y);
+  else if (x_dtype == SC_F16 && y_dtype == SC_F32) ::sc::launch(sc::rmsnorm_kernel<__half, float>, M, threads, 0, stream, x, H, w, eps, y);
+  else if (x_dtype == SC_F16 && y_dtype == SC_F16) ::sc::launch(sc::rmsnorm_kernel<__half, __half>, M, threads, 0, stream, x, H, w, eps, y);
   else SC_REQUIRE(false, SC_ERR_ARG, "rmsnorm: dtype");
   return sc::check_launch("rmsnorm");
 }
@@ -204,10 +235,10 @@ int sc_silu_mul(const void* gate, const void* up, int in_dtype, size_t n, void* 
   if (n == 0) return SC_OK;
   SC_REQUIRE(gate && up && out, SC_ERR_ARG, "silu_mul: null pointer");
   const int blocks = (int)std::min<size_t>((n + 255) / 256, 8 * (size_t)sc::sm_count());
-  if (in_dtype == SC_F32 && out_dtype == SC_F32) sc::silu_mul_kernel<float, float><<<blocks, 256, 0, stream>>>(gate, up, n, out);
-  else if (in_dtype == SC_F32 && out_dtype == SC_F16) sc::silu_mul_kernel<float, __half><<<blocks, 256, 0, stream>>>(gate, up, n, out);
-  else if (in_dtype == SC_F16 && out_dtype == SC_F32) sc::silu_mul_kernel<__half, float><<<blocks, 256, 0, stream>>>(gate, up, n, out);
-  else if (in_dtype == SC_F16 && out_dtype == SC_F16) sc::silu_mul_kernel<__half, __half><<<blocks, 256, 0, stream>>>(gate, up, n, out);
+  if (in_dtype == SC_F32 && out_dtype == SC_F32) ::sc::launch(sc::silu_mul_kernel<float, float>, blocks, 256, 0, stream, gate, up, n, out);
+  else if (in_dtype == SC_F32 && out_dtype == SC_F16) ::sc::launch(sc::silu_mul_kernel<float, __half>, blocks, 256, 0, stream, gate, up, n, out);
+  else if (in_dtype == SC_F16 && out_dtype == SC_F32) ::sc::launch(sc::silu_mul_kernel<__half, float>, blocks, 256, 0, stream, gate, up, n, out);
+  else if (in_dtype == SC_F16 && out_dtype == SC_F16) ::sc::launch(sc::silu_mul_kernel<__half, __half>, blocks, 256, 0, stream, gate, up, n, out);
   else SC_REQUIRE(false, SC_ERR_ARG, "silu_mul: dtype");
   return sc::check_launch("silu_mul");
 }
@@ -241,10 +272,10 @@ int sc_argmax(const float* logits, int M, int N, int ldl, int index_offset, floa
   const int nch = (N + sc::AM_CHUNK - 1) / sc::AM_CHUNK;
   float* pv = (float*)workspace;
   int* pi = (int*)(pv + (size_t)M * nch);
-  sc::argmax_partial_kernel<<<dim3(nch, M), sc::AM_THREADS, 0, stream>>>(logits, N, ldl, pv, pi, nch);
+  ::sc::launch(sc::argmax_partial_kernel, dim3(nch, M), sc::AM_THREADS, 0, stream, logits, N, ldl, pv, pi, nch);
   int st = sc::check_launch("argmax_partial");
   if (st != SC_OK) return st;
-  sc::argmax_final_kernel<<<M, 32, 0, stream>>>(pv, pi, nch, index_offset, val, idx);
+  ::sc::launch(sc::argmax_final_kernel, M, 32, 0, stream, pv, pi, nch, index_offset, val, idx);
   return sc::check_launch("argmax_final");
 }
 
@@ -253,7 +284,7 @@ int sc_argmax_merge(const float* vals, const int32_t* idxs, int M, int world, in
   SC_REQUIRE(world >= 1, SC_ERR_SHAPE, "argmax_merge: world must be >= 1");
   if (M <= 0) return SC_OK;
   SC_REQUIRE(vals && idxs && token_out, SC_ERR_ARG, "argmax_merge: null pointer");
-  sc::argmax_merge_kernel<<<1, 256, 0, stream>>>(vals, idxs, M, world, token_out, pos, pos_advance);
+  ::sc::launch(sc::argmax_merge_kernel, 1, 256, 0, stream, vals, idxs, M, world, token_out, pos, pos_advance);
   return sc::check_launch("argmax_merge");
 }
 

@@ -193,6 +193,8 @@ __device__ __forceinline__ void epilogue(const QGemvParams& p, int split, bool a
 template <int BITS, int MT, int EPI, bool NORM, typename XT, typename YT>
 __global__ void __launch_bounds__(QG_THREADS)
 qgemv_kernel(const QGemvParams p) {
+  pdl_trigger();
+  pdl_wait();
   using TR = QTraits<BITS>;
   constexpr int NMMA = TR::NMMA;
   constexpr bool DUAL = (EPI == SC_EPI_SWIGLU);
@@ -492,8 +494,13 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_trigger();
 
   if (warp == TC_NCW) {
+    // The producer streams weights, scales and biases only -- data no kernel
+    // of the step writes -- so it starts before the predecessor kernel has
+    // finished (no pdl_wait here); the consumers' pdl_wait orders everything
+    // that touches activations.
     // ============================ producer ============================
     if (lane == 0) {
       uint32_t it = 0;
@@ -540,6 +547,7 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
 
   // ============================ consumers ============================
   const int g = lane >> 2, t = lane & 3;
+  pdl_wait();  // x (and the residual / output buffers) belong to the predecessor until here
   stage_x<BITS, NORM, XT>(p, xs, s_rms, kc0, kc1, tid, NC, 1);
 
   // Work items of a stage: NACC weight sets x nch chunks; warp w takes items
@@ -744,8 +752,410 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
   if (aborted && lane == 0) atomicExch(&g_qgemv_error, 1);
 }
 
+// ---------------------------------------------------------------------------
+// Factored decode kernel (M * NGC <= 4, the batch-1 decode case).
+//
+// Same TMA ring and producer as qgemv_tma_kernel, different arithmetic: the
+// weights are never rounded.  Per group,
+//     y += scale * sum_k q_k x_k  +  bias * sum_k x_k
+// with q_k the exact integer codes.  The A registers hold 1024 + q (one AND/OR
+// per pair of codes, no conversion arithmetic); the 1024 * sum(x) excess is
+// cancelled by starting the mma accumulator at -1024 * sum(x) for that
+// column.  x itself is split into an fp16 high part and an fp16 low part
+// (x - hi), carried in otherwise idle columns of the n8 mma tile, so the
+// products see x to ~22 bits.  Because the four k-lanes of an mma can hold
+// codes of different groups (lane t owns words 4t..4t+3 of a chunk), the B
+// tile gives every (batch row m, part, group) its own column: column
+// n = (m * 2 + part) * NGC + group, NGC = groups per chunk (1, 2 or 4).
+// A lane's B value is x where its words' group matches the column, else 0.
+//
+// Each consumer warp accumulates its chunks of a tile in registers, reduces
+// over its k-lanes, and adds the tile's 16 row sums into a shared-memory
+// slot with shared atomics; the warp that arrives last on the slot's counter
+// runs the epilogue.  No CTA-wide barrier sits in the streaming loop.
+constexpr int FX_NSLOT = TC_MAX_NST + 2;  // > ring depth: a warp is never a ring ahead of the slowest
+
+template <int BITS>
+__device__ __forceinline__ void unpack_off(uint32_t w, uint32_t (&a)[4]) {
+  // 1024 + code in each fp16 half (exact); 4-bit: (e0,e4) (e1,e5) (e2,e6) (e3,e7); 8-bit: (e0,e2) (e1,e3)
+  const uint32_t MAG = 0x64006400u;
+  if (BITS == 4) {
+    a[0] = (w & 0x000F000Fu) | MAG;
+    a[1] = ((w >> 4) & 0x000F000Fu) | MAG;
+    a[2] = ((w >> 8) & 0x000F000Fu) | MAG;
+    a[3] = ((w >> 12) & 0x000F000Fu) | MAG;
+  } else {
+    a[0] = (w & 0x00FF00FFu) | MAG;
+    a[1] = ((w >> 8) & 0x00FF00FFu) | MAG;
+    a[2] = a[3] = 0u;
+  }
+}
+
+// Bytes of staged x per chunk: [m][part][q][t] 16-byte B-fragment units, then
+// a 64-byte table {xoff(2t), xoff(2t+1), xsum(2t), xsum(2t+1)} per lane t.
+__host__ __device__ constexpr int fx_chunk_bytes(int bits, int M) { return M * 2 * (bits == 4 ? 4 : 2) * 64 + 64; }
+
+// Stage normalised x for chunks [kc0, kc1) (consumer threads only).
+template <int BITS, int NGC, bool NORM, typename XT>
+__device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* xsb, float (*s_part)[4], float* s_rms,
+                                           int kc0, int kc1, int tid, int nthreads, int bar_id) {
+  using TR = QTraits<BITS>;
+  constexpr int XQ = TR::NMMA / 2;
+  constexpr int VPL = TR::KPC / 32;        // values per lane of a chunk (4-bit: 4, 8-bit: 2)
+  constexpr int GV = TR::KPC / NGC;        // values of one column-group inside a chunk
+  constexpr int GL = GV / VPL;             // lanes covering one column-group
+  const int M = p.M;
+  const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
+  const int CB = fx_chunk_bytes(BITS, M);
+  if (NORM) {
+    float ss[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = tid; k < p.K; k += nthreads)
+#pragma unroll
+      for (int m = 0; m < 4; ++m)
+        if (m < M) {
+          const float v = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
+          ss[m] = fmaf(v, v, ss[m]);
+        }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
+      if (lane == 0) s_part[warp][m] = ss[m];
+    }
+    named_bar_sync(bar_id, nthreads);
+    if (tid < M) {
+      float s = 0.f;
+      for (int w = 0; w < nwarps; ++w) s += s_part[w][tid];
+      s_rms[tid] = sqrtf(s / (float)p.K + p.eps);
+    }
+    named_bar_sync(bar_id, nthreads);
+  }
+  // one warp per (chunk, m): lane l owns the VPL consecutive values starting at
+  // chunk value l * VPL, i.e. word (l * VPL) / PF, elements from (l * VPL) % PF
+  const int nkc = kc1 - kc0;
+  for (int task = warp; task < nkc * M; task += nwarps) {
+    const int cl = task / M, m = task % M;
+    const int kbase = (kc0 + cl) * TR::KPC + lane * VPL;
+    float sh = 0.f, sl = 0.f, sx = 0.f;  // this lane's sums of hi, lo and exact x
+    unsigned char* cb = xsb + (size_t)cl * CB;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int k = kbase + v;
+      float x = 0.f;
+      if (k < p.K) {
+        x = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
+        if (NORM) x = (x / s_rms[m]) * __half2float(__ushort_as_half(p.norm_w[k]));
+      }
+      const __half hi = __float2half_rn(x);
+      const __half lo = __float2half_rn(x - __half2float(hi));
+      sh += __half2float(hi);
+      sl += __half2float(lo);
+      sx += x;
+      const int cv = lane * VPL + v;         // value index inside the chunk
+      const int wi = cv / TR::PF, e = cv % TR::PF;
+      const int t = wi >> 2, j = wi & 3;
+      int i, h;
+      if (BITS == 4) {
+        i = 2 * j + ((e >> 1) & 1);
+        h = 2 * (e & 1) + (e >> 2);
+      } else {
+        i = j;
+        h = 2 * (e & 1) + (e >> 1);
+      }
+      const int q = i >> 1, r = i & 1;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const int unit = ((m * 2 + part) * XQ + q) * 4 + t;
+        reinterpret_cast<__half*>(cb + unit * 16)[r * 4 + h] = part ? lo : hi;
+      }
+    }
+    // reduce over the lanes of one column-group
+#pragma unroll
+    for (int o = 1; o < GL; o <<= 1) {
+      sh += __shfl_xor_sync(0xffffffffu, sh, o);
+      sl += __shfl_xor_sync(0xffffffffu, sl, o);
+      sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    }
+    if (lane % GL == 0) {
+      const int grp = lane / GL;  // column-group within the chunk
+      float* tab = reinterpret_cast<float*>(cb + M * 2 * XQ * 64);
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const int col = (m * 2 + part) * NGC + grp;  // < 8
+        const int tl = col >> 1, hl = col & 1;
+        tab[tl * 4 + hl] = -1024.f * (part ? sl : sh);
+        tab[tl * 4 + 2 + hl] = part ? 0.f : sx;
+      }
+    }
+  }
+  // columns no (m, part, group) maps to: zero table entries
+  for (int idx = tid; idx < nkc * 8; idx += nthreads) {
+    const int cl = idx >> 3, col = idx & 7;
+    if (col >= M * 2 * NGC) {
+      float* tab = reinterpret_cast<float*>(xsb + (size_t)cl * CB + M * 2 * XQ * 64);
+      tab[(col >> 1) * 4 + (col & 1)] = 0.f;
+      tab[(col >> 1) * 4 + 2 + (col & 1)] = 0.f;
+    }
+  }
+  named_bar_sync(bar_id, nthreads);
+}
+
+template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ TmaMaps maps) {
+  using TR = QTraits<BITS>;
+  constexpr int NMMA = TR::NMMA;
+  constexpr int XQ = NMMA / 2;
+  constexpr bool DUAL = (EPI == SC_EPI_SWIGLU);
+  constexpr int NACC = DUAL ? 2 : 1;
+  constexpr int NC = TC_NCW * 32;
+
+  extern __shared__ __align__(128) unsigned char smem_tma[];
+  __shared__ int s_abort;
+  __shared__ float s_part[TC_NCW][4];
+  __shared__ float s_rms[4];
+  __shared__ int s_cnt[FX_NSLOT];
+  __shared__ float s_slot[FX_NSLOT][NACC][16][4];
+
+  const int M = p.M;
+  const int split = blockIdx.y;
+  const int kc0 = split * p.chunks_per_split;
+  const int KW = p.K / TR::PF;
+  const int KC = (KW + 15) / 16;
+  const int kc1 = min(KC, kc0 + p.chunks_per_split);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  unsigned char* sbase = smem_tma + ((1024 - (smem_u32(smem_tma) & 1023)) & 1023);
+  unsigned char* xsb = sbase;
+  unsigned char* ring = sbase + geo.ring_off;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + geo.bar_off);
+  uint64_t* empty = full + TC_MAX_NST;
+
+  for (int i = tid; i < FX_NSLOT * NACC * 16 * 4; i += blockDim.x) (&s_slot[0][0][0][0])[i] = 0.f;
+  if (tid < FX_NSLOT) s_cnt[tid] = 0;
+  if (tid == 0) {
+    for (int s = 0; s < geo.nst; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], TC_NCW);
+    }
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == TC_NCW) {
+    // producer: weights / scales / biases only, so no pdl_wait (see pdl_wait)
+    if (lane == 0) {
+      uint32_t it = 0;
+      const uint32_t tx = (uint32_t)(NACC * (geo.wset_bytes + 2 * 16 * geo.ngs * 2));
+      for (int tile = blockIdx.x; tile < p.tiles && !s_abort; tile += gridDim.x) {
+        const int n0 = tile * 16;
+        int sbase_row = 0;
+        const int sidx = DUAL ? 0 : tile_segment(p, n0, &sbase_row);
+        const int row0 = n0 - sbase_row;
+        for (int kcs = kc0; kcs < kc1; kcs += geo.cps) {
+          const int s = it % geo.nst;
+          const uint32_t ph = (it / geo.nst) & 1;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1, &s_abort, TC_WAIT_NS)) break;
+          unsigned char* st = ring + (size_t)s * geo.stage_bytes;
+          const int blk0 = kcs / 2;
+          const int g0 = kcs * TR::KPC / p.group;
+          mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+          for (int a = 0; a < NACC; ++a) {
+            const int mi = DUAL ? a : sidx;
+            unsigned char* wd = st + a * geo.wset_bytes;
+            if (geo.row_swz)
+              tma_load_3d(wd, &maps.w[mi], 0, row0, blk0, &full[s]);
+            else
+              tma_load_3d(wd, &maps.w[mi], 0, blk0, row0, &full[s]);
+            unsigned char* sd = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
+            tma_load_2d(sd, &maps.s[mi], g0, row0, &full[s]);
+            tma_load_2d(sd + geo.sset_bytes, &maps.b[mi], g0, row0, &full[s]);
+          }
+          ++it;
+        }
+      }
+      if (s_abort) {
+        for (uint32_t k = (it > (uint32_t)geo.nst ? it - geo.nst : 0); k < it; ++k) {
+          int dummy = 0;
+          mbar_wait_bounded(&full[k % geo.nst], (k / geo.nst) & 1, (volatile int*)&dummy, TC_WAIT_NS / 4);
+        }
+        atomicExch(&g_qgemv_error, 1);
+      }
+    }
+    return;
+  }
+
+  // ============================ consumers ============================
+  const int g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  stage_x_fx<BITS, NGC, NORM, XT>(p, xsb, s_part, s_rms, kc0, kc1, tid, NC, 1);
+  const int CB = fx_chunk_bytes(BITS, M);
+
+  // B-fragment column of this lane and whether its words' group feeds it
+  const int bm = g / (2 * NGC), bpart = (g / NGC) & 1, bgrp = g % NGC;
+  const bool bact = bm < M && bgrp == ((t * NGC) >> 2);
+  const int bx_off = (((bm * 2 + bpart) * XQ) * 4 + t) * 16;
+  // C-fragment columns 2t, 2t+1: their groups
+  const int grpA = (2 * t) % NGC, grpB = (2 * t + 1) % NGC;
+
+  const int pr0 = tile_row(g);
+  const int lgG = p.lg_group;
+  const int w_r8 = geo.row_swz ? 1024 : 8 * geo.nblk * 128;
+  const int s_r8 = 16 * geo.ngs;
+  auto woff = [&](int c) -> int {
+    const int u = ((c & 1) << 2) | t;
+    if (geo.row_swz) return (c >> 1) * 2048 + pr0 * 128 + ((u ^ (pr0 & 7)) << 4);
+    const int l = pr0 * geo.nblk + (c >> 1);
+    return l * 128 + ((u ^ (l & 7)) << 4);
+  };
+  auto soff = [&](int c, int grp) -> int {  // scale-box byte offset of (row pr0, group grp of chunk c)
+    const int gi = ((c * TR::KPC) >> lgG) + grp;
+    const int lo = pr0 * geo.ngs * 2 + gi * 2;
+    return lo ^ (((lo >> 7) & geo.s_swz) << 4);
+  };
+  auto ld_sb = [&](const unsigned char* sp, float& va, float& vb) {
+    if (NGC >= 2) {
+      const __half2 h = *reinterpret_cast<const __half2*>(sp);
+      va = __low2float(h);
+      vb = __high2float(h);
+    } else {
+      va = vb = __half2float(*reinterpret_cast<const __half*>(sp));
+    }
+  };
+
+  float acc[NACC][4];
+  int s = 0;
+  uint32_t ph = 0;
+  int ti = 0;  // tile iteration (slot = ti % FX_NSLOT)
+  bool aborted = false;
+  for (int tile = blockIdx.x; tile < p.tiles && !aborted; tile += gridDim.x, ++ti) {
+    const int n0 = tile * 16;
+#pragma unroll
+    for (int a = 0; a < NACC; ++a)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
+
+    for (int kcs = kc0; kcs < kc1; kcs += geo.cps) {
+      if (!mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS)) { aborted = true; break; }
+      const unsigned char* st = ring + (size_t)s * geo.stage_bytes;
+      const int nch = min(kc1 - kcs, geo.cps);
+      for (int c = warp; c < nch; c += TC_NCW) {
+        const unsigned char* cb = xsb + (size_t)(kcs - kc0 + c) * CB;
+        uint32_t bfr[NMMA][2];
+        if (bact) {
+#pragma unroll
+          for (int q = 0; q < XQ; ++q) {
+            const uint4 v = *reinterpret_cast<const uint4*>(cb + bx_off + q * 64);
+            bfr[2 * q][0] = v.x;
+            bfr[2 * q][1] = v.y;
+            bfr[2 * q + 1][0] = v.z;
+            bfr[2 * q + 1][1] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < NMMA; ++i) bfr[i][0] = bfr[i][1] = 0u;
+        }
+        const float4 tb = *reinterpret_cast<const float4*>(cb + M * 2 * XQ * 64 + t * 16);
+        const int wo = woff(c);
+        const int so = soff(c, grpA);
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          const unsigned char* wst = st + a * geo.wset_bytes;
+          const uint4 w0 = *reinterpret_cast<const uint4*>(wst + wo);
+          const uint4 w1 = *reinterpret_cast<const uint4*>(wst + wo + w_r8);
+          const unsigned char* sst = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
+          float sA0, sB0, sA1, sB1, bA0, bB0, bA1, bB1;
+          ld_sb(sst + so, sA0, sB0);
+          ld_sb(sst + so + s_r8, sA1, sB1);
+          ld_sb(sst + geo.sset_bytes + so, bA0, bB0);
+          ld_sb(sst + geo.sset_bytes + so + s_r8, bA1, bB1);
+          const uint32_t r0[4] = {w0.x, w0.y, w0.z, w0.w};
+          const uint32_t r1[4] = {w1.x, w1.y, w1.z, w1.w};
+          float ca[4] = {tb.x, tb.y, tb.x, tb.y};
+          float cz[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t A0[4], A1[4];
+            unpack_off<BITS>(r0[j], A0);
+            unpack_off<BITS>(r1[j], A1);
+            if (BITS == 4) {
+              mma_16816(ca, A0[0], A1[0], A0[1], A1[1], bfr[2 * j][0], bfr[2 * j][1]);
+              mma_16816(cz, A0[2], A1[2], A0[3], A1[3], bfr[2 * j + 1][0], bfr[2 * j + 1][1]);
+            } else {
+              if (j & 1)
+                mma_16816(cz, A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
+              else
+                mma_16816(ca, A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
+            }
+          }
+          acc[a][0] = fmaf(sA0, ca[0] + cz[0], fmaf(bA0, tb.z, acc[a][0]));
+          acc[a][1] = fmaf(sB0, ca[1] + cz[1], fmaf(bB0, tb.w, acc[a][1]));
+          acc[a][2] = fmaf(sA1, ca[2] + cz[2], fmaf(bA1, tb.z, acc[a][2]));
+          acc[a][3] = fmaf(sB1, ca[3] + cz[3], fmaf(bB1, tb.w, acc[a][3]));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == geo.nst) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+    if (aborted) break;
+
+    // ---- tile done for this warp: reduce over k-lanes, add into the slot
+    const int slot = ti % FX_NSLOT;
+    const int m = t / NGC;
+#pragma unroll
+    for (int a = 0; a < NACC; ++a) {
+      float vg = acc[a][0] + acc[a][1], vg8 = acc[a][2] + acc[a][3];
+#pragma unroll
+      for (int o = 1; o < NGC; o <<= 1) {
+        vg += __shfl_xor_sync(0xffffffffu, vg, o);
+        vg8 += __shfl_xor_sync(0xffffffffu, vg8, o);
+      }
+      if ((t % NGC) == 0 && m < M) {
+        atomicAdd(&s_slot[slot][a][pr0][m], vg);
+        atomicAdd(&s_slot[slot][a][pr0 + 8][m], vg8);
+      }
+    }
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&s_cnt[slot], 1) == TC_NCW - 1;
+      if (last) __threadfence_block();
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      for (int e = lane; e < 16 * M; e += 32) {
+        const int rl = e / M, mm = e % M;
+        const int row = n0 + rl;
+        float v[2];
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          v[a] = s_slot[slot][a][rl][mm];
+          s_slot[slot][a][rl][mm] = 0.f;
+        }
+        if (row < p.N) epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, mm, v);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        s_cnt[slot] = 0;
+        __threadfence_block();
+      }
+    }
+  }
+  if (aborted && lane == 0) atomicExch(&g_qgemv_error, 1);
+}
+
 template <int EPI, typename YT>
 __global__ void qgemv_splitk_reduce(const QGemvParams p) {
+  pdl_trigger();
+  pdl_wait();
   const size_t total = (size_t)p.M * p.N;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
     const int col = (int)(e / p.N), row = (int)(e % p.N);
@@ -823,8 +1233,9 @@ static int tma_unit(int bits, int group) { return std::max(2, 8 * group / kpc_of
 // SC_QGEMV_CPS chunks per stage, SC_QGEMV_NST ring depth, SC_QGEMV_PATH=ldg
 // forces the direct-load kernel.
 struct Knobs {
-  int cps = 0, nst = 0, ldg = 0;
+  int cps = 0, nst = 0, ldg = 0, nofx = 0;
   Knobs() {
+    if (const char* e = getenv("SC_QGEMV_FX")) nofx = e[0] == '0';
     if (const char* e = getenv("SC_QGEMV_CPS")) cps = atoi(e);
     if (const char* e = getenv("SC_QGEMV_NST")) nst = atoi(e);
     if (const char* e = getenv("SC_QGEMV_PATH")) ldg = strcmp(e, "ldg") == 0;
@@ -835,7 +1246,18 @@ static const Knobs& knobs() {
   return k;
 }
 
-static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int MT) {
+// Shared-memory budget for the staged x slice of the factored kernel (hi/lo
+// parts and per-chunk sums: 576 B per 128 values at 4 bits, M = 1).
+constexpr size_t TC_XS_BUDGET_FX = 80 * 1024;
+
+static int ngc_of(int bits, int group) { return std::max(1, kpc_of(bits) / group); }
+
+// The factored kernel serves passes whose B tile fits one n8 mma: M * NGC <= 4.
+static bool fx_eligible(int M, int bits, int group) { return M * ngc_of(bits, group) <= 4; }
+
+static size_t xs_fx_bytes(int bits, int M, int nkc) { return (size_t)nkc * fx_chunk_bytes(bits, M); }
+
+static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int MT, bool fx) {
   TmaPlan tp{};
   tp.ok = false;
   const int KW = K / (32 / bits);
@@ -848,7 +1270,9 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   sp.tiles = (N + 15) / 16;
   int splits = 1;
   auto cps_of = [&](int s) { return round_up((KC + s - 1) / s, U); };
-  while (cps_of(splits) > U && xs_bytes(bits, M, cps_of(splits)) > TC_XS_BUDGET) ++splits;
+  auto xsb = [&](int nkc) { return fx ? xs_fx_bytes(bits, M, nkc) : xs_bytes(bits, M, nkc); };
+  const size_t xs_budget = fx ? TC_XS_BUDGET_FX : TC_XS_BUDGET;
+  while (cps_of(splits) > U && xsb(cps_of(splits)) > xs_budget) ++splits;
   // more splits when there are too few tiles for the SMs (keep >= TC_NCW chunks per split)
   while (sp.tiles * splits < nsm && cps_of(splits + 1) >= TC_NCW) ++splits;
   sp.chunks_per_split = cps_of(splits);
@@ -868,8 +1292,8 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   geo.wset_bytes = 16 * geo.nblk * 128;
   geo.sset_bytes = round_up(16 * geo.ngs * 2, 1024);
   geo.stage_bytes = nacc * (geo.wset_bytes + 2 * geo.sset_bytes);
-  geo.ring_off = round_up((int)xs_bytes(bits, M, sp.chunks_per_split), 1024);
-  const int red_bytes = 2 * TC_NCW * 32 * nacc * MT * 4 * 4;  // double-buffered by tile
+  geo.ring_off = round_up((int)xsb(sp.chunks_per_split), 1024);
+  const int red_bytes = fx ? 0 : 2 * TC_NCW * 32 * nacc * MT * 4 * 4;  // double-buffered by tile
   const size_t fixed = geo.ring_off + red_bytes + 2 * TC_MAX_NST * 8 + 1024 /* base alignment */ + 64;
   if (fixed >= TC_SMEM_BUDGET) return tp;
   int nst = (int)std::min<size_t>(TC_MAX_NST, (TC_SMEM_BUDGET - fixed) / geo.stage_bytes);
@@ -974,7 +1398,7 @@ static int launch_qgemv(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, 
       configured = true;
     }
     dim3 grid(tp->grid_x, p.splits);
-    kern<<<grid, TC_THREADS, tp->smem, stream>>>(p, tp->geo, *maps);
+    ::sc::launch(kern, grid, TC_THREADS, tp->smem, stream, p, tp->geo, *maps);
     int st = check_launch("qgemv_tma");
     if (st != SC_OK || p.splits == 1 || tp->geo.atomic_out) return st;
   } else {
@@ -990,14 +1414,62 @@ static int launch_qgemv(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, 
     const int slots = std::max(1, std::max(nb, 1) * sm_count() / p.splits);
     const int per_cta = (p.tiles + slots - 1) / slots;
     dim3 grid((p.tiles + per_cta - 1) / per_cta, p.splits);
-    kern<<<grid, QG_THREADS, smem, stream>>>(p);
+    ::sc::launch(kern, grid, QG_THREADS, smem, stream, p);
     int st = check_launch("qgemv");
     if (st != SC_OK || p.splits == 1) return st;
   }
   const size_t total = (size_t)p.M * p.N;
   const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)4 * sm_count());
-  qgemv_splitk_reduce<EPI, YT><<<rb, 256, 0, stream>>>(p);
+  ::sc::launch(qgemv_splitk_reduce<EPI, YT>, rb, 256, 0, stream, p);
   return check_launch("qgemv_splitk_reduce");
+}
+
+template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
+static int launch_qgemv_fx(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, cudaStream_t stream) {
+  auto kern = qgemv_fx_kernel<BITS, NGC, EPI, NORM, XT, YT>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM_BUDGET);
+    configured = true;
+  }
+  dim3 grid(tp->grid_x, p.splits);
+  ::sc::launch(kern, grid, TC_THREADS, tp->smem, stream, p, tp->geo, *maps);
+  int st = check_launch("qgemv_fx");
+  if (st != SC_OK || p.splits == 1 || tp->geo.atomic_out) return st;
+  const size_t total = (size_t)p.M * p.N;
+  const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)4 * sm_count());
+  ::sc::launch(qgemv_splitk_reduce<EPI, YT>, rb, 256, 0, stream, p);
+  return check_launch("qgemv_splitk_reduce");
+}
+
+template <int BITS, int NGC, int EPI, bool NORM>
+static int dispatch_fx_types(QGemvParams& p, const TmaPlan* tp, const TmaMaps* mp, int x_dtype, int y_dtype,
+                             cudaStream_t stream) {
+  if (x_dtype == SC_F16 && y_dtype == SC_F16) return launch_qgemv_fx<BITS, NGC, EPI, NORM, __half, __half>(p, tp, mp, stream);
+  if (x_dtype == SC_F16 && y_dtype == SC_F32) return launch_qgemv_fx<BITS, NGC, EPI, NORM, __half, float>(p, tp, mp, stream);
+  if (x_dtype == SC_F32 && y_dtype == SC_F16) return launch_qgemv_fx<BITS, NGC, EPI, NORM, float, __half>(p, tp, mp, stream);
+  if (x_dtype == SC_F32 && y_dtype == SC_F32) return launch_qgemv_fx<BITS, NGC, EPI, NORM, float, float>(p, tp, mp, stream);
+  set_error("qlinear: unsupported dtype pair x=%d y=%d", x_dtype, y_dtype);
+  return SC_ERR_ARG;
+}
+
+template <int BITS, int NGC>
+static int dispatch_fx(QGemvParams& p, const TmaPlan* tp, const TmaMaps* mp, int epi, int x_dtype, int y_dtype,
+                       cudaStream_t stream) {
+  const bool n = p.norm_w != nullptr;
+  switch (epi) {
+    case SC_EPI_STORE:
+      return n ? dispatch_fx_types<BITS, NGC, SC_EPI_STORE, true>(p, tp, mp, x_dtype, y_dtype, stream)
+               : dispatch_fx_types<BITS, NGC, SC_EPI_STORE, false>(p, tp, mp, x_dtype, y_dtype, stream);
+    case SC_EPI_RESIDUAL:
+      return n ? dispatch_fx_types<BITS, NGC, SC_EPI_RESIDUAL, true>(p, tp, mp, x_dtype, y_dtype, stream)
+               : dispatch_fx_types<BITS, NGC, SC_EPI_RESIDUAL, false>(p, tp, mp, x_dtype, y_dtype, stream);
+    case SC_EPI_SWIGLU:
+      return n ? dispatch_fx_types<BITS, NGC, SC_EPI_SWIGLU, true>(p, tp, mp, x_dtype, y_dtype, stream)
+               : dispatch_fx_types<BITS, NGC, SC_EPI_SWIGLU, false>(p, tp, mp, x_dtype, y_dtype, stream);
+  }
+  set_error("qlinear: unknown epilogue %d", epi);
+  return SC_ERR_ARG;
 }
 
 template <int BITS, int MT, int EPI, bool NORM>
@@ -1034,6 +1506,7 @@ static int dispatch_epi(QGemvParams& p, const TmaPlan* tp, const TmaMaps* mp, in
 // the workspace-size query so both always agree.
 struct PassPlan {
   bool tma;
+  bool fx;  // factored kernel (exact weights); implies tma
   TmaPlan tp;
   SplitPlan sp;
 };
@@ -1044,7 +1517,12 @@ static PassPlan plan_pass(int mb, int K, int N, int bits, int group, int nacc, b
   PassPlan pp{};
   const int MT = mb > 8 ? 2 : 1;
   if (tma_ok && !knobs().ldg) {
-    pp.tp = plan_tma(mb, K, N, bits, group, nacc, MT);
+    pp.fx = fx_eligible(mb, bits, group) && !knobs().nofx;
+    pp.tp = plan_tma(mb, K, N, bits, group, nacc, MT, pp.fx);
+    if (!pp.tp.ok && pp.fx) {
+      pp.fx = false;
+      pp.tp = plan_tma(mb, K, N, bits, group, nacc, MT, false);
+    }
     if (pp.tp.ok) {
       pp.tma = true;
       pp.sp = pp.tp.sp;
@@ -1053,6 +1531,7 @@ static PassPlan plan_pass(int mb, int K, int N, int bits, int group, int nacc, b
     }
   }
   pp.tma = false;
+  pp.fx = false;
   pp.sp = plan_splits(mb, K, N, bits, nacc);
   return pp;
 }
@@ -1142,7 +1621,16 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
       p.partial = nullptr;
     }
     int st;
-    if (bits == 4)
+    if (tp && pp.fx) {
+      const int ngc = ngc_of(bits, group);
+      if (bits == 4)
+        st = ngc == 1 ? dispatch_fx<4, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
+             : ngc == 2 ? dispatch_fx<4, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
+                        : dispatch_fx<4, 4>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
+      else
+        st = ngc == 1 ? dispatch_fx<8, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
+                      : dispatch_fx<8, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
+    } else if (bits == 4)
       st = mb > 8 ? dispatch_epi<4, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
                   : dispatch_epi<4, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
     else

@@ -4,8 +4,10 @@ Tolerances:
 * unpack / dequantize / embedding gather / quantize: bit-exact;
 * quantized matmul: relative L2 <= 1e-3 against the oracle's exact-dequant
   float64 product, and <= 2e-5 against the
-  float64 product of the fp16-dequantized weights the kernel is defined on
-  (checks the in-register dequant is exact and accumulation is fp32);
+  float64 product the kernel is defined on: exact weights for the decode
+  kernel (scale * sum(q x) + bias * sum(x) with x split into fp16 high and
+  low parts), fp16-dequantized weights for the batched kernel (checks the
+  in-register arithmetic is exact and accumulation is fp32);
 * attention: relative L2 <= 1e-4 against the float64 oracle.
 """
 
@@ -40,6 +42,23 @@ def ref16(x, wq, s, b, group, bits):
     return np.asarray(x, np.float64) @ qa.dequantize(wq, s, b, group, bits).astype(np.float64).T
 
 
+def ref_exact(x, wq, s, b, group, bits):
+    return np.asarray(x, np.float64) @ qa.dequantize_exact(wq, s, b, group, bits).T
+
+
+def assert_kernel_close(y, refs, tol):
+    """The decode kernel (M * groups-per-chunk <= 4) keeps the weights exact;
+    the batched kernel rounds them once to fp16.  ``refs`` holds the float64
+    product for each definition; the output must match one of them."""
+    y = np.asarray(y)
+    rows = y.reshape(-1, y.shape[-1])
+    refs = [np.asarray(r).reshape(rows.shape) for r in refs]
+    # a pass of up to 16 rows runs one kernel, so each row matches one definition
+    for m in range(rows.shape[0]):
+        errs = [rel_l2(rows[m], r[m]) for r in refs]
+        assert min(errs) <= tol, (m, errs)
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("group", [32, 64, 128])
 @pytest.mark.parametrize("M,K,N", [(1, 256, 80), (3, 512, 48), (8, 1024, 200), (9, 384, 33),
@@ -54,7 +73,7 @@ def test_qlinear_matches_oracle(cuda, rng, bits, group, M, K, N):
     y = y.cpu().numpy()
     ref = qa.quantized_matmul(x, wq, s, b, group, bits)
     assert rel_l2(y, ref) <= 1e-3
-    assert rel_l2(y, ref16(x, wq, s, b, group, bits)) <= 2e-5
+    assert_kernel_close(y, [ref, ref16(x, wq, s, b, group, bits)], 2e-5)
     assert L.load().sc_qgemv_device_error(1) == 0
 
 
@@ -70,8 +89,8 @@ def test_qlinear_edge_shapes(cuda, rng, bits):
         bias = (rng.standard_normal(N) * 0.1).astype(np.float16)
         y = ops.qlinear(to_dev(x, cuda), to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda), group, bits,
                         bias=to_dev(bias, cuda), out_dtype=torch.float32).cpu().numpy()
-        ref = ref16(x, wq, s, b, group, bits) + bias
-        assert rel_l2(y, ref) <= 2e-5, (M, K, N)
+        assert_kernel_close(y, [ref16(x, wq, s, b, group, bits) + bias, ref_exact(x, wq, s, b, group, bits) + bias],
+                            2e-5)
 
 
 def test_qlinear_rejects_bad_shapes(cuda, rng):
@@ -93,11 +112,13 @@ def test_qlinear_fused_segments_norm_residual(cuda, rng, bits, rows):
     nw = (1.0 + 0.1 * rng.standard_normal(K)).astype(np.float16)
     y = ops.qlinear_fused(to_dev(h, cuda), [tuple(to_dev(a, cuda) for a in sg) for sg in segs], group, bits,
                           norm_weight=to_dev(nw, cuda), eps=eps).cpu().numpy()
-    xn = otp.rmsnorm(h, nw, eps).astype(np.float16).astype(np.float64)
+    xn64 = otp.rmsnorm(h, nw, eps)
+    xn = xn64.astype(np.float16).astype(np.float64)
     ref = np.concatenate([xn @ qa.dequantize(*sg, group, bits).astype(np.float64).T for sg in segs], axis=1)
-    # the kernel normalises in fp32 before rounding x to fp16; the float64
-    # reference can land one fp16 ulp away on a few elements
-    assert rel_l2(y, ref) <= 1e-4
+    ref_x = np.concatenate([ref_exact(xn64, *sg, group, bits) for sg in segs], axis=1)
+    # the batched kernel normalises in fp32 before rounding x to fp16; the
+    # float64 reference can land one fp16 ulp away on a few elements
+    assert_kernel_close(y, [ref, ref_x], 1e-4)
     # residual epilogue, in place
     for K2 in (256, 4096):
         wq, s, b = make_q(rng, K, K2, bits, group)
@@ -106,8 +127,8 @@ def test_qlinear_fused_segments_norm_residual(cuda, rng, bits, rows):
         r_dev = to_dev(res, cuda)
         ops.qlinear_fused(to_dev(x, cuda), [(to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda))], group, bits,
                           epilogue=L.SC_EPI_RESIDUAL, residual=r_dev, out=r_dev)
-        ref = res + ref16(x, wq, s, b, group, bits)
-        assert rel_l2(r_dev.cpu().numpy(), ref) <= 2e-5
+        assert_kernel_close(r_dev.cpu().numpy(), [res + ref16(x, wq, s, b, group, bits),
+                                                  res + ref_exact(x, wq, s, b, group, bits)], 2e-5)
 
 
 @pytest.mark.parametrize("M", [1, 4, 12])
@@ -119,9 +140,28 @@ def test_qlinear_swiglu(cuda, rng, M, K, F):
     x = rng.standard_normal((M, K)).astype(np.float16)
     y = ops.qlinear_fused(to_dev(x, cuda), [tuple(to_dev(a, cuda) for a in g), tuple(to_dev(a, cuda) for a in u)],
                           group, bits, epilogue=L.SC_EPI_SWIGLU, out_dtype=torch.float32).cpu().numpy()
-    xg = ref16(x, *g, group, bits)
-    xu = ref16(x, *u, group, bits)
-    assert rel_l2(y, otp.silu(xg) * xu) <= 5e-5
+    refs = [otp.silu(f(x, *g, group, bits)) * f(x, *u, group, bits) for f in (ref16, ref_exact)]
+    assert_kernel_close(y, refs, 5e-5)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("group", [32, 64, 128])
+@pytest.mark.parametrize("M", [1, 2, 4])
+def test_decode_kernel_exact_weights_fp32_input(cuda, rng, bits, group, M):
+    """fp32 activations through the decode kernel: weights exact and x carried
+    as fp16 high + low parts, so the product matches float64 to ~1e-5
+    (the fp16-rounding kernel would sit near 1e-4)."""
+    K, N = 4096, 1024
+    ngc = max(1, (128 if bits == 4 else 64) // group)
+    if M * ngc > 4:
+        pytest.skip("batched kernel")
+    wq, s, b = make_q(rng, N, K, bits, group)
+    x = (rng.standard_normal((M, K)) * np.exp(rng.uniform(-3, 3, size=(M, K)))).astype(np.float32)
+    y = ops.qlinear_fused(to_dev(x, cuda), [(to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda))], group, bits,
+                          out_dtype=torch.float32).cpu().numpy()
+    ref = ref_exact(x, wq, s, b, group, bits)
+    assert rel_l2(y, ref) <= 2e-5
+    assert L.load().sc_qgemv_device_error(1) == 0
 
 
 @pytest.mark.parametrize("bits", [4, 8])
