@@ -758,10 +758,11 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
 // Same TMA ring and producer as qgemv_tma_kernel, different arithmetic: the
 // weights are never rounded.  Per group,
 //     y += scale * sum_k q_k x_k  +  bias * sum_k x_k
-// with q_k the exact integer codes.  The A registers hold 1024 + q (one AND/OR
-// per pair of codes, no conversion arithmetic); the 1024 * sum(x) excess is
-// cancelled by starting the mma accumulator at -1024 * sum(x) for that
-// column.  x itself is split into an fp16 high part and an fp16 low part
+// with q_k the exact integer codes.  The A registers hold 1024 + q, or
+// 1024 + 16 q for the odd nibbles of a 4-bit word whose x slots then carry
+// x / 16 (one AND/OR per pair of codes, no conversion arithmetic); the excess
+// 1024 * sum(B) is cancelled by starting the mma accumulator at -1024 * sum(B)
+// for that column.  x itself is split into an fp16 high part and an fp16 low part
 // (x - hi), carried in otherwise idle columns of the n8 mma tile, so the
 // products see x to ~22 bits.  Because the four k-lanes of an mma can hold
 // codes of different groups (lane t owns words 4t..4t+3 of a chunk), the B
@@ -777,13 +778,15 @@ constexpr int FX_NSLOT = TC_MAX_NST + 2;  // > ring depth: a warp is never a rin
 
 template <int BITS>
 __device__ __forceinline__ void unpack_off(uint32_t w, uint32_t (&a)[4]) {
-  // 1024 + code in each fp16 half (exact); 4-bit: (e0,e4) (e1,e5) (e2,e6) (e3,e7); 8-bit: (e0,e2) (e1,e3)
+  // fp16 pairs, exact: 4-bit (e0,e4) = 1024 + q, (e1,e5) = 1024 + 16 q, (e2,e6) = 1024 + q,
+  // (e3,e7) = 1024 + 16 q -- the x slots of the odd codes hold x / 16; 8-bit (e0,e2) (e1,e3) = 1024 + q
   const uint32_t MAG = 0x64006400u;
   if (BITS == 4) {
+    const uint32_t w8 = w >> 8;
     a[0] = (w & 0x000F000Fu) | MAG;
-    a[1] = ((w >> 4) & 0x000F000Fu) | MAG;
-    a[2] = ((w >> 8) & 0x000F000Fu) | MAG;
-    a[3] = ((w >> 12) & 0x000F000Fu) | MAG;
+    a[1] = (w & 0x00F000F0u) | MAG;
+    a[2] = (w8 & 0x000F000Fu) | MAG;
+    a[3] = (w8 & 0x00F000F0u) | MAG;
   } else {
     a[0] = (w & 0x00FF00FFu) | MAG;
     a[1] = ((w >> 8) & 0x00FF00FFu) | MAG;
@@ -846,13 +849,17 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
         x = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
         if (NORM) x = (x / s_rms[m]) * __half2float(__ushort_as_half(p.norm_w[k]));
       }
-      const __half hi = __float2half_rn(x);
-      const __half lo = __float2half_rn(x - __half2float(hi));
+      const int cv = lane * VPL + v;         // value index inside the chunk
+      const int wi = cv / TR::PF, e = cv % TR::PF;
+      __half hi = __float2half_rn(x);
+      __half lo = __float2half_rn(x - __half2float(hi));
+      if (BITS == 4 && (e & 1)) {            // odd codes arrive as 16 q: their x slots carry x / 16
+        hi = __hmul(hi, __float2half_rn(0.0625f));
+        lo = __hmul(lo, __float2half_rn(0.0625f));
+      }
       sh += __half2float(hi);
       sl += __half2float(lo);
       sx += x;
-      const int cv = lane * VPL + v;         // value index inside the chunk
-      const int wi = cv / TR::PF, e = cv % TR::PF;
       const int t = wi >> 2, j = wi & 3;
       int i, h;
       if (BITS == 4) {
@@ -899,6 +906,15 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
   }
   named_bar_sync(bar_id, nthreads);
 }
+
+// Shared-memory operands of one chunk for the factored kernel.
+template <int NMMA, int NACC>
+struct FxChunk {
+  uint32_t bfr[NMMA][2];  // B fragments (x high / low parts by column)
+  float4 tb;              // {xoff(2t), xoff(2t+1), xsum(2t), xsum(2t+1)}
+  uint4 w0[NACC], w1[NACC];
+  float sb[NACC][8];      // scales then biases: (row g, grp A), (g, B), (g+8, A), (g+8, B)
+};
 
 template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -1027,6 +1043,66 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   };
 
   float acc[NACC][4];
+  const unsigned char* st = nullptr;  // current stage
+  const unsigned char* xst = nullptr; // staged x of the stage's first chunk
+  auto fx_load = [&](FxChunk<NMMA, NACC>& d, int c) {
+    const unsigned char* cb = xst + (size_t)c * CB;
+    if (bact) {
+#pragma unroll
+      for (int q = 0; q < XQ; ++q) {
+        const uint4 v = *reinterpret_cast<const uint4*>(cb + bx_off + q * 64);
+        d.bfr[2 * q][0] = v.x;
+        d.bfr[2 * q][1] = v.y;
+        d.bfr[2 * q + 1][0] = v.z;
+        d.bfr[2 * q + 1][1] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NMMA; ++i) d.bfr[i][0] = d.bfr[i][1] = 0u;
+    }
+    d.tb = *reinterpret_cast<const float4*>(cb + M * 2 * XQ * 64 + t * 16);
+    const int wo = woff(c);
+    const int so = soff(c, grpA);
+#pragma unroll
+    for (int a = 0; a < NACC; ++a) {
+      const unsigned char* wst = st + a * geo.wset_bytes;
+      d.w0[a] = *reinterpret_cast<const uint4*>(wst + wo);
+      d.w1[a] = *reinterpret_cast<const uint4*>(wst + wo + w_r8);
+      const unsigned char* sst = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
+      ld_sb(sst + so, d.sb[a][0], d.sb[a][1]);
+      ld_sb(sst + so + s_r8, d.sb[a][2], d.sb[a][3]);
+      ld_sb(sst + geo.sset_bytes + so, d.sb[a][4], d.sb[a][5]);
+      ld_sb(sst + geo.sset_bytes + so + s_r8, d.sb[a][6], d.sb[a][7]);
+    }
+  };
+  auto fx_compute = [&](const FxChunk<NMMA, NACC>& d) {
+#pragma unroll
+    for (int a = 0; a < NACC; ++a) {
+      const uint32_t r0[4] = {d.w0[a].x, d.w0[a].y, d.w0[a].z, d.w0[a].w};
+      const uint32_t r1[4] = {d.w1[a].x, d.w1[a].y, d.w1[a].z, d.w1[a].w};
+      float ca[4] = {d.tb.x, d.tb.y, d.tb.x, d.tb.y};
+      float cz[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t A0[4], A1[4];
+        unpack_off<BITS>(r0[j], A0);
+        unpack_off<BITS>(r1[j], A1);
+        if (BITS == 4) {
+          mma_16816(ca, A0[0], A1[0], A0[1], A1[1], d.bfr[2 * j][0], d.bfr[2 * j][1]);
+          mma_16816(cz, A0[2], A1[2], A0[3], A1[3], d.bfr[2 * j + 1][0], d.bfr[2 * j + 1][1]);
+        } else if (j & 1) {
+          mma_16816(cz, A0[0], A1[0], A0[1], A1[1], d.bfr[j][0], d.bfr[j][1]);
+        } else {
+          mma_16816(ca, A0[0], A1[0], A0[1], A1[1], d.bfr[j][0], d.bfr[j][1]);
+        }
+      }
+      const float* sb = d.sb[a];  // sA0 sB0 sA1 sB1 bA0 bB0 bA1 bB1
+      acc[a][0] = fmaf(sb[0], ca[0] + cz[0], fmaf(sb[4], d.tb.z, acc[a][0]));
+      acc[a][1] = fmaf(sb[1], ca[1] + cz[1], fmaf(sb[5], d.tb.w, acc[a][1]));
+      acc[a][2] = fmaf(sb[2], ca[2] + cz[2], fmaf(sb[6], d.tb.z, acc[a][2]));
+      acc[a][3] = fmaf(sb[3], ca[3] + cz[3], fmaf(sb[7], d.tb.w, acc[a][3]));
+    }
+  };
   int s = 0;
   uint32_t ph = 0;
   int ti = 0;  // tile iteration (slot = ti % FX_NSLOT)
@@ -1040,61 +1116,27 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
 
     for (int kcs = kc0; kcs < kc1; kcs += geo.cps) {
       if (!mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS)) { aborted = true; break; }
-      const unsigned char* st = ring + (size_t)s * geo.stage_bytes;
+      st = ring + (size_t)s * geo.stage_bytes;
+      xst = xsb + (size_t)(kcs - kc0) * CB;
       const int nch = min(kc1 - kcs, geo.cps);
-      for (int c = warp; c < nch; c += TC_NCW) {
-        const unsigned char* cb = xsb + (size_t)(kcs - kc0 + c) * CB;
-        uint32_t bfr[NMMA][2];
-        if (bact) {
-#pragma unroll
-          for (int q = 0; q < XQ; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4*>(cb + bx_off + q * 64);
-            bfr[2 * q][0] = v.x;
-            bfr[2 * q][1] = v.y;
-            bfr[2 * q + 1][0] = v.z;
-            bfr[2 * q + 1][1] = v.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < NMMA; ++i) bfr[i][0] = bfr[i][1] = 0u;
+      // a warp's chunks of the stage; single-set tiles take two at a time
+      // (every shared load of both issued before either is computed); the
+      // SwiGLU pair already has two independent weight sets per chunk and
+      // would exceed the 96-register budget of 17 warps per SM with two
+      if (DUAL) {
+        for (int c = warp; c < nch; c += TC_NCW) {
+          FxChunk<NMMA, NACC> da;
+          fx_load(da, c);
+          fx_compute(da);
         }
-        const float4 tb = *reinterpret_cast<const float4*>(cb + M * 2 * XQ * 64 + t * 16);
-        const int wo = woff(c);
-        const int so = soff(c, grpA);
-#pragma unroll
-        for (int a = 0; a < NACC; ++a) {
-          const unsigned char* wst = st + a * geo.wset_bytes;
-          const uint4 w0 = *reinterpret_cast<const uint4*>(wst + wo);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(wst + wo + w_r8);
-          const unsigned char* sst = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
-          float sA0, sB0, sA1, sB1, bA0, bB0, bA1, bB1;
-          ld_sb(sst + so, sA0, sB0);
-          ld_sb(sst + so + s_r8, sA1, sB1);
-          ld_sb(sst + geo.sset_bytes + so, bA0, bB0);
-          ld_sb(sst + geo.sset_bytes + so + s_r8, bA1, bB1);
-          const uint32_t r0[4] = {w0.x, w0.y, w0.z, w0.w};
-          const uint32_t r1[4] = {w1.x, w1.y, w1.z, w1.w};
-          float ca[4] = {tb.x, tb.y, tb.x, tb.y};
-          float cz[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t A0[4], A1[4];
-            unpack_off<BITS>(r0[j], A0);
-            unpack_off<BITS>(r1[j], A1);
-            if (BITS == 4) {
-              mma_16816(ca, A0[0], A1[0], A0[1], A1[1], bfr[2 * j][0], bfr[2 * j][1]);
-              mma_16816(cz, A0[2], A1[2], A0[3], A1[3], bfr[2 * j + 1][0], bfr[2 * j + 1][1]);
-            } else {
-              if (j & 1)
-                mma_16816(cz, A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
-              else
-                mma_16816(ca, A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
-            }
-          }
-          acc[a][0] = fmaf(sA0, ca[0] + cz[0], fmaf(bA0, tb.z, acc[a][0]));
-          acc[a][1] = fmaf(sB0, ca[1] + cz[1], fmaf(bB0, tb.w, acc[a][1]));
-          acc[a][2] = fmaf(sA1, ca[2] + cz[2], fmaf(bA1, tb.z, acc[a][2]));
-          acc[a][3] = fmaf(sB1, ca[3] + cz[3], fmaf(bB1, tb.w, acc[a][3]));
+      } else {
+        for (int c = warp; c < nch; c += 2 * TC_NCW) {
+          const bool two = c + TC_NCW < nch;
+          FxChunk<NMMA, NACC> da, db;
+          fx_load(da, c);
+          if (two) fx_load(db, c + TC_NCW);
+          fx_compute(da);
+          if (two) fx_compute(db);
         }
       }
       __syncwarp();

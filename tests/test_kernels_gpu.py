@@ -149,8 +149,10 @@ def test_qlinear_swiglu(cuda, rng, M, K, F):
 @pytest.mark.parametrize("M", [1, 2, 4])
 def test_decode_kernel_exact_weights_fp32_input(cuda, rng, bits, group, M):
     """fp32 activations through the decode kernel: weights exact and x carried
-    as fp16 high + low parts, so the product matches float64 to ~1e-5
-    (the fp16-rounding kernel would sit near 1e-4)."""
+    as fp16 high + low parts, so the product matches float64 to a few 1e-5
+    (the fp16-rounding kernel sits near 1e-4).  The bound allows for the low
+    parts of small |x| landing in the fp16 subnormal range, most of all in
+    the x/16 slots of odd 4-bit codes; |x| here spans e^-3 .. e^3."""
     K, N = 4096, 1024
     ngc = max(1, (128 if bits == 4 else 64) // group)
     if M * ngc > 4:
@@ -160,7 +162,7 @@ def test_decode_kernel_exact_weights_fp32_input(cuda, rng, bits, group, M):
     y = ops.qlinear_fused(to_dev(x, cuda), [(to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda))], group, bits,
                           out_dtype=torch.float32).cpu().numpy()
     ref = ref_exact(x, wq, s, b, group, bits)
-    assert rel_l2(y, ref) <= 2e-5
+    assert rel_l2(y, ref) <= 5e-5
     assert L.load().sc_qgemv_device_error(1) == 0
 
 
