@@ -83,6 +83,20 @@ int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx,
                void* y, int y_dtype, int ldy,
                void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* sc_qlinear without a caller workspace: its split-K scratch is a fixed
+ * 4 MiB array the library allocates statically on each device.  No
+ * counterpart in the reference.  For callers that cannot allocate on the
+ * call path (an FFI binding with no device allocator of its own; a serving
+ * loop whose HBM is fully reserved).  Shapes whose workspace bound
+ * (sc_qlinear_workspace_bytes) exceeds 4 MiB are refused with
+ * SC_ERR_WORKSPACE before any launch.  The first call on a device looks the
+ * scratch up; make it before any stream capture.  One scratch per device:
+ * calls overlapping in time on one device race. */
+int sc_qlinear_noalloc(const void* x, int x_dtype, int M, int K, int ldx,
+                       const uint32_t* wq, const uint16_t* scales, const uint16_t* biases,
+                       int N, int group_size, int bits, const uint16_t* bias,
+                       void* y, int y_dtype, int ldy, cudaStream_t stream);
+
 /* Device-side error word of the quantized-linear kernels: nonzero after a
  * kernel gave up on a bounded wait (it then stops without touching the
  * output).  Synchronises with the device; reset != 0 clears it.  No

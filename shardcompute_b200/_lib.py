@@ -34,6 +34,7 @@ SIGNATURES = {
     "sc_last_error": (C.c_char_p, []),
     "sc_launch_count": (C.c_ulonglong, []),
     "sc_qlinear_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "sc_qlinear_noalloc": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp]),
     "sc_qgemv_device_error": (_i, [_i]),
     "sc_qlinear": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "sc_qlinear_fused": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp, _i,

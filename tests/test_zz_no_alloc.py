@@ -1,0 +1,78 @@
+"""sc_qlinear_noalloc: the quantized linear with its split-K scratch in a
+static device array.  Compared, through the C ABI, with sc_qlinear (caller
+workspace) on two calls in a row, and checked to refuse a shape whose
+scratch bound exceeds the static array before launching anything.  Named to
+be collected last: it must pass both alone and after the other GPU tests."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mlx_affine as qa
+from shardcompute_b200 import _lib as L
+from shardcompute_b200 import ops
+from tests.conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+SCRATCH = 4 << 20
+
+
+def _dev(a, cuda):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return torch.from_numpy(a).to(cuda)
+
+
+def _noalloc(x, wq, s, b, group, bits, y):
+    lib = L.load()
+    M, K = x.shape
+    N = wq.shape[0]
+    return lib.sc_qlinear_noalloc(x.data_ptr(), ops._dt(x), M, K, K, wq.data_ptr(), s.data_ptr(), b.data_ptr(), N,
+                                  group, bits, None, y.data_ptr(), ops._dt(y), N,
+                                  torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("M,K,N,bits,group", [(1, 14336, 1024, 4, 64), (1, 4096, 6144, 4, 64),
+                                              (3, 4096, 1024, 8, 32), (1, 256, 80, 4, 32)])
+def test_noalloc_matches_workspace_entry_point(cuda, M, K, N, bits, group):
+    rng = np.random.default_rng(7)
+    wq, s, b = qa.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float16), group, bits)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    xd, wd, sd, bd = _dev(x, cuda), _dev(wq, cuda), _dev(s, cuda), _dev(b, cuda)
+    ref = ops.qlinear(xd, wd, sd, bd, group, bits, out_dtype=torch.float32).cpu().numpy()
+    exact = qa.quantized_matmul(x, wq, s, b, group, bits)
+    for _ in range(2):  # two calls in a row reuse the same static scratch
+        y = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+        st = _noalloc(xd, wd, sd, bd, group, bits, y)
+        assert st == L.SC_OK, L.load().sc_last_error()
+        got = y.cpu().numpy()
+        assert rel_l2(got, ref) <= 2e-5
+        assert rel_l2(got, exact) <= 1e-3
+    assert L.load().sc_qgemv_device_error(1) == 0
+
+
+def test_noalloc_uses_the_scratch_for_split_k(cuda):
+    # the first shape above plans split-K partials, so the static scratch is exercised
+    assert 0 < L.load().sc_qlinear_workspace_bytes(1, 14336, 1024, 4) <= SCRATCH
+
+
+def test_noalloc_refuses_oversize_before_launch(cuda):
+    M, K, N, bits, group = 16, 14336, 14336, 4, 64
+    need = L.load().sc_qlinear_workspace_bytes(M, K, N, bits)
+    assert need > SCRATCH
+    # real, correctly sized buffers: nothing may be launched, but nothing could go out of bounds either
+    wq = torch.zeros(N, K * bits // 32, dtype=torch.int32, device=cuda)
+    s = torch.zeros(N, K // group, dtype=torch.float16, device=cuda)
+    b = torch.zeros_like(s)
+    x = torch.zeros(M, K, dtype=torch.float16, device=cuda)
+    y = torch.full((M, N), 7.0, dtype=torch.float32, device=cuda)
+    st = _noalloc(x, wq, s, b, group, bits, y)
+    assert st == L.SC_ERR_WORKSPACE
+    msg = L.load().sc_last_error().decode()
+    assert "static scratch" in msg and str(need) in msg
+    torch.cuda.synchronize()
+    assert bool((y == 7.0).all())
