@@ -121,6 +121,15 @@ int sc_qlinear_fused(const void* x, int x_dtype, int M, int K, int ldx,
                      void* y, int y_dtype, int ldy, const float* residual, int ldr,
                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* Prefetch up to 12 device regions into L2 (at most max_bytes in total, 0 =
+ * no cap) without waiting for them.  The decode step issues it right after a
+ * GEMV for the next GEMV's weights, so HBM keeps streaming through kernel
+ * boundaries and the attention kernels in between.  Region starts are
+ * rounded up to 16 bytes.  No reference counterpart (the reference streams
+ * weights through MLX with no prefetch). */
+int sc_l2_prefetch(const void* const* ptrs, const size_t* bytes, int n, size_t max_bytes,
+                   cudaStream_t stream);
+
 /* ------------------------------------------------------------------ K3 --
  * Vocab-split embedding gather.  Replaces QuantizedParallelEmbedding.forward
  * before its all-reduce (parallel/embedding.py:322-356): local = id - v0,
@@ -162,12 +171,29 @@ int sc_rope_append(const float* qkv, int B, int S, int Hq, int Hkv, int hd,
 /* Split-KV GQA flash-decode over the preallocated cache.  Replaces
  * parallel/attention.py:436-466 (GQA repeat, q.k^T*scale, causal mask,
  * softmax, @v).  Query s of sequence b sees keys [0, min(*pos + s, Lmax-1)].
- *   q: fp32 [B*S, Hq*hd]; out: fp16 or fp32 [B*S, Hq*hd]. */
+ *   q: fp32 [B*S, Hq*hd]; out: fp16 or fp32 [B*S, Hq*hd]; splits 1..64. */
 size_t sc_flash_decode_workspace_bytes(int B, int S, int Hq, int hd, int splits);
 int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
                     const int32_t* pos, int B, int S, int Hq, int Hkv, int hd, int Lmax,
                     float scale, int splits, void* out, int out_dtype,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Fused decode attention for one new token per sequence (S = 1): RoPE of
+ * q and of the new k at position *pos, append of k and v to the cache, and
+ * split-KV attention over positions [0, *pos] with the splits merged by the
+ * last CTA of each (sequence, kv head) -- the work of sc_rope_append +
+ * sc_flash_decode (parallel/attention.py:421-466) in one launch.
+ *   qkv: fp32 [B, (Hq + 2*Hkv) * hd]; caches fp16 [B, Hkv, Lmax, hd];
+ *   out: fp16 or fp32 [B, Hq*hd]; splits 1..64; workspace:
+ *   sc_attn_decode_workspace_bytes;
+ *   tickets: int32 [B*Hkv], zero before the first call and left zero by
+ *   every call (the split merge counts arrivals in it). */
+size_t sc_attn_decode_workspace_bytes(int B, int Hq, int hd, int splits);
+int sc_attn_decode(const float* qkv, int B, int Hq, int Hkv, int hd, const int32_t* pos,
+                   const float* cos_tab, const float* sin_tab, int max_pos,
+                   uint16_t* k_cache, uint16_t* v_cache, int Lmax, float scale, int splits,
+                   void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                   int32_t* tickets, cudaStream_t stream);
 
 /* ------------------------------------------------------------------ K5 --
  * RMSNorm (parallel/transformer.py:46-61): y = x / sqrt(mean(x^2)+eps) * w. */

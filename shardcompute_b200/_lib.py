@@ -36,6 +36,7 @@ SIGNATURES = {
     "sc_qlinear_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "sc_qlinear_noalloc": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp]),
     "sc_qgemv_device_error": (_i, [_i]),
+    "sc_l2_prefetch": (_i, [_pp, C.POINTER(_sz), _i, _sz, _vp]),
     "sc_qlinear": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "sc_qlinear_fused": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp, _i,
                               _vp, _i, _i, _vp, _i, _vp, _sz, _vp]),
@@ -46,6 +47,9 @@ SIGNATURES = {
     "sc_rope_append": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _vp]),
     "sc_flash_decode_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "sc_flash_decode": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _i, _vp, _sz, _vp]),
+    "sc_attn_decode_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "sc_attn_decode": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _f, _i, _vp, _i, _vp, _sz, _vp,
+                            _vp]),
     "sc_rmsnorm": (_i, [_vp, _i, _i, _i, _vp, _f, _vp, _i, _vp]),
     "sc_silu_mul": (_i, [_vp, _vp, _i, _sz, _vp, _i, _vp]),
     "sc_add": (_i, [_vp, _i, _vp, _i, _sz, _vp, _i, _vp]),

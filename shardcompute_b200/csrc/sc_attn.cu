@@ -181,24 +181,74 @@ flash_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc, 
   }
 }
 
+// Merge of split-KV partials {m, l, o[HD]} for G heads by one CTA of NT
+// threads.  The split maxima and sums are read once, in parallel, into shared
+// memory; each output element then sums its splits with AM_BATCH loads in
+// flight (the merge is a chain of L2 round trips, so fewer rounds is faster).
+constexpr int FD_MAX_SPLITS = 64;
+constexpr int AM_BATCH = 16;
+
+template <int HD, int G, int NT, typename OT>
+__device__ __forceinline__ void merge_partials(const float* pbase, size_t sstride, size_t gstride, int splits,
+                                               OT* outp, float (*s_w)[G], float (*s_l)[G], float* s_inv) {
+  for (int i = threadIdx.x; i < splits * G; i += NT) {
+    const int sp = i / G, g = i % G;
+    const float* pp = pbase + sp * sstride + g * gstride;
+    s_w[sp][g] = __ldcg(pp);
+    s_l[sp][g] = __ldcg(pp + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float M = -INFINITY;
+    for (int sp = 0; sp < splits; ++sp) M = fmaxf(M, s_w[sp][g]);
+    float Ls = 0.f;
+    for (int sp = 0; sp < splits; ++sp) {
+      const float w = s_w[sp][g] == -INFINITY ? 0.f : expf(s_w[sp][g] - M);
+      s_w[sp][g] = w;
+      Ls = fmaf(s_l[sp][g], w, Ls);
+    }
+    s_inv[g] = 1.f / Ls;
+  }
+  __syncthreads();
+  constexpr int EPT = (G * HD + NT - 1) / NT;  // outputs per thread
+  float acc[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) acc[j] = 0.f;
+  for (int s0 = 0; s0 < splits; s0 += AM_BATCH) {
+    float v[EPT][AM_BATCH];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const int e = threadIdx.x + j * NT;
+      const int g = e / HD, d = e % HD;
+#pragma unroll
+      for (int u = 0; u < AM_BATCH; ++u)
+        v[j][u] = (e < G * HD && s0 + u < splits) ? __ldcg(pbase + (s0 + u) * sstride + g * gstride + 2 + d) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const int e = threadIdx.x + j * NT;
+      const int g = (e < G * HD ? e : 0) / HD;
+#pragma unroll
+      for (int u = 0; u < AM_BATCH; ++u)
+        if (s0 + u < splits) acc[j] = fmaf(v[j][u], s_w[s0 + u][g], acc[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int e = threadIdx.x + j * NT;
+    if (e < G * HD) outp[(size_t)(e / HD) * HD + e % HD] = from_f32<OT>(acc[j] * s_inv[e / HD]);
+  }
+}
+
 template <int HD, typename OT>
 __global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq, int splits, OT* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
   const int qh = blockIdx.x, tok = blockIdx.y;
-  const float* pp = part + ((size_t)tok * Hq + qh) * splits * (HD + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, pp[s * (HD + 2)]);
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float Ls = 0.f, O = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const float* q = pp + s * (HD + 2);
-      const float w = q[0] == -INFINITY ? 0.f : expf(q[0] - M);
-      Ls = fmaf(q[1], w, Ls);
-      O = fmaf(q[2 + d], w, O);
-    }
-    out[(size_t)tok * Hq * HD + (size_t)qh * HD + d] = from_f32<OT>(O / Ls);
-  }
+  __shared__ float s_w[FD_MAX_SPLITS][1], s_l[FD_MAX_SPLITS][1], s_inv[1];
+  merge_partials<HD, 1, HD, OT>(part + ((size_t)tok * Hq + qh) * splits * (HD + 2), HD + 2, 0, splits,
+                                out + (size_t)tok * Hq * HD + (size_t)qh * HD, s_w, s_l, s_inv);
 }
 
 template <int HD, int G, typename OT>
@@ -223,6 +273,236 @@ static int dispatch_g(int G, const float* q, const __half* kc, const __half* vc,
     case 8: return launch_fd<HD, 8, OT>(q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, out, stream);
   }
   set_error("flash_decode: GQA group %d unsupported (1, 2, 4, 8)", G);
+  return SC_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------------------
+// Fused decode attention (one new token per sequence): RoPE of q and the new
+// k, append of k and v to the cache, split-KV online softmax over the cache,
+// and the merge of the splits -- one launch instead of three.
+//
+// grid (splits, Hkv, B), FD_WARPS warps.  Every CTA rotates its G query
+// heads itself (they are a few hundred floats); the CTA whose key range
+// holds the new position also rotates the new k, writes k and v into the
+// cache and uses those fp16 values for that key directly.  Each warp walks
+// its keys in batches of AD_BATCH warp-steps whose K/V loads are all issued
+// before any is used (the decode step is latency-bound, not bandwidth-bound,
+// at these sizes).  Partials go to the workspace; the last CTA of a
+// (sequence, kv head) -- an atomic ticket per pair -- merges the splits and
+// writes the output, then resets its ticket to zero for the next call.
+
+template <int HD>
+__device__ __forceinline__ void rope_pair(float x1, float x2, float c, float sn, float& o1, float& o2) {
+  // x*cos + rotate_half(x)*sin, rotate_half = [-x2, x1]; products unfused, as sc_rope_append
+  o1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, sn));
+  o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+}
+
+template <int HD, int G, typename OT>
+__global__ void __launch_bounds__(FD_WARPS * 32)
+attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ pos_ptr,
+                   const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int max_pos, int Hq,
+                   int Hkv, int Lmax, float scale, int splits, __half* __restrict__ kc, __half* __restrict__ vc,
+                   float* __restrict__ part, int* __restrict__ tickets, OT* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int LPK = HD / 8;    // lanes per key (8 halves each)
+  constexpr int KPS = 32 / LPK;  // keys per warp step
+  constexpr int HALF = HD / 2;
+  constexpr int AD_BATCH = G >= 8 ? 2 : 4;  // warp steps whose loads are in flight together
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / LPK, dl = lane % LPK;
+  const int d0 = dl * 8;
+
+  const int pos = *pos_ptr;
+  const bool append = pos >= 0 && pos < Lmax && pos < max_pos;
+  const int L = append ? pos + 1 : min(max(pos, 0), Lmax);
+  const int chunk = (L + splits - 1) / splits;
+  const int k_beg = split * chunk;
+  const int k_end = min(L, k_beg + chunk);
+  const bool owner = append && pos >= k_beg && pos < k_end;
+  const int width = (Hq + 2 * Hkv) * HD;
+  const float* src = qkv + (size_t)b * width;
+
+  __shared__ float s_q[G][HD];
+  __shared__ __align__(16) __half s_knew[HD], s_vnew[HD];
+  // rotated queries (and, for the owner, the new key / value)
+  for (int e = threadIdx.x; e < G * HALF; e += FD_WARPS * 32) {
+    const int g = e / HALF, d = e % HALF;
+    const float* qh = src + (size_t)(kvh * G + g) * HD;
+    float o1 = qh[d], o2 = qh[d + HALF];
+    if (append) rope_pair<HD>(qh[d], qh[d + HALF], cos_tab[(size_t)pos * HALF + d], sin_tab[(size_t)pos * HALF + d],
+                              o1, o2);
+    s_q[g][d] = o1;
+    s_q[g][d + HALF] = o2;
+  }
+  if (owner) {
+    const float* kh = src + (size_t)(Hq + kvh) * HD;
+    const float* vh = src + (size_t)(Hq + Hkv + kvh) * HD;
+    __half* kdst = kc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
+    __half* vdst = vc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
+    for (int d = threadIdx.x; d < HALF; d += FD_WARPS * 32) {
+      float o1, o2;
+      rope_pair<HD>(kh[d], kh[d + HALF], cos_tab[(size_t)pos * HALF + d], sin_tab[(size_t)pos * HALF + d], o1, o2);
+      const __half h1 = __float2half_rn(o1), h2 = __float2half_rn(o2);
+      s_knew[d] = h1;
+      s_knew[d + HALF] = h2;
+      kdst[d] = h1;
+      kdst[d + HALF] = h2;
+    }
+    for (int d = threadIdx.x; d < HD; d += FD_WARPS * 32) {
+      const __half hv = __float2half_rn(vh[d]);
+      s_vnew[d] = hv;
+      vdst[d] = hv;
+    }
+  }
+  __syncthreads();
+
+  float qr[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qr[g][i] = s_q[g][d0 + i];
+  float m[G], l[G], o[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
+  }
+  const __half* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  const __half* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  constexpr int STEP = FD_WARPS * KPS;  // keys per CTA step
+  for (int k0 = k_beg + warp * KPS; k0 < k_end; k0 += STEP * AD_BATCH) {
+    uint4 kv4[AD_BATCH], vv4[AD_BATCH];
+#pragma unroll
+    for (int j = 0; j < AD_BATCH; ++j) {
+      const int key = k0 + j * STEP + sub;
+      kv4[j] = vv4[j] = make_uint4(0, 0, 0, 0);
+      if (key < k_end) {
+        if (owner && key == pos) {
+          kv4[j] = *reinterpret_cast<const uint4*>(s_knew + d0);
+          vv4[j] = *reinterpret_cast<const uint4*>(s_vnew + d0);
+        } else {
+          kv4[j] = *reinterpret_cast<const uint4*>(kbase + (size_t)key * HD + d0);
+          vv4[j] = *reinterpret_cast<const uint4*>(vbase + (size_t)key * HD + d0);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < AD_BATCH; ++j) {
+      const int key = k0 + j * STEP + sub;
+      const bool valid = key < k_end;
+      float kf[8], vf[8];
+      const uint32_t kw[4] = {kv4[j].x, kv4[j].y, kv4[j].z, kv4[j].w};
+      const uint32_t vw[4] = {vv4[j].x, vv4[j].y, vv4[j].z, vv4[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __half22float2(u32_as_h2(kw[i]));
+        const float2 c = __half22float2(u32_as_h2(vw[i]));
+        kf[2 * i] = a.x; kf[2 * i + 1] = a.y;
+        vf[2 * i] = c.x; vf[2 * i + 1] = c.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot = fmaf(qr[g][i], kf[i], dot);
+#pragma unroll
+        for (int off = LPK / 2; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        if (valid) {
+          const float sc = dot * scale;
+          const float mn = fmaxf(m[g], sc);
+          const float corr = expf(m[g] - mn);
+          const float pr = expf(sc - mn);
+          l[g] = l[g] * corr + pr;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[g][i] = fmaf(pr, vf[i], o[g][i] * corr);
+          m[g] = mn;
+        }
+      }
+    }
+  }
+
+  // merge the lane groups of the CTA
+  __shared__ float sm_m[FD_WARPS * KPS][G], sm_l[FD_WARPS * KPS][G];
+  __shared__ float sm_o[FD_WARPS * KPS][G][HD];
+  const int grp = warp * KPS + sub;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (dl == 0) {
+      sm_m[grp][g] = m[g];
+      sm_l[grp][g] = l[g];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sm_o[grp][g][d0 + i] = o[g][i];
+  }
+  __syncthreads();
+  float* pbase = part + (((size_t)b * Hkv + kvh) * splits) * G * (HD + 2);
+  for (int e = threadIdx.x; e < G * HD; e += FD_WARPS * 32) {
+    const int g = e / HD, d = e % HD;
+    float M = -INFINITY;
+    for (int r = 0; r < FD_WARPS * KPS; ++r) M = fmaxf(M, sm_m[r][g]);
+    float Ls = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int r = 0; r < FD_WARPS * KPS; ++r) {
+        const float w = expf(sm_m[r][g] - M);
+        Ls = fmaf(sm_l[r][g], w, Ls);
+        O = fmaf(sm_o[r][g][d], w, O);
+      }
+    }
+    if (splits == 1) {
+      out[(size_t)b * Hq * HD + (size_t)(kvh * G + g) * HD + d] = from_f32<OT>(O / Ls);
+    } else {
+      float* pp = pbase + ((size_t)split * G + g) * (HD + 2);
+      pp[2 + d] = O;
+      if (d == 0) {
+        pp[0] = M;
+        pp[1] = Ls;
+      }
+    }
+  }
+  if (splits == 1) return;
+
+  // the last CTA of this (sequence, kv head) merges the splits
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int t = atomicAdd(&tickets[b * Hkv + kvh], 1);
+    s_last = (t == splits - 1);
+    if (s_last) __threadfence();
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __shared__ float s_w[FD_MAX_SPLITS][G], s_l[FD_MAX_SPLITS][G], s_inv[G];
+  merge_partials<HD, G, FD_WARPS * 32, OT>(pbase, (size_t)G * (HD + 2), HD + 2, splits,
+                                           out + (size_t)b * Hq * HD + (size_t)kvh * G * HD, s_w, s_l, s_inv);
+  if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
+}
+
+template <int HD, int G, typename OT>
+static int launch_ad(const float* qkv, const int32_t* pos, const float* cos_tab, const float* sin_tab, int max_pos,
+                     int B, int Hq, int Hkv, int Lmax, float scale, int splits, __half* kc, __half* vc, float* part,
+                     int* tickets, OT* out, cudaStream_t stream) {
+  ::sc::launch(attn_decode_kernel<HD, G, OT>, dim3(splits, Hkv, B), FD_WARPS * 32, 0, stream, qkv, pos, cos_tab,
+               sin_tab, max_pos, Hq, Hkv, Lmax, scale, splits, kc, vc, part, tickets, out);
+  return check_launch("attn_decode");
+}
+
+template <int HD, typename OT>
+static int dispatch_ad(int G, const float* qkv, const int32_t* pos, const float* cos_tab, const float* sin_tab,
+                       int max_pos, int B, int Hq, int Hkv, int Lmax, float scale, int splits, __half* kc, __half* vc,
+                       float* part, int* tickets, OT* out, cudaStream_t stream) {
+  switch (G) {
+    case 1: return launch_ad<HD, 1, OT>(qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc, part, tickets, out, stream);
+    case 2: return launch_ad<HD, 2, OT>(qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc, part, tickets, out, stream);
+    case 4: return launch_ad<HD, 4, OT>(qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc, part, tickets, out, stream);
+    case 8: return launch_ad<HD, 8, OT>(qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc, part, tickets, out, stream);
+  }
+  set_error("attn_decode: GQA group %d unsupported (1, 2, 4, 8)", G);
   return SC_ERR_UNSUPPORTED;
 }
 
@@ -252,7 +532,8 @@ int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_c
                     void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   SC_REQUIRE(hd == 64 || hd == 128, SC_ERR_UNSUPPORTED, "flash_decode: head_dim %d unsupported (64, 128)", hd);
   SC_REQUIRE(Hkv > 0 && Hq % Hkv == 0, SC_ERR_SHAPE, "flash_decode: Hq=%d not a multiple of Hkv=%d", Hq, Hkv);
-  SC_REQUIRE(B > 0 && S > 0 && splits >= 1 && splits <= 1024, SC_ERR_SHAPE, "flash_decode: bad B/S/splits");
+  SC_REQUIRE(B > 0 && S > 0 && splits >= 1 && splits <= sc::FD_MAX_SPLITS, SC_ERR_SHAPE,
+             "flash_decode: bad B/S/splits (splits 1..%d)", sc::FD_MAX_SPLITS);
   SC_REQUIRE(q && k_cache && v_cache && pos && out, SC_ERR_ARG, "flash_decode: null pointer");
   SC_REQUIRE(out_dtype == SC_F16 || out_dtype == SC_F32, SC_ERR_ARG, "flash_decode: out dtype");
   const size_t need = sc_flash_decode_workspace_bytes(B, S, Hq, hd, splits);
@@ -273,6 +554,44 @@ int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_c
     return sc::dispatch_g<64, __half>(G, q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, (__half*)out,
                                       stream);
   return sc::dispatch_g<64, float>(G, q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, (float*)out, stream);
+}
+
+size_t sc_attn_decode_workspace_bytes(int B, int Hq, int hd, int splits) {
+  if (splits <= 1) return 0;
+  return (size_t)B * Hq * splits * (hd + 2) * sizeof(float);
+}
+
+int sc_attn_decode(const float* qkv, int B, int Hq, int Hkv, int hd, const int32_t* pos, const float* cos_tab,
+                   const float* sin_tab, int max_pos, uint16_t* k_cache, uint16_t* v_cache, int Lmax, float scale,
+                   int splits, void* out, int out_dtype, void* workspace, size_t workspace_bytes, int32_t* tickets,
+                   cudaStream_t stream) {
+  SC_REQUIRE(hd == 64 || hd == 128, SC_ERR_UNSUPPORTED, "attn_decode: head_dim %d unsupported (64, 128)", hd);
+  SC_REQUIRE(Hkv > 0 && Hq % Hkv == 0, SC_ERR_SHAPE, "attn_decode: Hq=%d not a multiple of Hkv=%d", Hq, Hkv);
+  SC_REQUIRE(B > 0 && splits >= 1 && splits <= sc::FD_MAX_SPLITS && Lmax > 0, SC_ERR_SHAPE,
+             "attn_decode: bad B/splits/Lmax (splits 1..%d)", sc::FD_MAX_SPLITS);
+  SC_REQUIRE(qkv && pos && cos_tab && sin_tab && k_cache && v_cache && out, SC_ERR_ARG,
+             "attn_decode: null pointer");
+  SC_REQUIRE(out_dtype == SC_F16 || out_dtype == SC_F32, SC_ERR_ARG, "attn_decode: out dtype");
+  const size_t need = sc_attn_decode_workspace_bytes(B, Hq, hd, splits);
+  SC_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), SC_ERR_WORKSPACE,
+             "attn_decode: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
+  SC_REQUIRE(splits == 1 || tickets, SC_ERR_ARG, "attn_decode: split-KV needs the ticket array");
+  const int G = Hq / Hkv;
+  __half* kc = (__half*)k_cache;
+  __half* vc = (__half*)v_cache;
+  float* part = (float*)workspace;
+  if (hd == 128) {
+    if (out_dtype == SC_F16)
+      return sc::dispatch_ad<128, __half>(G, qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc,
+                                          vc, part, tickets, (__half*)out, stream);
+    return sc::dispatch_ad<128, float>(G, qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc,
+                                       part, tickets, (float*)out, stream);
+  }
+  if (out_dtype == SC_F16)
+    return sc::dispatch_ad<64, __half>(G, qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc,
+                                       part, tickets, (__half*)out, stream);
+  return sc::dispatch_ad<64, float>(G, qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc,
+                                    part, tickets, (float*)out, stream);
 }
 
 }  // extern "C"

@@ -414,6 +414,7 @@ struct TmaGeo {
   int atomic_out;   // split-K partials added atomically into y (in-place residual)
   int row_swz;      // 1: box lines ordered (block, row) with row-dependent swizzle
   int s_swz;        // scale-box swizzle mask: 0 none, 1 (32 B), 3 (64 B), 7 (128 B)
+  int pre_stages;   // factored kernel: stages the producer issues before x is staged
 };
 
 struct TmaMaps {
@@ -422,20 +423,30 @@ struct TmaMaps {
   CUtensorMap b[QG_MAX_SEG];
 };
 
+// Weights are read once per decode step (gigabytes apart), so their L2 lines
+// are marked evict-first: streaming them must not push out what is reused
+// (activations, KV, and weights prefetched ahead by sc_l2_prefetch).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            uint64_t* bar) {
+                                            uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
+                                            uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 
@@ -505,6 +516,7 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
     if (lane == 0) {
       uint32_t it = 0;
       const uint32_t tx = (uint32_t)(NACC * (geo.wset_bytes + 2 * 16 * geo.ngs * 2));
+      const uint64_t pol = l2_evict_first_policy();
       for (int tile = blockIdx.x; tile < p.tiles && !s_abort; tile += gridDim.x) {
         const int n0 = tile * 16;
         int sbase_row = 0;
@@ -523,12 +535,12 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
             const int mi = DUAL ? a : sidx;
             unsigned char* wd = st + a * geo.wset_bytes;
             if (geo.row_swz)
-              tma_load_3d(wd, &maps.w[mi], 0, row0, blk0, &full[s]);
+              tma_load_3d(wd, &maps.w[mi], 0, row0, blk0, &full[s], pol);
             else
-              tma_load_3d(wd, &maps.w[mi], 0, blk0, row0, &full[s]);
+              tma_load_3d(wd, &maps.w[mi], 0, blk0, row0, &full[s], pol);
             unsigned char* sd = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
-            tma_load_2d(sd, &maps.s[mi], g0, row0, &full[s]);
-            tma_load_2d(sd + geo.sset_bytes, &maps.b[mi], g0, row0, &full[s]);
+            tma_load_2d(sd, &maps.s[mi], g0, row0, &full[s], pol);
+            tma_load_2d(sd + geo.sset_bytes, &maps.b[mi], g0, row0, &full[s], pol);
           }
           ++it;
         }
@@ -810,15 +822,25 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
   const int M = p.M;
   const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
   const int CB = fx_chunk_bytes(BITS, M);
+  // Both passes issue all of a thread's global loads before using any: the
+  // prologue is a chain of L2 round trips, so the fewer, the better.
   if (NORM) {
+    constexpr int U = 8;
     float ss[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = tid; k < p.K; k += nthreads)
+    for (int k0 = tid; k0 < p.K; k0 += nthreads * U) {
+      float v[4][U];
 #pragma unroll
       for (int m = 0; m < 4; ++m)
-        if (m < M) {
-          const float v = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
-          ss[m] = fmaf(v, v, ss[m]);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int k = k0 + u * nthreads;
+          v[m][u] = (m < M && k < p.K) ? ld_x<XT>(p.x, (size_t)m * p.ldx + k) : 0.f;
         }
+#pragma unroll
+      for (int m = 0; m < 4; ++m)
+#pragma unroll
+        for (int u = 0; u < U; ++u) ss[m] = fmaf(v[m][u], v[m][u], ss[m]);
+    }
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
 #pragma unroll
@@ -833,65 +855,82 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
     }
     named_bar_sync(bar_id, nthreads);
   }
-  // one warp per (chunk, m): lane l owns the VPL consecutive values starting at
-  // chunk value l * VPL, i.e. word (l * VPL) / PF, elements from (l * VPL) % PF
+  // one warp per (chunk, m) task, TB tasks of a warp loaded together: lane l
+  // owns the VPL consecutive values starting at chunk value l * VPL, i.e.
+  // word (l * VPL) / PF, elements from (l * VPL) % PF
+  constexpr int TB = 4;
   const int nkc = kc1 - kc0;
-  for (int task = warp; task < nkc * M; task += nwarps) {
-    const int cl = task / M, m = task % M;
-    const int kbase = (kc0 + cl) * TR::KPC + lane * VPL;
-    float sh = 0.f, sl = 0.f, sx = 0.f;  // this lane's sums of hi, lo and exact x
-    unsigned char* cb = xsb + (size_t)cl * CB;
+  const int ntask = nkc * M;
+  for (int t0 = warp; t0 < ntask; t0 += nwarps * TB) {
+    float xv[TB][VPL], nw[TB][VPL];
 #pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-      const int k = kbase + v;
-      float x = 0.f;
-      if (k < p.K) {
-        x = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
-        if (NORM) x = (x / s_rms[m]) * __half2float(__ushort_as_half(p.norm_w[k]));
-      }
-      const int cv = lane * VPL + v;         // value index inside the chunk
-      const int wi = cv / TR::PF, e = cv % TR::PF;
-      __half hi = __float2half_rn(x);
-      __half lo = __float2half_rn(x - __half2float(hi));
-      if (BITS == 4 && (e & 1)) {            // odd codes arrive as 16 q: their x slots carry x / 16
-        hi = __hmul(hi, __float2half_rn(0.0625f));
-        lo = __hmul(lo, __float2half_rn(0.0625f));
-      }
-      sh += __half2float(hi);
-      sl += __half2float(lo);
-      sx += x;
-      const int t = wi >> 2, j = wi & 3;
-      int i, h;
-      if (BITS == 4) {
-        i = 2 * j + ((e >> 1) & 1);
-        h = 2 * (e & 1) + (e >> 2);
-      } else {
-        i = j;
-        h = 2 * (e & 1) + (e >> 1);
-      }
-      const int q = i >> 1, r = i & 1;
+    for (int b = 0; b < TB; ++b) {
+      const int task = t0 + b * nwarps;
+      const int cl = task / M, m = task % M;
+      const int kbase = (kc0 + cl) * TR::KPC + lane * VPL;
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        const int unit = ((m * 2 + part) * XQ + q) * 4 + t;
-        reinterpret_cast<__half*>(cb + unit * 16)[r * 4 + h] = part ? lo : hi;
+      for (int v = 0; v < VPL; ++v) {
+        const int k = kbase + v;
+        const bool ok = task < ntask && k < p.K;
+        xv[b][v] = ok ? ld_x<XT>(p.x, (size_t)m * p.ldx + k) : 0.f;
+        nw[b][v] = (NORM && ok) ? __half2float(__ushort_as_half(p.norm_w[k])) : 1.f;
       }
     }
-    // reduce over the lanes of one column-group
 #pragma unroll
-    for (int o = 1; o < GL; o <<= 1) {
-      sh += __shfl_xor_sync(0xffffffffu, sh, o);
-      sl += __shfl_xor_sync(0xffffffffu, sl, o);
-      sx += __shfl_xor_sync(0xffffffffu, sx, o);
-    }
-    if (lane % GL == 0) {
-      const int grp = lane / GL;  // column-group within the chunk
-      float* tab = reinterpret_cast<float*>(cb + M * 2 * XQ * 64);
+    for (int b = 0; b < TB; ++b) {
+      const int task = t0 + b * nwarps;
+      if (task >= ntask) break;
+      const int cl = task / M, m = task % M;
+      float sh = 0.f, sl = 0.f, sx = 0.f;  // this lane's sums of hi, lo and exact x
+      unsigned char* cb = xsb + (size_t)cl * CB;
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        const int col = (m * 2 + part) * NGC + grp;  // < 8
-        const int tl = col >> 1, hl = col & 1;
-        tab[tl * 4 + hl] = -1024.f * (part ? sl : sh);
-        tab[tl * 4 + 2 + hl] = part ? 0.f : sx;
+      for (int v = 0; v < VPL; ++v) {
+        float x = xv[b][v];
+        if (NORM) x = (x / s_rms[m]) * nw[b][v];
+        const int cv = lane * VPL + v;         // value index inside the chunk
+        const int wi = cv / TR::PF, e = cv % TR::PF;
+        __half hi = __float2half_rn(x);
+        __half lo = __float2half_rn(x - __half2float(hi));
+        if (BITS == 4 && (e & 1)) {            // odd codes arrive as 16 q: their x slots carry x / 16
+          hi = __hmul(hi, __float2half_rn(0.0625f));
+          lo = __hmul(lo, __float2half_rn(0.0625f));
+        }
+        sh += __half2float(hi);
+        sl += __half2float(lo);
+        sx += x;
+        const int t = wi >> 2, j = wi & 3;
+        int i, h;
+        if (BITS == 4) {
+          i = 2 * j + ((e >> 1) & 1);
+          h = 2 * (e & 1) + (e >> 2);
+        } else {
+          i = j;
+          h = 2 * (e & 1) + (e >> 1);
+        }
+        const int q = i >> 1, r = i & 1;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const int unit = ((m * 2 + part) * XQ + q) * 4 + t;
+          reinterpret_cast<__half*>(cb + unit * 16)[r * 4 + h] = part ? lo : hi;
+        }
+      }
+      // reduce over the lanes of one column-group
+#pragma unroll
+      for (int o = 1; o < GL; o <<= 1) {
+        sh += __shfl_xor_sync(0xffffffffu, sh, o);
+        sl += __shfl_xor_sync(0xffffffffu, sl, o);
+        sx += __shfl_xor_sync(0xffffffffu, sx, o);
+      }
+      if (lane % GL == 0) {
+        const int grp = lane / GL;  // column-group within the chunk
+        float* tab = reinterpret_cast<float*>(cb + M * 2 * XQ * 64);
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const int col = (m * 2 + part) * NGC + grp;  // < 8
+          const int tl = col >> 1, hl = col & 1;
+          tab[tl * 4 + hl] = -1024.f * (part ? sl : sh);
+          tab[tl * 4 + 2 + hl] = part ? 0.f : sx;
+        }
       }
     }
   }
@@ -932,6 +971,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   __shared__ float s_rms[4];
   __shared__ int s_cnt[FX_NSLOT];
   __shared__ float s_slot[FX_NSLOT][NACC][16][4];
+  __shared__ __align__(8) uint64_t s_xready;  // consumers have staged x (lets the producer run on)
 
   const int M = p.M;
   const int split = blockIdx.y;
@@ -954,6 +994,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], TC_NCW);
     }
+    mbar_init(&s_xready, 1);
     s_abort = 0;
     fence_mbar_init();
   }
@@ -965,6 +1006,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     if (lane == 0) {
       uint32_t it = 0;
       const uint32_t tx = (uint32_t)(NACC * (geo.wset_bytes + 2 * 16 * geo.ngs * 2));
+      const uint64_t pol = l2_evict_first_policy();
       for (int tile = blockIdx.x; tile < p.tiles && !s_abort; tile += gridDim.x) {
         const int n0 = tile * 16;
         int sbase_row = 0;
@@ -973,6 +1015,10 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
         for (int kcs = kc0; kcs < kc1; kcs += geo.cps) {
           const int s = it % geo.nst;
           const uint32_t ph = (it / geo.nst) & 1;
+          // the first pre_stages go out at once (before the predecessor
+          // kernel has even finished); the rest wait until x is staged, so
+          // the consumers' activation loads do not queue behind a full ring
+          if ((int)it == geo.pre_stages && !mbar_wait_bounded(&s_xready, 0, &s_abort, TC_WAIT_NS)) break;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1, &s_abort, TC_WAIT_NS)) break;
           unsigned char* st = ring + (size_t)s * geo.stage_bytes;
           const int blk0 = kcs / 2;
@@ -983,12 +1029,12 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
             const int mi = DUAL ? a : sidx;
             unsigned char* wd = st + a * geo.wset_bytes;
             if (geo.row_swz)
-              tma_load_3d(wd, &maps.w[mi], 0, row0, blk0, &full[s]);
+              tma_load_3d(wd, &maps.w[mi], 0, row0, blk0, &full[s], pol);
             else
-              tma_load_3d(wd, &maps.w[mi], 0, blk0, row0, &full[s]);
+              tma_load_3d(wd, &maps.w[mi], 0, blk0, row0, &full[s], pol);
             unsigned char* sd = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
-            tma_load_2d(sd, &maps.s[mi], g0, row0, &full[s]);
-            tma_load_2d(sd + geo.sset_bytes, &maps.b[mi], g0, row0, &full[s]);
+            tma_load_2d(sd, &maps.s[mi], g0, row0, &full[s], pol);
+            tma_load_2d(sd + geo.sset_bytes, &maps.b[mi], g0, row0, &full[s], pol);
           }
           ++it;
         }
@@ -1008,14 +1054,15 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   const int g = lane >> 2, t = lane & 3;
   pdl_wait();
   stage_x_fx<BITS, NGC, NORM, XT>(p, xsb, s_part, s_rms, kc0, kc1, tid, NC, 1);
+  if (tid == 0) mbar_arrive(&s_xready);
   const int CB = fx_chunk_bytes(BITS, M);
 
   // B-fragment column of this lane and whether its words' group feeds it
   const int bm = g / (2 * NGC), bpart = (g / NGC) & 1, bgrp = g % NGC;
   const bool bact = bm < M && bgrp == ((t * NGC) >> 2);
   const int bx_off = (((bm * 2 + bpart) * XQ) * 4 + t) * 16;
-  // C-fragment columns 2t, 2t+1: their groups
-  const int grpA = (2 * t) % NGC, grpB = (2 * t + 1) % NGC;
+  // C-fragment columns 2t, 2t+1 hold groups grpA and grpA + 1 (the same group when NGC == 1)
+  const int grpA = (2 * t) % NGC;
 
   const int pr0 = tile_row(g);
   const int lgG = p.lg_group;
@@ -1045,12 +1092,22 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   float acc[NACC][4];
   const unsigned char* st = nullptr;  // current stage
   const unsigned char* xst = nullptr; // staged x of the stage's first chunk
-  auto fx_load = [&](FxChunk<NMMA, NACC>& d, int c) {
-    const unsigned char* cb = xst + (size_t)c * CB;
+  // A warp's chunks in a stage are warp and warp + TC_NCW (cps <= 2 * TC_NCW),
+  // so every shared-memory offset of its loads is fixed for the kernel.
+  int fo_w[2], fo_s[2], fo_x[2], fo_t[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int c = warp + j * TC_NCW;
+    fo_w[j] = woff(c);
+    fo_s[j] = soff(c, grpA);
+    fo_x[j] = c * CB + bx_off;
+    fo_t[j] = c * CB + M * 2 * XQ * 64 + t * 16;
+  }
+  auto fx_load = [&](FxChunk<NMMA, NACC>& d, int j) {
     if (bact) {
 #pragma unroll
       for (int q = 0; q < XQ; ++q) {
-        const uint4 v = *reinterpret_cast<const uint4*>(cb + bx_off + q * 64);
+        const uint4 v = *reinterpret_cast<const uint4*>(xst + fo_x[j] + q * 64);
         d.bfr[2 * q][0] = v.x;
         d.bfr[2 * q][1] = v.y;
         d.bfr[2 * q + 1][0] = v.z;
@@ -1060,9 +1117,9 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
 #pragma unroll
       for (int i = 0; i < NMMA; ++i) d.bfr[i][0] = d.bfr[i][1] = 0u;
     }
-    d.tb = *reinterpret_cast<const float4*>(cb + M * 2 * XQ * 64 + t * 16);
-    const int wo = woff(c);
-    const int so = soff(c, grpA);
+    d.tb = *reinterpret_cast<const float4*>(xst + fo_t[j]);
+    const int wo = fo_w[j];
+    const int so = fo_s[j];
 #pragma unroll
     for (int a = 0; a < NACC; ++a) {
       const unsigned char* wst = st + a * geo.wset_bytes;
@@ -1124,20 +1181,20 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       // SwiGLU pair already has two independent weight sets per chunk and
       // would exceed the 96-register budget of 17 warps per SM with two
       if (DUAL) {
-        for (int c = warp; c < nch; c += TC_NCW) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if (warp + j * TC_NCW >= nch) break;
           FxChunk<NMMA, NACC> da;
-          fx_load(da, c);
+          fx_load(da, j);
           fx_compute(da);
         }
-      } else {
-        for (int c = warp; c < nch; c += 2 * TC_NCW) {
-          const bool two = c + TC_NCW < nch;
-          FxChunk<NMMA, NACC> da, db;
-          fx_load(da, c);
-          if (two) fx_load(db, c + TC_NCW);
-          fx_compute(da);
-          if (two) fx_compute(db);
-        }
+      } else if (warp < nch) {
+        const bool two = warp + TC_NCW < nch;
+        FxChunk<NMMA, NACC> da, db;
+        fx_load(da, 0);
+        if (two) fx_load(db, 1);
+        fx_compute(da);
+        if (two) fx_compute(db);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -1273,10 +1330,14 @@ static int tma_unit(int bits, int group) { return std::max(2, 8 * group / kpc_of
 
 // Tuning knobs read once from the environment (0 / unset = built-in choice):
 // SC_QGEMV_CPS chunks per stage, SC_QGEMV_NST ring depth, SC_QGEMV_PATH=ldg
-// forces the direct-load kernel.
+// forces the direct-load kernel, SC_QGEMV_FX=0 the batched kernel for decode,
+// SC_QGEMV_WMODE=0/1 the packed-word tensor-map layout (block-major /
+// row-swizzled; default: row-swizzled when the driver accepts it).
 struct Knobs {
-  int cps = 0, nst = 0, ldg = 0, nofx = 0;
+  int cps = 0, nst = 0, ldg = 0, nofx = 0, wmode = -1, pre = -1;
   Knobs() {
+    if (const char* e = getenv("SC_QGEMV_PRE")) pre = atoi(e);
+    if (const char* e = getenv("SC_QGEMV_WMODE")) wmode = atoi(e);
     if (const char* e = getenv("SC_QGEMV_FX")) nofx = e[0] == '0';
     if (const char* e = getenv("SC_QGEMV_CPS")) cps = atoi(e);
     if (const char* e = getenv("SC_QGEMV_NST")) nst = atoi(e);
@@ -1321,6 +1382,7 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   sp.splits = (KC + sp.chunks_per_split - 1) / sp.chunks_per_split;
   TmaGeo geo{};
   int cps = knobs().cps > 0 ? knobs().cps : TC_STAGE_CHUNKS / nacc;
+  cps = std::min(cps, 2 * TC_NCW);  // each consumer warp takes at most two chunks of a stage
   while (cps > U && cps * kpc_of(bits) / group * 2 > 128) cps /= 2;  // scale-box row <= 128 B (swizzle span)
   cps = std::min(cps, sp.chunks_per_split);
   cps = std::max(U, cps / U * U);
@@ -1342,6 +1404,7 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   if (knobs().nst > 0) nst = std::min(nst, knobs().nst);
   if (nst < 2) return tp;
   geo.nst = nst;
+  geo.pre_stages = knobs().pre >= 0 ? std::min(knobs().pre, nst) : nst;
   geo.red_off = geo.ring_off + nst * geo.stage_bytes;
   geo.bar_off = round_up(geo.red_off + red_bytes, 16);
   geo.atomic_out = 0;
@@ -1406,7 +1469,7 @@ static bool encode_smap(CUtensorMap* m, const uint16_t* s, int rows, int KG, int
 // Encode every segment's maps; prefers the row-swizzled layout, falls back to
 // the block-major one if the driver rejects non-monotonic strides.
 static bool encode_maps(const QGemvParams& p, int bits, int nacc, TmaGeo* geo, TmaMaps* maps) {
-  static int mode_ok = -1;  // -1 unknown, 1 row-swizzled works, 0 use block-major
+  static int mode_ok = knobs().wmode;  // -1 unknown, 1 row-swizzled works, 0 use block-major
   const int KW = p.K / (32 / bits), KG = p.K / p.group;
   const int nmaps = nacc == 2 ? 2 : p.nseg;
   for (int pass = 0; pass < 2; ++pass) {

@@ -217,6 +217,28 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     return out
 
 
+def attn_decode_workspace_bytes(B: int, Hq: int, hd: int, splits: int) -> int:
+    return int(L.load().sc_attn_decode_workspace_bytes(B, Hq, hd, splits))
+
+
+def attn_decode(qkv: torch.Tensor, B: int, Hq: int, Hkv: int, hd: int, pos: torch.Tensor, cos_tab: torch.Tensor,
+                sin_tab: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, splits: int, out: torch.Tensor,
+                tickets: torch.Tensor, workspace: Optional[torch.Tensor] = None,
+                scale: Optional[float] = None) -> torch.Tensor:
+    """One decode token per sequence: RoPE + KV append + split-KV attention
+    (+ merge) in one launch.  ``tickets`` is int32 [B*Hkv], zero on entry
+    and left zero."""
+    _cuda(qkv, pos, cos_tab, sin_tab, k_cache, v_cache, out, tickets, workspace)
+    nbytes = attn_decode_workspace_bytes(B, Hq, hd, splits)
+    if workspace is None:
+        workspace = Workspace.get(nbytes, qkv.device)
+    sc = (1.0 / math.sqrt(hd)) if scale is None else scale
+    L.call("sc_attn_decode", _p(qkv), B, Hq, Hkv, hd, _p(pos), _p(cos_tab), _p(sin_tab), cos_tab.shape[0],
+           _p(k_cache), _p(v_cache), k_cache.shape[2], float(sc), splits, _p(out), _dt(out), _p(workspace),
+           nbytes if workspace is not None else 0, _p(tickets), stream_handle(qkv.device))
+    return out
+
+
 # ---------------------------------------------------------------- K5 / K7
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:

@@ -5,9 +5,10 @@ This is the hot path behind ``ParallelTransformer.forward`` /
 worker/executor.py:229-325), re-laid for B200:
 
 * one step = embedding gather (K3) -> per layer [RMSNorm+q|k|v GEMV (K1) ->
-  RoPE+KV append (K4) -> split-KV flash-decode (K4) -> o GEMV + residual (K1)
+  fused RoPE + KV append + split-KV attention (K4) -> o GEMV + residual (K1)
   -> RMSNorm+gate|up GEMV with SiLU*mul (K1) -> down GEMV + residual (K1)] ->
-  RMSNorm+tied LM-head GEMV (K1) -> argmax (K7);
+  RMSNorm+tied LM-head GEMV (K1) -> argmax (K7); optionally (``prefetch_mb``)
+  an L2 prefetch of the next GEMV's weights is queued after each GEMV;
 * TP > 1: the embedding and the two row-parallel outputs per layer are
   all-reduced with NCCL; rank 0 folds the residual into its partial so the
   all-reduce output *is* the new hidden state; greedy sampling gathers only
@@ -21,7 +22,9 @@ worker/executor.py:229-325), re-laid for B200:
 
 from __future__ import annotations
 
+import ctypes as C
 import math
+import os
 from typing import List, Optional
 
 import numpy as np
@@ -47,7 +50,8 @@ class DecodeEngine:
     """One rank's decoder state: weights, KV cache, buffers, captured step."""
 
     def __init__(self, weights: RankWeights, comm=None, max_batch: int = 1, max_seq: int = 2048,
-                 device: Optional[torch.device] = None, attn_splits: Optional[int] = None):
+                 device: Optional[torch.device] = None, attn_splits: Optional[int] = None,
+                 prefetch_mb: Optional[float] = None):
         cfg: ModelConfig = weights.cfg
         self.cfg = cfg
         self.w = weights
@@ -76,10 +80,17 @@ class DecodeEngine:
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.host_pos = 0  # host mirror of pos: bounds every step against the cache length
         self.tok = torch.zeros(self.B, dtype=torch.int32, device=dev)  # decode input / sampled output
+        self.tickets = torch.zeros(self.B * self.Hkv, dtype=torch.int32, device=dev)  # attention split merge
+        self.fused_attn = os.environ.get("SC_ATTN_FUSED", "1") != "0"
         if attn_splits is None:
             attn_splits = max(1, min(64, math.ceil(2 * 148 / max(1, self.Hkv * self.B)), math.ceil(self.Lmax / 64)))
         self.splits = attn_splits
         self._bufs = {}
+        # L2 prefetch of the next GEMV's weights (bytes per GEMV; 0 = off)
+        if prefetch_mb is None:  # off by default: measured slower on B200 (the prefetches compete with the GEMV)
+            prefetch_mb = float(os.environ.get("SC_PREFETCH_MB", "0"))
+        self.prefetch_bytes = int(prefetch_mb * (1 << 20))
+        self._pf_lists = {}
         self._probe: Optional[list] = None  # (start, end, bytes) per GEMV while instrumenting
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self._graph_stream: Optional[torch.cuda.Stream] = None
@@ -98,6 +109,7 @@ class DecodeEngine:
                 ops.qlinear_workspace_bytes(M, self.F, self.H, self.bits),
                 ops.qlinear_workspace_bytes(M, self.H, self.Vl, self.bits),
                 ops.flash_decode_workspace_bytes(B, S, self.Hq, self.hd, self.splits if S == 1 else 1),
+                ops.attn_decode_workspace_bytes(B, self.Hq, self.hd, self.splits),
                 ops.argmax_workspace_bytes(B, self.Vl)]
         return max(max(need), 1 << 16)
 
@@ -168,6 +180,28 @@ class DecodeEngine:
                       M * N * out.element_size() + (M * N * residual.element_size() if residual is not None else 0))
             self._probe.append((ev0, ev1, nbytes))
 
+    def _prefetch(self, segs):
+        """Queue an L2 prefetch of (a budget's share of) the next GEMV's weights.
+
+        Issued right after a GEMV launch: it runs beside that GEMV and keeps
+        HBM busy through its tail and the kernels before the next GEMV.  Each
+        tensor of the next GEMV is prefetched from its start, in proportion to
+        the budget, so every CTA's first tiles are covered."""
+        if self.prefetch_bytes <= 0:
+            return
+        key = tuple(t.data_ptr() for tri in segs for t in tri)
+        lst = self._pf_lists.get(key)
+        if lst is None:
+            tensors = [t for tri in segs for t in tri]
+            sizes = [t.numel() * t.element_size() for t in tensors]
+            frac = min(1.0, self.prefetch_bytes / max(1, sum(sizes)))
+            n = len(tensors)
+            lst = ((C.c_void_p * n)(*[t.data_ptr() for t in tensors]),
+                   (C.c_size_t * n)(*[int(z * frac) for z in sizes]), n)
+            self._pf_lists[key] = lst
+        ptrs, sizes, n = lst
+        L.call("sc_l2_prefetch", C.cast(ptrs, L._pp), sizes, n, 0, ops.stream_handle(self.device))
+
     def _allreduce(self, send, recv):
         if self.world == 1:
             if send.data_ptr() != recv.data_ptr():
@@ -185,35 +219,55 @@ class DecodeEngine:
         if hidden is not None:
             hidden.append(h.clone())
         splits = self.splits if S == 1 else 1
+        nl = len(w.layers)
+        pf = S == 1  # decode steps prefetch; a prefill reads each weight many times anyway
         for i, lw in enumerate(w.layers):
             kc, vc = self.kv[i, 0], self.kv[i, 1]
             self._qlin(h, [lw.q, lw.k, lw.v], bf["qkv"], norm=lw.ln1)
-            ops.rope_append(bf["qkv"], B, S, self.Hq, self.Hkv, self.hd, self.pos, self.cos, self.sin, bf["q"], kc, vc)
-            ops.flash_decode(bf["q"], kc, vc, self.pos, B, S, self.Hq, self.Hkv, self.hd, splits, bf["attn"],
-                             workspace=self._ws)
-            self._row_out(bf["attn"], lw.o, h, bf["part"])
+            if pf:
+                self._prefetch([lw.o])
+            if S == 1 and self.fused_attn:
+                ops.attn_decode(bf["qkv"], B, self.Hq, self.Hkv, self.hd, self.pos, self.cos, self.sin, kc, vc,
+                                splits, bf["attn"], self.tickets[: B * self.Hkv], workspace=self._ws)
+            else:
+                ops.rope_append(bf["qkv"], B, S, self.Hq, self.Hkv, self.hd, self.pos, self.cos, self.sin, bf["q"],
+                                kc, vc)
+                ops.flash_decode(bf["q"], kc, vc, self.pos, B, S, self.Hq, self.Hkv, self.hd, splits, bf["attn"],
+                                 workspace=self._ws)
+            self._row_out(bf["attn"], lw.o, h, bf["part"], [lw.gate, lw.up] if pf else None)
             self._qlin(h, [lw.gate, lw.up], bf["act"], epilogue=L.SC_EPI_SWIGLU, norm=lw.ln2)
-            self._row_out(bf["act"], lw.down, h, bf["part"])
+            if pf:
+                self._prefetch([lw.down])
+            nxt = None
+            if pf:
+                nxt = [w.layers[i + 1].q, w.layers[i + 1].k, w.layers[i + 1].v] if i + 1 < nl else [w.embed]
+            self._row_out(bf["act"], lw.down, h, bf["part"], nxt)
             if hidden is not None:
                 hidden.append(h.clone())
 
-    def _row_out(self, x, tri, h, part):
+    def _row_out(self, x, tri, h, part, prefetch_next=None):
         """Row-parallel linear + residual.  TP=1: h += x.W^T in place.  TP>1:
         rank 0 writes h + x.W^T, others x.W^T, and the all-reduce of those
-        partials lands in h (the residual is added exactly once)."""
+        partials lands in h (the residual is added exactly once).  The next
+        GEMV's weights are prefetched while the all-reduce runs."""
         if self.world == 1:
             self._qlin(x, [tri], h, epilogue=L.SC_EPI_RESIDUAL, residual=h)
-            return
-        if self.rank == 0:
+        elif self.rank == 0:
             self._qlin(x, [tri], part, epilogue=L.SC_EPI_RESIDUAL, residual=h)
         else:
             self._qlin(x, [tri], part)
-        self._allreduce(part, h)
+        if prefetch_next is not None:
+            self._prefetch(prefetch_next)
+        if self.world > 1:
+            self._allreduce(part, h)
 
     def _sample(self, bf, hlast, B: int, advance: int):
         """Tied LM head on the last position of each sequence + greedy argmax."""
         w = self.w
         self._qlin(hlast, [w.embed], bf["logits"], norm=w.norm)
+        if B == self.B and hlast.shape[0] == self.B and w.layers:
+            lw = w.layers[0]
+            self._prefetch([lw.q, lw.k, lw.v])  # the next step starts with layer 0's q|k|v
         ops.argmax(bf["logits"], index_offset=w.vocab_start, val=bf["val"], idx=bf["idx"])
         if self.world > 1:
             self.comm.allgather_into(bf["val"], bf["gval"])

@@ -296,3 +296,62 @@ def test_rmsnorm_silu_add_argmax(cuda, rng):
     ops.argmax_merge(vals, idxs, 3, tok, pos, 1)
     assert tok.cpu().tolist() == otp.distributed_argmax(parts, 50).tolist()
     assert int(pos.item()) == 8
+
+
+def test_l2_prefetch_is_a_pure_hint(cuda, rng):
+    """sc_l2_prefetch touches no data: buffers are unchanged, unaligned starts
+    are rounded, empty lists are a no-op and more than 12 regions are refused."""
+    import ctypes as C
+
+    lib = L.load()
+    bufs = [torch.randn(n, device=cuda) for n in (1000, 4096, 77)]
+    before = [b.clone() for b in bufs]
+    ptrs = [b.data_ptr() for b in bufs] + [bufs[0].data_ptr() + 4]
+    sizes = [b.numel() * 4 for b in bufs] + [100]
+    P = (C.c_void_p * 4)(*ptrs)
+    Z = (C.c_size_t * 4)(*sizes)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.sc_l2_prefetch(C.cast(P, L._pp), Z, 4, 0, stream) == L.SC_OK
+    assert lib.sc_l2_prefetch(C.cast(P, L._pp), Z, 4, 1024, stream) == L.SC_OK
+    assert lib.sc_l2_prefetch(None, None, 0, 0, stream) == L.SC_OK
+    P13 = (C.c_void_p * 13)(*([ptrs[0]] * 13))
+    Z13 = (C.c_size_t * 13)(*([64] * 13))
+    assert lib.sc_l2_prefetch(C.cast(P13, L._pp), Z13, 13, 0, stream) == L.SC_ERR_ARG
+    torch.cuda.synchronize()
+    for a, b in zip(bufs, before):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("hd,Hq,Hkv", [(128, 32, 8), (64, 8, 1), (128, 4, 4), (64, 16, 2), (128, 16, 2)])
+@pytest.mark.parametrize("splits,past", [(1, 37), (3, 37), (33, 2047), (8, 0), (64, 5)])
+def test_attn_decode_matches_rope_append_plus_flash(cuda, rng, hd, Hq, Hkv, splits, past):
+    """The fused decode attention appends exactly what sc_rope_append writes
+    and matches sc_rope_append + sc_flash_decode (and the float64 oracle)."""
+    B, Lmax = 2, 2112
+    cos, sin = otp.rope_tables(hd, 4096, 5e5)
+    cos_t, sin_t = torch.from_numpy(cos).to(cuda), torch.from_numpy(sin).to(cuda)
+    kc = torch.from_numpy((rng.standard_normal((B, Hkv, Lmax, hd))).astype(np.float16)).to(cuda)
+    vc = torch.from_numpy((rng.standard_normal((B, Hkv, Lmax, hd))).astype(np.float16)).to(cuda)
+    kc2, vc2 = kc.clone(), vc.clone()
+    qkv = torch.from_numpy(rng.standard_normal((B, (Hq + 2 * Hkv) * hd)).astype(np.float32)).to(cuda)
+    pos = torch.tensor([past], dtype=torch.int32, device=cuda)
+    out = torch.empty(B, Hq * hd, dtype=torch.float32, device=cuda)
+    tickets = torch.zeros(B * Hkv, dtype=torch.int32, device=cuda)
+    ws = torch.empty(max(1, ops.attn_decode_workspace_bytes(B, Hq, hd, splits)), dtype=torch.uint8, device=cuda)
+    for _ in range(2):  # twice: the tickets must come back to zero
+        ops.attn_decode(qkv, B, Hq, Hkv, hd, pos, cos_t, sin_t, kc, vc, splits, out, tickets, workspace=ws)
+    assert int(tickets.abs().sum()) == 0
+    q2 = torch.empty(B, Hq * hd, dtype=torch.float32, device=cuda)
+    ops.rope_append(qkv, B, 1, Hq, Hkv, hd, pos, cos_t, sin_t, q2, kc2, vc2)
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    ref = torch.empty_like(out)
+    ops.flash_decode(q2, kc2, vc2, pos, B, 1, Hq, Hkv, hd, max(1, splits), ref)
+    assert rel_l2(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-5
+    # float64 oracle over the cache as the kernel left it
+    k64 = kc[:, :, : past + 1].double().cpu().numpy()
+    v64 = vc[:, :, : past + 1].double().cpu().numpy()
+    q64 = q2.double().cpu().numpy().reshape(B, Hq, 1, hd)
+    G = Hq // Hkv
+    kk, vv = np.repeat(k64, G, 1), np.repeat(v64, G, 1)
+    o64 = otp.softmax(q64 @ kk.transpose(0, 1, 3, 2) / math.sqrt(hd)) @ vv
+    assert rel_l2(out.cpu().numpy(), o64.reshape(B, Hq * hd)) <= 1e-4

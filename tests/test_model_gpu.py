@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 HIDDEN_TOL = 1e-3
 
 
-def _engine(shape, shard, world=1, rank=0, comm=None, max_seq=128, max_batch=1, dev=None):
+def _engine(shape, shard, world=1, rank=0, comm=None, max_seq=128, max_batch=1, dev=None, prefetch_mb=None):
     from shardcompute_b200.model.config import ModelConfig
     from shardcompute_b200.parallel.decode_engine import DecodeEngine
     from shardcompute_b200.parallel.weights import RankWeights
@@ -26,7 +26,7 @@ def _engine(shape, shard, world=1, rank=0, comm=None, max_seq=128, max_batch=1, 
     dev = dev or torch.device("cuda", 0)
     cfg = ModelConfig.from_dict(synth.model_config_dict(shape))
     w = RankWeights.from_shard(cfg, shard, world, rank, shape.bits, shape.group_size, dev)
-    return DecodeEngine(w, comm, max_batch=max_batch, max_seq=max_seq, device=dev)
+    return DecodeEngine(w, comm, max_batch=max_batch, max_seq=max_seq, device=dev, prefetch_mb=prefetch_mb)
 
 
 def _rel(a, b):
@@ -71,11 +71,12 @@ def test_prefill_then_decode_hidden_states(cuda, name):
     assert _rel(logits2.cpu().numpy(), ref_logits2) <= HIDDEN_TOL
 
 
-def test_greedy_agreement_graph_decode(cuda):
+@pytest.mark.parametrize("prefetch_mb", [0, 32])
+def test_greedy_agreement_graph_decode(cuda, prefetch_mb):
     shape = synth.tiny_shape(num_layers=2)
     full = synth.checkpoint(shape, seed=5, std=0.05)
     shard = osh.shard_weights(full, 1, 0)
-    eng = _engine(shape, shard, max_seq=192)
+    eng = _engine(shape, shard, max_seq=192, prefetch_mb=prefetch_mb)
     ref = TPModel([shard], shape, max_len=192)
     rng = np.random.Generator(np.random.PCG64(11))
     prompt = rng.integers(0, shape.vocab_size, size=(1, 16))
