@@ -9,7 +9,9 @@
  *     not synchronise; they are safe to capture in a CUDA graph.
  *   - Buffers are caller-owned.  Entry points that need scratch take a
  *     `workspace` pointer and size; the matching *_workspace_bytes() query
- *     gives the size.  Nothing here allocates device memory.
+ *     gives the size.  Nothing here allocates device memory, except the
+ *     peer-memory transport's arena (sc_p2p_create / sc_p2p_destroy) and the
+ *     static scratch of sc_qlinear_noalloc.
  *   - fp16 tensors are passed as uint16_t*; dtype codes are SC_F16 / SC_F32.
  *   - The weight format is MLX's group-wise affine format that the reference
  *     stores in its shards: wq uint32 [rows, K*bits/32] with element j of a
@@ -120,6 +122,24 @@ int sc_qlinear_fused(const void* x, int x_dtype, int M, int K, int ldx,
                      int group_size, int bits, const uint16_t* bias, int epilogue,
                      void* y, int y_dtype, int ldy, const float* residual, int ldr,
                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* sc_qlinear_fused that also pulls the NEXT kernel's weights into L2: up to
+ * 12 regions (pf_ptrs / pf_bytes, at most pf_max_bytes in total, 0 = no
+ * cap; starts rounded up and lengths down to 16 bytes).  The decode kernel
+ * (M <= 4 rows) issues them from each CTA's copy engine as soon as that CTA's
+ * own last weight tile has landed, so HBM keeps streaming through the
+ * consumers' drain, the kernel boundary and the next kernel's start; other
+ * passes ignore the list.  A hint only: results do not depend on it.  No
+ * reference counterpart (the reference streams weights through MLX). */
+int sc_qlinear_fused_prefetch(const void* x, int x_dtype, int M, int K, int ldx,
+                              const uint16_t* norm_weight, float norm_eps,
+                              int nseg, const uint32_t* const* wq, const uint16_t* const* scales,
+                              const uint16_t* const* biases, const int* seg_rows,
+                              int group_size, int bits, const uint16_t* bias, int epilogue,
+                              void* y, int y_dtype, int ldy, const float* residual, int ldr,
+                              void* workspace, size_t workspace_bytes,
+                              const void* const* pf_ptrs, const size_t* pf_bytes, int pf_n,
+                              size_t pf_max_bytes, cudaStream_t stream);
 
 /* Prefetch up to 12 device regions into L2 (at most max_bytes in total, 0 =
  * no cap) without waiting for them.  The decode step issues it right after a
@@ -237,6 +257,39 @@ int sc_allgather(const void* send, void* recv, size_t count_per_rank, int dtype,
                  cudaStream_t stream);
 int sc_broadcast(const void* send, void* recv, size_t count, int dtype, int root, void* comm,
                  cudaStream_t stream);
+
+/* ------------------------------------------------------ NVLink peer memory --
+ * One-shot all-reduce / all-gather through peer memory for the small
+ * per-token messages of decode (same reference interfaces as above:
+ * collectives/all_reduce.py:58-193, collectives/all_gather.py:54-162); the
+ * Python Communicator uses them instead of NCCL for messages up to max_bytes.
+ * Each rank owns an IPC-exported device arena (the one allocation of this
+ * library, made by sc_p2p_create and freed by sc_p2p_destroy).  Setup:
+ * sc_p2p_create on every rank -> exchange the handle bytes (host store) ->
+ * sc_p2p_open with all ranks' handles in rank order (own entry ignored) ->
+ * host barrier before the first call.  Every rank must make the same
+ * sequence of calls (same counts), like any collective, and must not
+ * destroy its transport while a peer may still send (host barrier first).
+ * Waits are bounded (sc_p2p_set_timeout, default 2 s); after a timeout
+ * sc_p2p_status reports 1 (read from host memory, no GPU call) and results
+ * are undefined until the transport is recreated.  All-reduce: sum in rank
+ * order with fp32 accumulation, f16 / f32, recv may alias send.  All-gather:
+ * recv[q * count + i] = rank q's send[i], 4-byte dtypes (f32 / i32). */
+size_t sc_p2p_handle_bytes(void);
+int sc_p2p_create(int world, int rank, size_t max_bytes, void** p2p_out, void* handle_out,
+                  size_t handle_bytes);
+int sc_p2p_open(void* p2p, const void* handles, size_t handle_bytes);
+/* Maps every unmapped rank onto this process's own arena: nothing but this
+ * process writes it, so a call waits for peers that never send.  Used to
+ * test the bounded wait on one GPU. */
+int sc_p2p_open_loopback(void* p2p);
+int sc_p2p_set_timeout(void* p2p, uint64_t timeout_ns);
+int sc_p2p_status(void* p2p, int* timed_out);
+int sc_p2p_destroy(void* p2p);
+int sc_p2p_allreduce(const void* send, void* recv, size_t count, int dtype, void* p2p,
+                     cudaStream_t stream);
+int sc_p2p_allgather(const void* send, void* recv, size_t count_per_rank, int dtype, void* p2p,
+                     cudaStream_t stream);
 
 #ifdef __cplusplus
 }

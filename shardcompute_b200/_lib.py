@@ -40,6 +40,8 @@ SIGNATURES = {
     "sc_qlinear": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "sc_qlinear_fused": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp, _i,
                               _vp, _i, _i, _vp, _i, _vp, _sz, _vp]),
+    "sc_qlinear_fused_prefetch": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp,
+                                       _i, _vp, _i, _i, _vp, _i, _vp, _sz, _pp, C.POINTER(_sz), _i, _sz, _vp]),
     "sc_embed_gather_q": (_i, [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp]),
     "sc_embed_gather_f16": (_i, [_vp, _i, _vp, _i, _i, _i, _vp, _i, _vp]),
     "sc_dequantize": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
@@ -64,6 +66,15 @@ SIGNATURES = {
     "sc_allreduce": (_i, [_vp, _vp, _sz, _i, _i, _vp, _vp]),
     "sc_allgather": (_i, [_vp, _vp, _sz, _i, _vp, _vp]),
     "sc_broadcast": (_i, [_vp, _vp, _sz, _i, _i, _vp, _vp]),
+    "sc_p2p_handle_bytes": (_sz, []),
+    "sc_p2p_create": (_i, [_i, _i, _sz, _pp, _vp, _sz]),
+    "sc_p2p_open": (_i, [_vp, _vp, _sz]),
+    "sc_p2p_open_loopback": (_i, [_vp]),
+    "sc_p2p_set_timeout": (_i, [_vp, C.c_uint64]),
+    "sc_p2p_status": (_i, [_vp, C.POINTER(_i)]),
+    "sc_p2p_destroy": (_i, [_vp]),
+    "sc_p2p_allreduce": (_i, [_vp, _vp, _sz, _i, _vp, _vp]),
+    "sc_p2p_allgather": (_i, [_vp, _vp, _sz, _i, _vp, _vp]),
 }
 
 _lib = None
@@ -117,3 +128,8 @@ def check(status: int, what: str = "") -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
+
+
+def last_error() -> str:
+    """The library's message for the last failure on this thread."""
+    return (load().sc_last_error() or b"").decode(errors="replace")

@@ -25,7 +25,9 @@ from __future__ import annotations
 
 import ctypes as C
 import datetime
+import itertools
 import logging
+import os
 import pickle
 import time
 from dataclasses import dataclass
@@ -36,6 +38,12 @@ import torch
 logger = logging.getLogger(__name__)
 
 _OPS = {"sum": 0, "max": 1, "min": 2, "mean": 3}
+
+# poll() code for a timed-out NVLink peer-memory collective.
+P2P_TIMEOUT = -1
+# Communicators a process creates, in order: the same sequence on every rank
+# gives matching store keys for each communicator's peer-memory setup.
+_P2P_GENERATION = itertools.count()
 
 
 @dataclass
@@ -86,6 +94,8 @@ class Communicator:
         self._bcast_counter = 0
         self._p2p_counter: Dict[tuple, int] = {}
         self._comm_stream: Optional[torch.cuda.Stream] = None
+        self._p2p = None  # sc_p2p handle: NVLink one-shot collectives for small messages
+        self._p2p_max = 0
 
     # ------------------------------------------------------------ setup
 
@@ -139,7 +149,61 @@ class Communicator:
             L.check(lib.sc_comm_init(uid, 128, self.world_size, self.rank, C.byref(handle)), "sc_comm_init")
             self._comm = handle
             self._comm_stream = torch.cuda.Stream()
+            self._init_p2p(timeout)
         self._initialized = True
+
+    def _init_p2p(self, timeout: float):
+        """Map every peer's IPC arena for the NVLink one-shot collectives.
+
+        Used for all-reduce (sum, f16/f32) and all-gather (4-byte types) of
+        messages up to ``SC_P2P_MAX_BYTES`` (default 1 MiB); ``SC_P2P=0``
+        keeps everything on NCCL.  Ranks publish whether their setup worked
+        and either all use the transport or none does."""
+        gen = next(_P2P_GENERATION)
+        if self.world_size < 2 or self.world_size > 8 or os.environ.get("SC_P2P", "1") == "0":
+            return
+        from .. import _lib as L
+
+        lib = L.load()
+        hb = int(lib.sc_p2p_handle_bytes())
+        max_bytes = int(os.environ.get("SC_P2P_MAX_BYTES", 1 << 20))
+        handle = C.c_void_p()
+        buf = (C.c_char * hb)()
+        ok = lib.sc_p2p_create(self.world_size, self.rank, max_bytes, C.byref(handle), buf, hb) == L.SC_OK
+        if not ok:
+            logger.warning("p2p transport unavailable on rank %d: %s", self.rank, L.last_error())
+        pre = f"shardcompute_b200/p2p/{gen}"
+        wait = datetime.timedelta(seconds=timeout)
+        self._store.set(f"{pre}/h/{self.rank}", bytes(buf) if ok else b"-")
+        keys = [f"{pre}/h/{q}" for q in range(self.world_size)]
+        self._store.wait(keys, wait)
+        hs = [self._store.get(k) for k in keys]
+        if ok and all(len(h) == hb for h in hs):
+            table = (C.c_char * (hb * self.world_size))()
+            for q, h in enumerate(hs):
+                C.memmove(C.addressof(table) + q * hb, h, hb)
+            ok = lib.sc_p2p_open(handle, table, hb) == L.SC_OK
+            if not ok:
+                logger.warning("p2p open failed on rank %d: %s", self.rank, L.last_error())
+        else:
+            ok = False
+        self._store.set(f"{pre}/ok/{self.rank}", b"1" if ok else b"0")
+        keys = [f"{pre}/ok/{q}" for q in range(self.world_size)]
+        self._store.wait(keys, wait)
+        if all(self._store.get(k) == b"1" for k in keys):
+            self._p2p, self._p2p_max = handle, max_bytes
+            self._p2p_gen = gen
+        elif handle.value:
+            lib.sc_p2p_destroy(handle)
+
+    @property
+    def p2p_enabled(self) -> bool:
+        """True when small all-reduces / all-gathers go through NVLink peer memory."""
+        return self._p2p is not None
+
+    def _p2p_fits(self, t: torch.Tensor, dtypes) -> bool:
+        return (self._p2p is not None and t.dtype in dtypes
+                and t.numel() * t.element_size() <= self._p2p_max)
 
     def _require(self):
         if not self._initialized:
@@ -175,8 +239,13 @@ class Communicator:
             return
         from .. import _lib as L
 
+        stream = torch.cuda.current_stream(send.device).cuda_stream
+        if op == "sum" and self._p2p_fits(send, (torch.float16, torch.float32)):
+            L.call("sc_p2p_allreduce", send.data_ptr(), recv.data_ptr(), send.numel(), self._dt(send), self._p2p,
+                   stream)
+            return
         L.call("sc_allreduce", send.data_ptr(), recv.data_ptr(), send.numel(), self._dt(send), _OPS[op],
-               self._comm, torch.cuda.current_stream(send.device).cuda_stream)
+               self._comm, stream)
 
     def allgather_into(self, send: torch.Tensor, recv: torch.Tensor) -> None:
         """Enqueue an all-gather: ``recv`` is ``[world, *send.shape]`` contiguous."""
@@ -193,8 +262,12 @@ class Communicator:
             return
         from .. import _lib as L
 
-        L.call("sc_allgather", send.data_ptr(), recv.data_ptr(), send.numel(), self._dt(send), self._comm,
-               torch.cuda.current_stream(send.device).cuda_stream)
+        stream = torch.cuda.current_stream(send.device).cuda_stream
+        if self._p2p_fits(send, (torch.float32, torch.int32)):
+            L.call("sc_p2p_allgather", send.data_ptr(), recv.data_ptr(), send.numel(), self._dt(send), self._p2p,
+                   stream)
+            return
+        L.call("sc_allgather", send.data_ptr(), recv.data_ptr(), send.numel(), self._dt(send), self._comm, stream)
 
     # ------------------------------------------------------------ reference API
 
@@ -365,18 +438,52 @@ class Communicator:
     # ------------------------------------------------------------ failure handling
 
     def poll(self) -> int:
-        """NCCL asynchronous error code (0 = healthy); never blocks."""
+        """0 when healthy, else NCCL's asynchronous error code, or
+        ``P2P_TIMEOUT`` when a peer-memory collective gave up waiting for a
+        peer.  Never blocks and makes no GPU call."""
         if self.backend != "nccl" or self._comm is None:
             return 0
         from .. import _lib as L
 
+        if self._p2p is not None:
+            t = C.c_int(0)
+            L.check(L.load().sc_p2p_status(self._p2p, C.byref(t)), "sc_p2p_status")
+            if t.value:
+                return P2P_TIMEOUT
         err = C.c_int(0)
         L.check(L.load().sc_comm_poll(self._comm, C.byref(err)), "sc_comm_poll")
         return err.value
 
+    def check_health(self):
+        """Raise if a collective failed (TimeoutError for a peer that stopped
+        answering a peer-memory collective, RuntimeError for NCCL)."""
+        code = self.poll()
+        if code == P2P_TIMEOUT:
+            raise TimeoutError(f"rank {self.rank}: a peer-memory collective timed out waiting for a peer")
+        if code:
+            raise RuntimeError(f"rank {self.rank}: NCCL asynchronous error {code}")
+
+    def _close_p2p(self, wait_for_peers: bool):
+        """Free the peer-memory transport; first (unless aborting) wait until
+        every rank got here, so no peer still sends into this rank's arena."""
+        if self._p2p is None:
+            return
+        from .. import _lib as L
+
+        if wait_for_peers:
+            pre = f"shardcompute_b200/p2p/{self._p2p_gen}"
+            self._store.set(f"{pre}/bye/{self.rank}", b"1")
+            try:
+                self._store.wait([f"{pre}/bye/{q}" for q in range(self.world_size)], datetime.timedelta(seconds=60))
+            except Exception:  # noqa: BLE001 - a dead peer sends nothing more
+                logger.warning("rank %d: peers missing at p2p shutdown", self.rank)
+        L.load().sc_p2p_destroy(self._p2p)
+        self._p2p = None
+
     def abort(self):
         """Tear the communicator down without waiting for peers (unblocks a rank stuck on a dead peer)."""
         if self.backend == "nccl" and self._comm is not None:
+            self._close_p2p(wait_for_peers=False)
             from .. import _lib as L
 
             L.load().sc_comm_abort(self._comm)
@@ -391,6 +498,7 @@ class Communicator:
             from .. import _lib as L
 
             torch.cuda.synchronize()
+            self._close_p2p(wait_for_peers=True)
             L.check(L.load().sc_comm_destroy(self._comm), "sc_comm_destroy")
             self._comm = None
         self._initialized = False

@@ -66,6 +66,43 @@ inline cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t 
     }                                        \
   } while (0)
 
+// ---------------------------------------------------------------- L2 prefetch
+
+// Up to PF_MAX_REGIONS device byte ranges to pull into L2 (16-byte aligned
+// starts, lengths multiples of 16), cut into PF_CHUNK-byte bulk prefetches.
+constexpr int PF_MAX_REGIONS = 12;
+constexpr unsigned PF_CHUNK = 32u << 10;
+
+struct PrefetchList {
+  const unsigned char* p[PF_MAX_REGIONS];
+  unsigned long long n[PF_MAX_REGIONS];
+  int count;
+};
+
+// Builds a list from caller regions: starts rounded up to 16 bytes, lengths
+// down to 16, at most max_bytes in total (0 = no cap), regions in order.
+int make_prefetch_list(const void* const* ptrs, const size_t* bytes, int n, size_t max_bytes, PrefetchList* L);
+
+// Issues this participant's share of the list's chunks (chunk c of the whole
+// list goes to participant c % nparts).  Fire and forget: nothing waits for
+// the data, and a prefetch is only a hint to the memory system.
+__device__ __forceinline__ void l2_prefetch_share(const PrefetchList& L, uint32_t part, uint32_t nparts) {
+  unsigned long long c0 = 0;  // first list-wide chunk index of region r
+#pragma unroll
+  for (int r = 0; r < PF_MAX_REGIONS; ++r) {
+    if (r >= L.count) break;
+    const unsigned long long n = L.n[r];
+    const unsigned long long nch = (n + PF_CHUNK - 1) / PF_CHUNK;
+    for (unsigned long long c = (part + nparts - c0 % nparts) % nparts; c < nch; c += nparts) {
+      const unsigned long long off = c * PF_CHUNK;
+      const unsigned long long rem = n - off;
+      const uint32_t sz = (uint32_t)(rem < PF_CHUNK ? rem : PF_CHUNK);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(L.p[r] + off), "r"(sz) : "memory");
+    }
+    c0 += nch;
+  }
+}
+
 inline int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -156,12 +193,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread is parked by the
+// hardware until the phase completes (or the hint, in ns, runs out) instead of
+// re-polling the barrier, which would take shared-memory issue slots from the
+// warps and the TMA writes that do the work.
+constexpr uint32_t MBAR_SUSPEND_NS = 20000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(MBAR_SUSPEND_NS)
       : "memory");
   return ok != 0;
 }

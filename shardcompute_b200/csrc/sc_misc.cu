@@ -299,40 +299,16 @@ int sc_argmax_merge(const float* vals, const int32_t* idxs, int M, int world, in
 // stream order is kept for everything after it.
 namespace sc {
 
-constexpr int PF_MAX_REGIONS = 12;
-constexpr unsigned PF_CHUNK = 32u << 10;
-
-struct PrefetchList {
-  const unsigned char* p[PF_MAX_REGIONS];
-  unsigned long long n[PF_MAX_REGIONS];
-  int count;
-};
-
 __global__ void l2_prefetch_kernel(const PrefetchList L) {
   pdl_trigger();
-  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  const size_t nth = (size_t)gridDim.x * blockDim.x;
-  for (int r = 0; r < L.count; ++r) {
-    const unsigned long long n = L.n[r];
-    const size_t nch = (size_t)((n + PF_CHUNK - 1) / PF_CHUNK);
-    for (size_t c = tid; c < nch; c += nth) {
-      const unsigned long long off = (unsigned long long)c * PF_CHUNK;
-      const unsigned long long rem = n - off;
-      const uint32_t sz = (uint32_t)(rem < PF_CHUNK ? rem : PF_CHUNK) & ~15u;
-      if (sz) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(L.p[r] + off), "r"(sz) : "memory");
-    }
-  }
+  l2_prefetch_share(L, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
   pdl_wait();
 }
 
-}  // namespace sc
-
-extern "C" int sc_l2_prefetch(const void* const* ptrs, const size_t* bytes, int n, size_t max_bytes,
-                              cudaStream_t stream) {
-  SC_REQUIRE(n >= 0 && n <= sc::PF_MAX_REGIONS, SC_ERR_ARG, "l2_prefetch: 0..%d regions (got %d)",
-             sc::PF_MAX_REGIONS, n);
-  SC_REQUIRE(n == 0 || (ptrs && bytes), SC_ERR_ARG, "l2_prefetch: null region list");
-  sc::PrefetchList L = {};
+int make_prefetch_list(const void* const* ptrs, const size_t* bytes, int n, size_t max_bytes, PrefetchList* L) {
+  SC_REQUIRE(n >= 0 && n <= PF_MAX_REGIONS, SC_ERR_ARG, "l2 prefetch: 0..%d regions (got %d)", PF_MAX_REGIONS, n);
+  SC_REQUIRE(n == 0 || (ptrs && bytes), SC_ERR_ARG, "l2 prefetch: null region list");
+  *L = PrefetchList{};
   size_t budget = max_bytes ? max_bytes : (size_t)-1;
   for (int r = 0; r < n && budget; ++r) {
     const uintptr_t a = (uintptr_t)ptrs[r];
@@ -341,11 +317,20 @@ extern "C" int sc_l2_prefetch(const void* const* ptrs, const size_t* bytes, int 
     size_t len = bytes[r] - (a16 - a);
     len = std::min(len & ~(size_t)15, budget);
     if (!len) continue;
-    L.p[L.count] = reinterpret_cast<const unsigned char*>(a16);
-    L.n[L.count] = len;
-    ++L.count;
+    L->p[L->count] = reinterpret_cast<const unsigned char*>(a16);
+    L->n[L->count] = len;
+    ++L->count;
     budget -= len;
   }
+  return SC_OK;
+}
+
+}  // namespace sc
+
+extern "C" int sc_l2_prefetch(const void* const* ptrs, const size_t* bytes, int n, size_t max_bytes,
+                              cudaStream_t stream) {
+  sc::PrefetchList L;
+  if (int st = sc::make_prefetch_list(ptrs, bytes, n, max_bytes, &L)) return st;
   if (L.count == 0) return SC_OK;
   ::sc::launch(sc::l2_prefetch_kernel, 8, 128, 0, stream, L);
   return sc::check_launch("l2_prefetch");

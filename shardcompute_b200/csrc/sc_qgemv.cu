@@ -72,6 +72,7 @@ struct QGemvParams {
   int chunks_per_split;  // chunk count of each K split
   int tiles;             // ceil(N / 16)
   int lg_group;          // log2(group)
+  PrefetchList pf;       // the next kernel's weights, pulled into L2 by the decode kernel's producer
 };
 
 template <int BITS>
@@ -415,6 +416,7 @@ struct TmaGeo {
   int row_swz;      // 1: box lines ordered (block, row) with row-dependent swizzle
   int s_swz;        // scale-box swizzle mask: 0 none, 1 (32 B), 3 (64 B), 7 (128 B)
   int pre_stages;   // factored kernel: stages the producer issues before x is staged
+  int pf_after;     // factored kernel: L2 prefetch waits until this CTA's last stage has landed
 };
 
 struct TmaMaps {
@@ -1039,6 +1041,16 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
           ++it;
         }
       }
+      if (p.pf.count && !s_abort) {
+        // The next kernel's weights: once this CTA's own last stage has
+        // landed, HBM would otherwise idle through the consumers' drain, the
+        // epilogue and the next kernel's start, so pull this CTA's share of
+        // them into L2 now (issued earlier they would compete with its own).
+        const uint32_t k = it ? it - 1 : 0;
+        if (!it || !geo.pf_after ||
+            mbar_wait_bounded(&full[k % geo.nst], (k / geo.nst) & 1, &s_abort, TC_WAIT_NS))
+          l2_prefetch_share(p.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+      }
       if (s_abort) {
         for (uint32_t k = (it > (uint32_t)geo.nst ? it - geo.nst : 0); k < it; ++k) {
           int dummy = 0;
@@ -1334,8 +1346,9 @@ static int tma_unit(int bits, int group) { return std::max(2, 8 * group / kpc_of
 // SC_QGEMV_WMODE=0/1 the packed-word tensor-map layout (block-major /
 // row-swizzled; default: row-swizzled when the driver accepts it).
 struct Knobs {
-  int cps = 0, nst = 0, ldg = 0, nofx = 0, wmode = -1, pre = -1;
+  int cps = 0, nst = 0, ldg = 0, nofx = 0, wmode = -1, pre = -1, pf_after = 1;
   Knobs() {
+    if (const char* e = getenv("SC_PF_AFTER")) pf_after = atoi(e);
     if (const char* e = getenv("SC_QGEMV_PRE")) pre = atoi(e);
     if (const char* e = getenv("SC_QGEMV_WMODE")) wmode = atoi(e);
     if (const char* e = getenv("SC_QGEMV_FX")) nofx = e[0] == '0';
@@ -1405,6 +1418,7 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   if (nst < 2) return tp;
   geo.nst = nst;
   geo.pre_stages = knobs().pre >= 0 ? std::min(knobs().pre, nst) : nst;
+  geo.pf_after = knobs().pf_after;
   geo.red_off = geo.ring_off + nst * geo.stage_bytes;
   geo.bar_off = round_up(geo.red_off + red_bytes, 16);
   geo.atomic_out = 0;
@@ -1650,7 +1664,7 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
                        int nseg, const uint32_t* const* wq, const uint16_t* const* scales,
                        const uint16_t* const* biases, const int* seg_rows, int group, int bits,
                        const uint16_t* bias, int epi, void* y, int y_dtype, int ldy, const float* residual,
-                       int ldr, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                       int ldr, void* ws, size_t ws_bytes, const PrefetchList* pf, cudaStream_t stream) {
   SC_REQUIRE(x && y && wq && scales && biases && seg_rows, SC_ERR_ARG, "qlinear: null pointer argument");
   SC_REQUIRE(bits == 4 || bits == 8, SC_ERR_SHAPE, "qlinear: bits must be 4 or 8 (got %d)", bits);
   SC_REQUIRE(group == 32 || group == 64 || group == 128, SC_ERR_SHAPE,
@@ -1706,6 +1720,7 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
     p.x = static_cast<const char*>(x) + (size_t)m0 * ldx * xsz;
     p.y = static_cast<char*>(y) + (size_t)m0 * ldy * ysz;
     p.residual = residual ? residual + (size_t)m0 * ldr : nullptr;
+    p.pf = (pf && m0 + mb == M) ? *pf : PrefetchList{};  // the last pass carries the prefetch
     TmaMaps maps;
     const TmaPlan* tp = nullptr;
     if (pp.tma && encode_maps(p, bits, nacc, &pp.tp.geo, &maps)) {
@@ -1783,7 +1798,7 @@ int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const uint32_t
   const uint16_t* b[1] = {biases};
   int rows[1] = {N};
   return sc::run_qlinear(x, x_dtype, M, K, ldx, nullptr, 0.f, 1, w, s, b, rows, group_size, bits, bias,
-                         SC_EPI_STORE, y, y_dtype, ldy, nullptr, 0, workspace, workspace_bytes, stream);
+                         SC_EPI_STORE, y, y_dtype, ldy, nullptr, 0, workspace, workspace_bytes, nullptr, stream);
 }
 
 int sc_qlinear_fused(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_weight,
@@ -1793,7 +1808,21 @@ int sc_qlinear_fused(const void* x, int x_dtype, int M, int K, int ldx, const ui
                      int ldr, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   return sc::run_qlinear(x, x_dtype, M, K, ldx, norm_weight, norm_eps, nseg, wq, scales, biases, seg_rows,
                          group_size, bits, bias, epilogue, y, y_dtype, ldy, residual, ldr, workspace,
-                         workspace_bytes, stream);
+                         workspace_bytes, nullptr, stream);
+}
+
+int sc_qlinear_fused_prefetch(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_weight,
+                              float norm_eps, int nseg, const uint32_t* const* wq, const uint16_t* const* scales,
+                              const uint16_t* const* biases, const int* seg_rows, int group_size, int bits,
+                              const uint16_t* bias, int epilogue, void* y, int y_dtype, int ldy,
+                              const float* residual, int ldr, void* workspace, size_t workspace_bytes,
+                              const void* const* pf_ptrs, const size_t* pf_bytes, int pf_n, size_t pf_max_bytes,
+                              cudaStream_t stream) {
+  sc::PrefetchList pf;
+  if (int st = sc::make_prefetch_list(pf_ptrs, pf_bytes, pf_n, pf_max_bytes, &pf)) return st;
+  return sc::run_qlinear(x, x_dtype, M, K, ldx, norm_weight, norm_eps, nseg, wq, scales, biases, seg_rows,
+                         group_size, bits, bias, epilogue, y, y_dtype, ldy, residual, ldr, workspace,
+                         workspace_bytes, pf.count ? &pf : nullptr, stream);
 }
 
 }  // extern "C"

@@ -8,9 +8,11 @@ worker/executor.py:229-325), re-laid for B200:
   fused RoPE + KV append + split-KV attention (K4) -> o GEMV + residual (K1)
   -> RMSNorm+gate|up GEMV with SiLU*mul (K1) -> down GEMV + residual (K1)] ->
   RMSNorm+tied LM-head GEMV (K1) -> argmax (K7); optionally (``prefetch_mb``)
-  an L2 prefetch of the next GEMV's weights is queued after each GEMV;
+  each GEMV's producer also pulls a share of the next GEMV's weights into L2
+  once its own have landed;
 * TP > 1: the embedding and the two row-parallel outputs per layer are
-  all-reduced with NCCL; rank 0 folds the residual into its partial so the
+  all-reduced through NVLink peer memory (one-shot, NCCL for messages above
+  the transport's limit); rank 0 folds the residual into its partial so the
   all-reduce output *is* the new hidden state; greedy sampling gathers only
   (max, index) per rank instead of the vocab-split logits;
 * the residual stream is fp32, GEMV inputs fp16, KV cache fp16
@@ -87,7 +89,7 @@ class DecodeEngine:
         self.splits = attn_splits
         self._bufs = {}
         # L2 prefetch of the next GEMV's weights (bytes per GEMV; 0 = off)
-        if prefetch_mb is None:  # off by default: measured slower on B200 (the prefetches compete with the GEMV)
+        if prefetch_mb is None:
             prefetch_mb = float(os.environ.get("SC_PREFETCH_MB", "0"))
         self.prefetch_bytes = int(prefetch_mb * (1 << 20))
         self._pf_lists = {}
@@ -149,10 +151,13 @@ class DecodeEngine:
 
     # ------------------------------------------------------------ kernels of one step
 
-    def _qlin(self, x, segs, out, epilogue=L.SC_EPI_STORE, norm=None, residual=None):
-        """Fused GEMV through the C ABI with the engine's workspace."""
+    def _qlin(self, x, segs, out, epilogue=L.SC_EPI_STORE, norm=None, residual=None, prefetch=None):
+        """Fused GEMV through the C ABI with the engine's workspace.
+
+        ``prefetch``: the next GEMV's weight segments; a budget's share of them
+        is pulled into L2 by this GEMV's producer once its own weights have
+        landed (decode steps only; see ``prefetch_mb``)."""
         n = len(segs)
-        import ctypes as C
 
         M, K = x.shape
         rows = [int(s[0].shape[0]) for s in segs]
@@ -165,12 +170,16 @@ class DecodeEngine:
             ev0 = torch.cuda.Event(enable_timing=True, external=True)
             ev1 = torch.cuda.Event(enable_timing=True, external=True)
             ev0.record()
-        L.call("sc_qlinear_fused", x.data_ptr(), ops._dt(x), M, K, K,
-               None if norm is None else norm.data_ptr(), float(self.eps), n,
-               C.cast(W, L._pp), C.cast(Sp, L._pp), C.cast(Bp, L._pp), R, self.group, self.bits, None, epilogue,
-               out.data_ptr(), ops._dt(out), N, None if residual is None else residual.data_ptr(),
-               N if residual is not None else 0, self._ws.data_ptr(), self._ws.numel(),
-               ops.stream_handle(self.device))
+        args = (x.data_ptr(), ops._dt(x), M, K, K, None if norm is None else norm.data_ptr(), float(self.eps), n,
+                C.cast(W, L._pp), C.cast(Sp, L._pp), C.cast(Bp, L._pp), R, self.group, self.bits, None, epilogue,
+                out.data_ptr(), ops._dt(out), N, None if residual is None else residual.data_ptr(),
+                N if residual is not None else 0, self._ws.data_ptr(), self._ws.numel())
+        pf = self._pf_list(prefetch) if prefetch else None
+        if pf is None:
+            L.call("sc_qlinear_fused", *args, ops.stream_handle(self.device))
+        else:
+            L.call("sc_qlinear_fused_prefetch", *args, C.cast(pf[0], L._pp), pf[1], pf[2], 0,
+                   ops.stream_handle(self.device))
         if self._probe is not None:
             ev1.record()
             # algorithmic bytes: packed words + fp16 scale/bias of every segment,
@@ -180,15 +189,12 @@ class DecodeEngine:
                       M * N * out.element_size() + (M * N * residual.element_size() if residual is not None else 0))
             self._probe.append((ev0, ev1, nbytes))
 
-    def _prefetch(self, segs):
-        """Queue an L2 prefetch of (a budget's share of) the next GEMV's weights.
-
-        Issued right after a GEMV launch: it runs beside that GEMV and keeps
-        HBM busy through its tail and the kernels before the next GEMV.  Each
-        tensor of the next GEMV is prefetched from its start, in proportion to
-        the budget, so every CTA's first tiles are covered."""
+    def _pf_list(self, segs):
+        """(ptrs, sizes, n) for an L2 prefetch of a budget's share of ``segs``:
+        every tensor of the next GEMV from its start, in proportion to the
+        budget, so the first tiles of every CTA are covered.  None when off."""
         if self.prefetch_bytes <= 0:
-            return
+            return None
         key = tuple(t.data_ptr() for tri in segs for t in tri)
         lst = self._pf_lists.get(key)
         if lst is None:
@@ -199,8 +205,7 @@ class DecodeEngine:
             lst = ((C.c_void_p * n)(*[t.data_ptr() for t in tensors]),
                    (C.c_size_t * n)(*[int(z * frac) for z in sizes]), n)
             self._pf_lists[key] = lst
-        ptrs, sizes, n = lst
-        L.call("sc_l2_prefetch", C.cast(ptrs, L._pp), sizes, n, 0, ops.stream_handle(self.device))
+        return lst
 
     def _allreduce(self, send, recv):
         if self.world == 1:
@@ -223,9 +228,7 @@ class DecodeEngine:
         pf = S == 1  # decode steps prefetch; a prefill reads each weight many times anyway
         for i, lw in enumerate(w.layers):
             kc, vc = self.kv[i, 0], self.kv[i, 1]
-            self._qlin(h, [lw.q, lw.k, lw.v], bf["qkv"], norm=lw.ln1)
-            if pf:
-                self._prefetch([lw.o])
+            self._qlin(h, [lw.q, lw.k, lw.v], bf["qkv"], norm=lw.ln1, prefetch=[lw.o] if pf else None)
             if S == 1 and self.fused_attn:
                 ops.attn_decode(bf["qkv"], B, self.Hq, self.Hkv, self.hd, self.pos, self.cos, self.sin, kc, vc,
                                 splits, bf["attn"], self.tickets[: B * self.Hkv], workspace=self._ws)
@@ -235,9 +238,8 @@ class DecodeEngine:
                 ops.flash_decode(bf["q"], kc, vc, self.pos, B, S, self.Hq, self.Hkv, self.hd, splits, bf["attn"],
                                  workspace=self._ws)
             self._row_out(bf["attn"], lw.o, h, bf["part"], [lw.gate, lw.up] if pf else None)
-            self._qlin(h, [lw.gate, lw.up], bf["act"], epilogue=L.SC_EPI_SWIGLU, norm=lw.ln2)
-            if pf:
-                self._prefetch([lw.down])
+            self._qlin(h, [lw.gate, lw.up], bf["act"], epilogue=L.SC_EPI_SWIGLU, norm=lw.ln2,
+                       prefetch=[lw.down] if pf else None)
             nxt = None
             if pf:
                 nxt = [w.layers[i + 1].q, w.layers[i + 1].k, w.layers[i + 1].v] if i + 1 < nl else [w.embed]
@@ -249,25 +251,24 @@ class DecodeEngine:
         """Row-parallel linear + residual.  TP=1: h += x.W^T in place.  TP>1:
         rank 0 writes h + x.W^T, others x.W^T, and the all-reduce of those
         partials lands in h (the residual is added exactly once).  The next
-        GEMV's weights are prefetched while the all-reduce runs."""
+        GEMV's weights are prefetched by this GEMV's producer."""
         if self.world == 1:
-            self._qlin(x, [tri], h, epilogue=L.SC_EPI_RESIDUAL, residual=h)
+            self._qlin(x, [tri], h, epilogue=L.SC_EPI_RESIDUAL, residual=h, prefetch=prefetch_next)
         elif self.rank == 0:
-            self._qlin(x, [tri], part, epilogue=L.SC_EPI_RESIDUAL, residual=h)
+            self._qlin(x, [tri], part, epilogue=L.SC_EPI_RESIDUAL, residual=h, prefetch=prefetch_next)
         else:
-            self._qlin(x, [tri], part)
-        if prefetch_next is not None:
-            self._prefetch(prefetch_next)
+            self._qlin(x, [tri], part, prefetch=prefetch_next)
         if self.world > 1:
             self._allreduce(part, h)
 
     def _sample(self, bf, hlast, B: int, advance: int):
         """Tied LM head on the last position of each sequence + greedy argmax."""
         w = self.w
-        self._qlin(hlast, [w.embed], bf["logits"], norm=w.norm)
+        nxt = None
         if B == self.B and hlast.shape[0] == self.B and w.layers:
             lw = w.layers[0]
-            self._prefetch([lw.q, lw.k, lw.v])  # the next step starts with layer 0's q|k|v
+            nxt = [lw.q, lw.k, lw.v]  # the next step starts with layer 0's q|k|v
+        self._qlin(hlast, [w.embed], bf["logits"], norm=w.norm, prefetch=nxt)
         ops.argmax(bf["logits"], index_offset=w.vocab_start, val=bf["val"], idx=bf["idx"])
         if self.world > 1:
             self.comm.allgather_into(bf["val"], bf["gval"])
@@ -400,6 +401,8 @@ class DecodeEngine:
                 self.replay()
             else:
                 self.decode_step()
+        if self.world > 1:
+            self.comm.check_health()  # a timed-out peer-memory collective leaves undefined tokens
         return torch.stack(out, dim=1)
 
     def forward_logits(self, input_ids: torch.Tensor, return_hidden: bool = False):
