@@ -72,6 +72,7 @@ struct QGemvParams {
   int chunks_per_split;  // chunk count of each K split
   int tiles;             // ceil(N / 16)
   int lg_group;          // log2(group)
+  int x_vec;             // x rows start on 16 bytes: 8 values load as one or two 16-byte vectors
   PrefetchList pf;       // the next kernel's weights, pulled into L2 by the decode kernel's producer
 };
 
@@ -396,7 +397,7 @@ qgemv_kernel(const QGemvParams p) {
 // sc_qgemv_device_error().
 constexpr int TC_NCW = 16;  // consumer warps
 constexpr int TC_THREADS = (TC_NCW + 1) * 32;
-constexpr int TC_MAX_NST = 8;
+constexpr int TC_MAX_NST = 12;
 constexpr uint64_t TC_WAIT_NS = 2000000000ull;  // 2 s
 
 static __device__ int g_qgemv_error = 0;
@@ -417,6 +418,8 @@ struct TmaGeo {
   int s_swz;        // scale-box swizzle mask: 0 none, 1 (32 B), 3 (64 B), 7 (128 B)
   int pre_stages;   // factored kernel: stages the producer issues before x is staged
   int pf_after;     // factored kernel: L2 prefetch waits until this CTA's last stage has landed
+  int acc_off;      // factored kernel: byte offset of the per-tile output accumulators
+  int acc_floats;   // factored kernel: their count (tiles of a CTA x 16 rows x M x sets), 8 bytes each
 };
 
 struct TmaMaps {
@@ -788,7 +791,14 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
 // over its k-lanes, and adds the tile's 16 row sums into a shared-memory
 // slot with shared atomics; the warp that arrives last on the slot's counter
 // runs the epilogue.  No CTA-wide barrier sits in the streaming loop.
-constexpr int FX_NSLOT = TC_MAX_NST + 2;  // > ring depth: a warp is never a ring ahead of the slowest
+
+// 64-bit two's-complement fixed point with 32 fraction bits (|v| < 2^31).
+__device__ __forceinline__ unsigned long long fx_to_fixed(float v) {
+  return (unsigned long long)__double2ll_rn((double)v * 4294967296.0);
+}
+__device__ __forceinline__ float fx_from_fixed(unsigned long long u) {
+  return (float)((double)(long long)u * (1.0 / 4294967296.0));
+}
 
 template <int BITS>
 __device__ __forceinline__ void unpack_off(uint32_t w, uint32_t (&a)[4]) {
@@ -812,36 +822,84 @@ __device__ __forceinline__ void unpack_off(uint32_t w, uint32_t (&a)[4]) {
 // a 64-byte table {xoff(2t), xoff(2t+1), xsum(2t), xsum(2t+1)} per lane t.
 __host__ __device__ constexpr int fx_chunk_bytes(int bits, int M) { return M * 2 * (bits == 4 ? 4 : 2) * 64 + 64; }
 
+// 8 consecutive x values of row m from k0 (k0 + 8 <= K), as floats.
+template <typename XT>
+__device__ __forceinline__ void ld_x8(const QGemvParams& p, int m, int k0, float (&v)[8]) {
+  const size_t base = (size_t)m * p.ldx + k0;
+  if (p.x_vec) {
+    if constexpr (sizeof(XT) == 4) {
+      const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + base);
+      const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + base + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+      const uint4 a = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + base);
+      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(u32_as_h2(w[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = ld_x<XT>(p.x, base + i);
+  }
+}
+
 // Stage normalised x for chunks [kc0, kc1) (consumer threads only).
+// Work unit: 8 consecutive values of one row m -- one packed word at 4 bits,
+// two at 8 bits -- which fill exactly one 16-byte B-fragment unit per part
+// (hi / lo).  Consecutive lanes take consecutive units, so a column-group's
+// units sit in aligned lane groups and its sums reduce by shuffles.  A thread
+// loads all its units (up to FXS_UB per batch) before using any, and with
+// RMSNorm keeps them in registers across the norm reduction when one batch
+// covers the slice (one L2 round trip instead of two).
+constexpr int FXS_UB = 4;
+
 template <int BITS, int NGC, bool NORM, typename XT>
 __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* xsb, float (*s_part)[4], float* s_rms,
                                            int kc0, int kc1, int tid, int nthreads, int bar_id) {
   using TR = QTraits<BITS>;
   constexpr int XQ = TR::NMMA / 2;
-  constexpr int VPL = TR::KPC / 32;        // values per lane of a chunk (4-bit: 4, 8-bit: 2)
-  constexpr int GV = TR::KPC / NGC;        // values of one column-group inside a chunk
-  constexpr int GL = GV / VPL;             // lanes covering one column-group
+  constexpr int UPC = TR::KPC / 8;       // units per chunk
+  constexpr int GU = TR::KPC / NGC / 8;  // units of one column-group inside a chunk (>= 4)
   const int M = p.M;
-  const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
   const int CB = fx_chunk_bytes(BITS, M);
-  // Both passes issue all of a thread's global loads before using any: the
-  // prologue is a chain of L2 round trips, so the fewer, the better.
+  const int upm = (kc1 - kc0) * UPC;  // units per row of x
+  const int nu = upm * M;
+  const int kb = kc0 * TR::KPC;
+  const int nbatch = (nu + FXS_UB * nthreads - 1) / (FXS_UB * nthreads);
+  float v[FXS_UB][8];
+  auto load_batch = [&](int b0) {
+#pragma unroll
+    for (int b = 0; b < FXS_UB; ++b) {
+      const int u = b0 + b * nthreads + tid;
+      const int m = u / upm, k0 = kb + (u - m * upm) * 8;
+      if (u < nu && k0 < p.K) {
+        ld_x8<XT>(p, m, k0, v[b]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[b][i] = 0.f;
+      }
+    }
+  };
   if (NORM) {
-    constexpr int U = 8;
     float ss[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k0 = tid; k0 < p.K; k0 += nthreads * U) {
-      float v[4][U];
+    for (int bi = 0; bi < nbatch; ++bi) {
+      const int b0 = bi * FXS_UB * nthreads;
+      load_batch(b0);
 #pragma unroll
-      for (int m = 0; m < 4; ++m)
+      for (int b = 0; b < FXS_UB; ++b) {
+        const int u = b0 + b * nthreads + tid;
+        const int m = u < nu ? u / upm : 0;
+        float q = 0.f;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int k = k0 + u * nthreads;
-          v[m][u] = (m < M && k < p.K) ? ld_x<XT>(p.x, (size_t)m * p.ldx + k) : 0.f;
-        }
+        for (int i = 0; i < 8; ++i) q = fmaf(v[b][i], v[b][i], q);
 #pragma unroll
-      for (int m = 0; m < 4; ++m)
-#pragma unroll
-        for (int u = 0; u < U; ++u) ss[m] = fmaf(v[m][u], v[m][u], ss[m]);
+        for (int mm = 0; mm < 4; ++mm) ss[mm] += (mm == m) ? q : 0.f;
+      }
     }
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
@@ -851,80 +909,97 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
     }
     named_bar_sync(bar_id, nthreads);
     if (tid < M) {
-      float s = 0.f;
-      for (int w = 0; w < nwarps; ++w) s += s_part[w][tid];
-      s_rms[tid] = sqrtf(s / (float)p.K + p.eps);
+      float sum = 0.f;
+      for (int w = 0; w < nwarps; ++w) sum += s_part[w][tid];
+      s_rms[tid] = sqrtf(sum / (float)p.K + p.eps);
     }
     named_bar_sync(bar_id, nthreads);
   }
-  // one warp per (chunk, m) task, TB tasks of a warp loaded together: lane l
-  // owns the VPL consecutive values starting at chunk value l * VPL, i.e.
-  // word (l * VPL) / PF, elements from (l * VPL) % PF
-  constexpr int TB = 4;
-  const int nkc = kc1 - kc0;
-  const int ntask = nkc * M;
-  for (int t0 = warp; t0 < ntask; t0 += nwarps * TB) {
-    float xv[TB][VPL], nw[TB][VPL];
+  for (int bi = 0; bi < nbatch; ++bi) {
+    const int b0 = bi * FXS_UB * nthreads;
+    if (!NORM || nbatch > 1) load_batch(b0);
 #pragma unroll
-    for (int b = 0; b < TB; ++b) {
-      const int task = t0 + b * nwarps;
-      const int cl = task / M, m = task % M;
-      const int kbase = (kc0 + cl) * TR::KPC + lane * VPL;
+    for (int b = 0; b < FXS_UB; ++b) {
+      const int u = b0 + b * nthreads + tid;
+      if (b0 + b * nthreads >= nu) break;  // warp-uniform: no unit of this slot anywhere
+      const bool ok = u < nu;
+      const int m = ok ? u / upm : 0;
+      const int ul = ok ? u - m * upm : 0;
+      const int k0 = kb + ul * 8;
+      const int cl = ul / UPC, uc = ul % UPC;
+      float x[8];
+      if (NORM) {
+        float nw[8];
+        if (ok && k0 < p.K) {
+          if (p.x_vec) {
+            const uint4 nwv = *reinterpret_cast<const uint4*>(p.norm_w + k0);
+            const uint32_t nww[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
 #pragma unroll
-      for (int v = 0; v < VPL; ++v) {
-        const int k = kbase + v;
-        const bool ok = task < ntask && k < p.K;
-        xv[b][v] = ok ? ld_x<XT>(p.x, (size_t)m * p.ldx + k) : 0.f;
-        nw[b][v] = (NORM && ok) ? __half2float(__ushort_as_half(p.norm_w[k])) : 1.f;
-      }
-    }
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = __half22float2(u32_as_h2(nww[i]));
+              nw[2 * i] = f.x;
+              nw[2 * i + 1] = f.y;
+            }
+          } else {
 #pragma unroll
-    for (int b = 0; b < TB; ++b) {
-      const int task = t0 + b * nwarps;
-      if (task >= ntask) break;
-      const int cl = task / M, m = task % M;
-      float sh = 0.f, sl = 0.f, sx = 0.f;  // this lane's sums of hi, lo and exact x
-      unsigned char* cb = xsb + (size_t)cl * CB;
-#pragma unroll
-      for (int v = 0; v < VPL; ++v) {
-        float x = xv[b][v];
-        if (NORM) x = (x / s_rms[m]) * nw[b][v];
-        const int cv = lane * VPL + v;         // value index inside the chunk
-        const int wi = cv / TR::PF, e = cv % TR::PF;
-        __half hi = __float2half_rn(x);
-        __half lo = __float2half_rn(x - __half2float(hi));
-        if (BITS == 4 && (e & 1)) {            // odd codes arrive as 16 q: their x slots carry x / 16
-          hi = __hmul(hi, __float2half_rn(0.0625f));
-          lo = __hmul(lo, __float2half_rn(0.0625f));
-        }
-        sh += __half2float(hi);
-        sl += __half2float(lo);
-        sx += x;
-        const int t = wi >> 2, j = wi & 3;
-        int i, h;
-        if (BITS == 4) {
-          i = 2 * j + ((e >> 1) & 1);
-          h = 2 * (e & 1) + (e >> 2);
+            for (int i = 0; i < 8; ++i) nw[i] = __half2float(__ushort_as_half(p.norm_w[k0 + i]));
+          }
         } else {
-          i = j;
-          h = 2 * (e & 1) + (e >> 1);
-        }
-        const int q = i >> 1, r = i & 1;
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {
-          const int unit = ((m * 2 + part) * XQ + q) * 4 + t;
-          reinterpret_cast<__half*>(cb + unit * 16)[r * 4 + h] = part ? lo : hi;
+          for (int i = 0; i < 8; ++i) nw[i] = 0.f;
         }
+        const float r = s_rms[m];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = (v[b][i] / r) * nw[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = v[b][i];
       }
-      // reduce over the lanes of one column-group
+      // hi / lo halves in B-fragment order: 4-bit [x0 x4 x1 x5 x2 x6 x3 x7]
+      // (odd codes arrive as 16 q, so their slots carry x / 16), 8-bit
+      // [x0 x2 x1 x3 x4 x6 x5 x7]
+      __half hi[8], lo[8];
+      float sh = 0.f, sl = 0.f, sx = 0.f;
 #pragma unroll
-      for (int o = 1; o < GL; o <<= 1) {
+      for (int e = 0; e < 8; ++e) {
+        __half h = __float2half_rn(x[e]);
+        __half l = __float2half_rn(x[e] - __half2float(h));
+        if (BITS == 4 && (e & 1)) {
+          h = __hmul(h, __float2half_rn(0.0625f));
+          l = __hmul(l, __float2half_rn(0.0625f));
+        }
+        sh += __half2float(h);
+        sl += __half2float(l);
+        sx += x[e];
+        const int pos = BITS == 4 ? 4 * ((e >> 1) & 1) + 2 * (e & 1) + (e >> 2)
+                                  : 4 * (e >> 2) + 2 * (e & 1) + ((e >> 1) & 1);
+        hi[pos] = h;
+        lo[pos] = l;
+      }
+      // reduce over the lanes of one column-group (aligned lane groups of GU)
+#pragma unroll
+      for (int o = 1; o < GU; o <<= 1) {
         sh += __shfl_xor_sync(0xffffffffu, sh, o);
         sl += __shfl_xor_sync(0xffffffffu, sl, o);
         sx += __shfl_xor_sync(0xffffffffu, sx, o);
       }
-      if (lane % GL == 0) {
-        const int grp = lane / GL;  // column-group within the chunk
+      if (!ok) continue;
+      unsigned char* cb = xsb + (size_t)cl * CB;
+      const int t = BITS == 4 ? (uc >> 2) : (uc >> 1);
+      const int q = BITS == 4 ? (uc & 3) : (uc & 1);
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const __half* src = part ? lo : hi;
+        uint4 o;
+        o.x = h2_as_u32(__halves2half2(src[0], src[1]));
+        o.y = h2_as_u32(__halves2half2(src[2], src[3]));
+        o.z = h2_as_u32(__halves2half2(src[4], src[5]));
+        o.w = h2_as_u32(__halves2half2(src[6], src[7]));
+        const int unit = ((m * 2 + part) * XQ + q) * 4 + t;
+        *reinterpret_cast<uint4*>(cb + unit * 16) = o;
+      }
+      if (uc % GU == 0) {
+        const int grp = uc / GU;  // column-group within the chunk
         float* tab = reinterpret_cast<float*>(cb + M * 2 * XQ * 64);
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
@@ -937,7 +1012,7 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
     }
   }
   // columns no (m, part, group) maps to: zero table entries
-  for (int idx = tid; idx < nkc * 8; idx += nthreads) {
+  for (int idx = tid; idx < (kc1 - kc0) * 8; idx += nthreads) {
     const int cl = idx >> 3, col = idx & 7;
     if (col >= M * 2 * NGC) {
       float* tab = reinterpret_cast<float*>(xsb + (size_t)cl * CB + M * 2 * XQ * 64);
@@ -947,15 +1022,6 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
   }
   named_bar_sync(bar_id, nthreads);
 }
-
-// Shared-memory operands of one chunk for the factored kernel.
-template <int NMMA, int NACC>
-struct FxChunk {
-  uint32_t bfr[NMMA][2];  // B fragments (x high / low parts by column)
-  float4 tb;              // {xoff(2t), xoff(2t+1), xsum(2t), xsum(2t+1)}
-  uint4 w0[NACC], w1[NACC];
-  float sb[NACC][8];      // scales then biases: (row g, grp A), (g, B), (g+8, A), (g+8, B)
-};
 
 template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -971,8 +1037,6 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   __shared__ int s_abort;
   __shared__ float s_part[TC_NCW][4];
   __shared__ float s_rms[4];
-  __shared__ int s_cnt[FX_NSLOT];
-  __shared__ float s_slot[FX_NSLOT][NACC][16][4];
   __shared__ __align__(8) uint64_t s_xready;  // consumers have staged x (lets the producer run on)
 
   const int M = p.M;
@@ -989,8 +1053,11 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   uint64_t* full = reinterpret_cast<uint64_t*>(sbase + geo.bar_off);
   uint64_t* empty = full + TC_MAX_NST;
 
-  for (int i = tid; i < FX_NSLOT * NACC * 16 * 4; i += blockDim.x) (&s_slot[0][0][0][0])[i] = 0.f;
-  if (tid < FX_NSLOT) s_cnt[tid] = 0;
+  // Per-output accumulators of the CTA's tiles in 64-bit fixed point
+  // (2^-32 units): integer atomics make the sum over warps independent of
+  // their order, so every run (and every replay) gives the same bits.
+  unsigned long long* s_acc = reinterpret_cast<unsigned long long*>(sbase + geo.acc_off);
+  for (int i = tid; i < geo.acc_floats; i += blockDim.x) s_acc[i] = 0ull;
   if (tid == 0) {
     for (int s = 0; s < geo.nst; ++s) {
       mbar_init(&full[s], 1);
@@ -1080,187 +1147,205 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   const int lgG = p.lg_group;
   const int w_r8 = geo.row_swz ? 1024 : 8 * geo.nblk * 128;
   const int s_r8 = 16 * geo.ngs;
-  auto woff = [&](int c) -> int {
+  // Every consumer warp takes chunk `warp` of every stage (cps <= TC_NCW), so
+  // all its shared-memory offsets are fixed for the kernel.
+  int fo_w, fo_s;
+  {
+    const int c = warp;
     const int u = ((c & 1) << 2) | t;
-    if (geo.row_swz) return (c >> 1) * 2048 + pr0 * 128 + ((u ^ (pr0 & 7)) << 4);
-    const int l = pr0 * geo.nblk + (c >> 1);
-    return l * 128 + ((u ^ (l & 7)) << 4);
-  };
-  auto soff = [&](int c, int grp) -> int {  // scale-box byte offset of (row pr0, group grp of chunk c)
-    const int gi = ((c * TR::KPC) >> lgG) + grp;
-    const int lo = pr0 * geo.ngs * 2 + gi * 2;
-    return lo ^ (((lo >> 7) & geo.s_swz) << 4);
-  };
-  auto ld_sb = [&](const unsigned char* sp, float& va, float& vb) {
-    if (NGC >= 2) {
-      const __half2 h = *reinterpret_cast<const __half2*>(sp);
-      va = __low2float(h);
-      vb = __high2float(h);
+    if (geo.row_swz) {
+      fo_w = (c >> 1) * 2048 + pr0 * 128 + ((u ^ (pr0 & 7)) << 4);
     } else {
-      va = vb = __half2float(*reinterpret_cast<const __half*>(sp));
+      const int l = pr0 * geo.nblk + (c >> 1);
+      fo_w = l * 128 + ((u ^ (l & 7)) << 4);
     }
+    const int gi = ((c * TR::KPC) >> lgG) + grpA;
+    const int lo = pr0 * geo.ngs * 2 + gi * 2;
+    fo_s = lo ^ (((lo >> 7) & geo.s_swz) << 4);
+  }
+  const int fo_x = warp * CB + bx_off;
+  const int fo_t = warp * CB + M * 2 * XQ * 64 + t * 16;
+
+  // A stage's weight words and raw scale / bias words of this lane.  The
+  // SwiGLU pair keeps only its words a stage ahead (96 registers): its scales
+  // and biases are read from the held slot when they are used.
+  constexpr bool PIPE_SB = NACC == 1;
+  struct StageRegs {
+    uint4 w0[NACC], w1[NACC];
+    uint32_t sb[PIPE_SB ? NACC : 1][4];  // scale(row g), scale(row g+8), bias(row g), bias(row g+8)
+  };
+  auto ld_sb_raw = [&](const unsigned char* sp) -> uint32_t {
+    if (NGC >= 2) return *reinterpret_cast<const uint32_t*>(sp);  // groups grpA, grpA + 1
+    return (uint32_t)*reinterpret_cast<const uint16_t*>(sp);
+  };
+  auto ld_sb4 = [&](uint32_t (&d)[4], const unsigned char* st, int a) {
+    const unsigned char* sst = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
+    d[0] = ld_sb_raw(sst + fo_s);
+    d[1] = ld_sb_raw(sst + fo_s + s_r8);
+    d[2] = ld_sb_raw(sst + geo.sset_bytes + fo_s);
+    d[3] = ld_sb_raw(sst + geo.sset_bytes + fo_s + s_r8);
+  };
+  // A stage holds cps chunks (fewer than TC_NCW for a short K or a narrow
+  // scale box): warps past them read nothing, their offsets would leave the stage.
+  const bool has_chunk = warp < geo.cps;
+  auto ld_stage = [&](StageRegs& d, const unsigned char* st) {
+#pragma unroll
+    for (int a = 0; a < NACC; ++a) {
+      if (!has_chunk) {
+        d.w0[a] = d.w1[a] = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      const unsigned char* wst = st + a * geo.wset_bytes;
+      d.w0[a] = *reinterpret_cast<const uint4*>(wst + fo_w);
+      d.w1[a] = *reinterpret_cast<const uint4*>(wst + fo_w + w_r8);
+      if (PIPE_SB) ld_sb4(d.sb[PIPE_SB ? a : 0], st, a);
+    }
+  };
+  // (group grpA, group grpA + 1) of a raw scale / bias word
+  auto sb_lo = [](uint32_t r) { return __half2float(__ushort_as_half((uint16_t)(r & 0xffffu))); };
+  auto sb_hi = [](uint32_t r) {
+    return NGC >= 2 ? __half2float(__ushort_as_half((uint16_t)(r >> 16))) : __half2float(__ushort_as_half((uint16_t)(r & 0xffffu)));
   };
 
-  float acc[NACC][4];
-  const unsigned char* st = nullptr;  // current stage
-  const unsigned char* xst = nullptr; // staged x of the stage's first chunk
-  // A warp's chunks in a stage are warp and warp + TC_NCW (cps <= 2 * TC_NCW),
-  // so every shared-memory offset of its loads is fixed for the kernel.
-  int fo_w[2], fo_s[2], fo_x[2], fo_t[2];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int c = warp + j * TC_NCW;
-    fo_w[j] = woff(c);
-    fo_s[j] = soff(c, grpA);
-    fo_x[j] = c * CB + bx_off;
-    fo_t[j] = c * CB + M * 2 * XQ * 64 + t * 16;
-  }
-  auto fx_load = [&](FxChunk<NMMA, NACC>& d, int j) {
-    if (bact) {
-#pragma unroll
-      for (int q = 0; q < XQ; ++q) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xst + fo_x[j] + q * 64);
-        d.bfr[2 * q][0] = v.x;
-        d.bfr[2 * q][1] = v.y;
-        d.bfr[2 * q + 1][0] = v.z;
-        d.bfr[2 * q + 1][1] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < NMMA; ++i) d.bfr[i][0] = d.bfr[i][1] = 0u;
-    }
-    d.tb = *reinterpret_cast<const float4*>(xst + fo_t[j]);
-    const int wo = fo_w[j];
-    const int so = fo_s[j];
-#pragma unroll
-    for (int a = 0; a < NACC; ++a) {
-      const unsigned char* wst = st + a * geo.wset_bytes;
-      d.w0[a] = *reinterpret_cast<const uint4*>(wst + wo);
-      d.w1[a] = *reinterpret_cast<const uint4*>(wst + wo + w_r8);
-      const unsigned char* sst = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
-      ld_sb(sst + so, d.sb[a][0], d.sb[a][1]);
-      ld_sb(sst + so + s_r8, d.sb[a][2], d.sb[a][3]);
-      ld_sb(sst + geo.sset_bytes + so, d.sb[a][4], d.sb[a][5]);
-      ld_sb(sst + geo.sset_bytes + so + s_r8, d.sb[a][6], d.sb[a][7]);
-    }
-  };
-  auto fx_compute = [&](const FxChunk<NMMA, NACC>& d) {
-#pragma unroll
-    for (int a = 0; a < NACC; ++a) {
-      const uint32_t r0[4] = {d.w0[a].x, d.w0[a].y, d.w0[a].z, d.w0[a].w};
-      const uint32_t r1[4] = {d.w1[a].x, d.w1[a].y, d.w1[a].z, d.w1[a].w};
-      float ca[4] = {d.tb.x, d.tb.y, d.tb.x, d.tb.y};
-      float cz[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t A0[4], A1[4];
-        unpack_off<BITS>(r0[j], A0);
-        unpack_off<BITS>(r1[j], A1);
-        if (BITS == 4) {
-          mma_16816(ca, A0[0], A1[0], A0[1], A1[1], d.bfr[2 * j][0], d.bfr[2 * j][1]);
-          mma_16816(cz, A0[2], A1[2], A0[3], A1[3], d.bfr[2 * j + 1][0], d.bfr[2 * j + 1][1]);
-        } else if (j & 1) {
-          mma_16816(cz, A0[0], A1[0], A0[1], A1[1], d.bfr[j][0], d.bfr[j][1]);
-        } else {
-          mma_16816(ca, A0[0], A1[0], A0[1], A1[1], d.bfr[j][0], d.bfr[j][1]);
-        }
-      }
-      const float* sb = d.sb[a];  // sA0 sB0 sA1 sB1 bA0 bB0 bA1 bB1
-      acc[a][0] = fmaf(sb[0], ca[0] + cz[0], fmaf(sb[4], d.tb.z, acc[a][0]));
-      acc[a][1] = fmaf(sb[1], ca[1] + cz[1], fmaf(sb[5], d.tb.w, acc[a][1]));
-      acc[a][2] = fmaf(sb[2], ca[2] + cz[2], fmaf(sb[6], d.tb.z, acc[a][2]));
-      acc[a][3] = fmaf(sb[3], ca[3] + cz[3], fmaf(sb[7], d.tb.w, acc[a][3]));
-    }
-  };
+  // This CTA's tiles (blockIdx.x, + gridDim.x, ...) and the stages of each.
+  const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int spt = (kc1 - kc0 + geo.cps - 1) / geo.cps;
+  const int nq = my_tiles * spt;
   int s = 0;
   uint32_t ph = 0;
-  int ti = 0;  // tile iteration (slot = ti % FX_NSLOT)
   bool aborted = false;
-  for (int tile = blockIdx.x; tile < p.tiles && !aborted; tile += gridDim.x, ++ti) {
-    const int n0 = tile * 16;
+  StageRegs cur;
+  if (nq > 0) {
+    if (mbar_wait_bounded(&full[0], 0, &s_abort, TC_WAIT_NS))
+      ld_stage(cur, ring);
+    else
+      aborted = true;
+  }
+  float acc[NACC][4];
 #pragma unroll
-    for (int a = 0; a < NACC; ++a)
+  for (int a = 0; a < NACC; ++a)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
-
-    for (int kcs = kc0; kcs < kc1; kcs += geo.cps) {
-      if (!mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS)) { aborted = true; break; }
-      st = ring + (size_t)s * geo.stage_bytes;
-      xst = xsb + (size_t)(kcs - kc0) * CB;
-      const int nch = min(kc1 - kcs, geo.cps);
-      // a warp's chunks of the stage; single-set tiles take two at a time
-      // (every shared load of both issued before either is computed); the
-      // SwiGLU pair already has two independent weight sets per chunk and
-      // would exceed the 96-register budget of 17 warps per SM with two
-      if (DUAL) {
+    for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
+  int kst = 0, tl = 0;  // stage within the tile, tile of this CTA
+  for (int q = 0; q < nq && !aborted; ++q) {
+    const int kcs = kc0 + kst * geo.cps;
+    const bool act = warp < min(kc1 - kcs, geo.cps);
+    // ---- MMAs of the current stage (registers loaded one stage ahead)
+    float ca[NACC][4], cz[NACC][4];
+    float4 tb = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (act) {
+      const unsigned char* xst = xsb + (size_t)(kcs - kc0) * CB;
+      uint32_t bfr[NMMA][2];
+      if (bact) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          if (warp + j * TC_NCW >= nch) break;
-          FxChunk<NMMA, NACC> da;
-          fx_load(da, j);
-          fx_compute(da);
+        for (int qq = 0; qq < XQ; ++qq) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xst + fo_x + qq * 64);
+          bfr[2 * qq][0] = v.x;
+          bfr[2 * qq][1] = v.y;
+          bfr[2 * qq + 1][0] = v.z;
+          bfr[2 * qq + 1][1] = v.w;
         }
-      } else if (warp < nch) {
-        const bool two = warp + TC_NCW < nch;
-        FxChunk<NMMA, NACC> da, db;
-        fx_load(da, 0);
-        if (two) fx_load(db, 1);
-        fx_compute(da);
-        if (two) fx_compute(db);
+      } else {
+#pragma unroll
+        for (int i = 0; i < NMMA; ++i) bfr[i][0] = bfr[i][1] = 0u;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (++s == geo.nst) {
-        s = 0;
-        ph ^= 1;
+      tb = *reinterpret_cast<const float4*>(xst + fo_t);
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+        const uint32_t r0[4] = {cur.w0[a].x, cur.w0[a].y, cur.w0[a].z, cur.w0[a].w};
+        const uint32_t r1[4] = {cur.w1[a].x, cur.w1[a].y, cur.w1[a].z, cur.w1[a].w};
+        ca[a][0] = tb.x;
+        ca[a][1] = tb.y;
+        ca[a][2] = tb.x;
+        ca[a][3] = tb.y;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) cz[a][r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t A0[4], A1[4];
+          unpack_off<BITS>(r0[j], A0);
+          unpack_off<BITS>(r1[j], A1);
+          if (BITS == 4) {
+            mma_16816(ca[a], A0[0], A1[0], A0[1], A1[1], bfr[2 * j][0], bfr[2 * j][1]);
+            mma_16816(cz[a], A0[2], A1[2], A0[3], A1[3], bfr[2 * j + 1][0], bfr[2 * j + 1][1]);
+          } else if (j & 1) {
+            mma_16816(cz[a], A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
+          } else {
+            mma_16816(ca[a], A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
+          }
+        }
       }
     }
-    if (aborted) break;
-
-    // ---- tile done for this warp: reduce over k-lanes, add into the slot
-    const int slot = ti % FX_NSLOT;
-    const int m = t / NGC;
+    // ---- the next stage's registers load while those MMAs run
+    const int s_cur = s;
+    if (++s == geo.nst) {
+      s = 0;
+      ph ^= 1;
+    }
+    StageRegs nxt;
+    const bool more = q + 1 < nq;
+    if (more) {
+      if (mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS))
+        ld_stage(nxt, ring + (size_t)s * geo.stage_bytes);
+      else
+        aborted = true;
+    }
+    // ---- scales / biases of the current stage; then its slot is free
+    if (act) {
 #pragma unroll
-    for (int a = 0; a < NACC; ++a) {
-      float vg = acc[a][0] + acc[a][1], vg8 = acc[a][2] + acc[a][3];
+      for (int a = 0; a < NACC; ++a) {
+        uint32_t sbv[4];
+        if (PIPE_SB) {
 #pragma unroll
-      for (int o = 1; o < NGC; o <<= 1) {
-        vg += __shfl_xor_sync(0xffffffffu, vg, o);
-        vg8 += __shfl_xor_sync(0xffffffffu, vg8, o);
-      }
-      if ((t % NGC) == 0 && m < M) {
-        atomicAdd(&s_slot[slot][a][pr0][m], vg);
-        atomicAdd(&s_slot[slot][a][pr0 + 8][m], vg8);
+          for (int i = 0; i < 4; ++i) sbv[i] = cur.sb[PIPE_SB ? a : 0][i];
+        } else {
+          ld_sb4(sbv, ring + (size_t)s_cur * geo.stage_bytes, a);
+        }
+        acc[a][0] = fmaf(sb_lo(sbv[0]), ca[a][0] + cz[a][0], fmaf(sb_lo(sbv[2]), tb.z, acc[a][0]));
+        acc[a][1] = fmaf(sb_hi(sbv[0]), ca[a][1] + cz[a][1], fmaf(sb_hi(sbv[2]), tb.w, acc[a][1]));
+        acc[a][2] = fmaf(sb_lo(sbv[1]), ca[a][2] + cz[a][2], fmaf(sb_lo(sbv[3]), tb.z, acc[a][2]));
+        acc[a][3] = fmaf(sb_hi(sbv[1]), ca[a][3] + cz[a][3], fmaf(sb_hi(sbv[3]), tb.w, acc[a][3]));
       }
     }
     __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      last = atomicAdd(&s_cnt[slot], 1) == TC_NCW - 1;
-      if (last) __threadfence_block();
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      for (int e = lane; e < 16 * M; e += 32) {
-        const int rl = e / M, mm = e % M;
-        const int row = n0 + rl;
-        float v[2];
+    if (lane == 0) mbar_arrive(&empty[s_cur]);
+    // ---- tile done for this warp: reduce over k-lanes, add into the CTA's tile accumulators
+    if (++kst == spt) {
+      kst = 0;
+      const int m = t / NGC;
 #pragma unroll
-        for (int a = 0; a < NACC; ++a) {
-          v[a] = s_slot[slot][a][rl][mm];
-          s_slot[slot][a][rl][mm] = 0.f;
+      for (int a = 0; a < NACC; ++a) {
+        float vg = acc[a][0] + acc[a][1], vg8 = acc[a][2] + acc[a][3];
+#pragma unroll
+        for (int o = 1; o < NGC; o <<= 1) {
+          vg += __shfl_xor_sync(0xffffffffu, vg, o);
+          vg8 += __shfl_xor_sync(0xffffffffu, vg8, o);
         }
-        if (row < p.N) epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, mm, v);
+        if ((t % NGC) == 0 && m < M) {
+          atomicAdd(&s_acc[((tl * 16 + pr0) * M + m) * NACC + a], fx_to_fixed(vg));
+          atomicAdd(&s_acc[((tl * 16 + pr0 + 8) * M + m) * NACC + a], fx_to_fixed(vg8));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
       }
-      __syncwarp();
-      if (lane == 0) {
-        s_cnt[slot] = 0;
-        __threadfence_block();
-      }
+      ++tl;
     }
+    if (more) cur = nxt;
   }
   if (aborted && lane == 0) atomicExch(&g_qgemv_error, 1);
+  // ---- all warps' partial sums are in: the epilogue of every tile of this CTA
+  named_bar_sync(1, NC);
+  if (s_abort) return;  // a wait gave up: leave the output untouched
+  const int total = my_tiles * 16 * M;
+  for (int idx = tid; idx < total; idx += NC) {
+    const int tli = idx / (16 * M), rem = idx - tli * 16 * M;
+    const int rl = rem / M, mm = rem - rl * M;
+    const int row = ((int)blockIdx.x + tli * (int)gridDim.x) * 16 + rl;
+    float v[2];
+#pragma unroll
+    for (int a = 0; a < NACC; ++a) v[a] = fx_from_fixed(s_acc[idx * NACC + a]);
+    if (row < p.N) epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, mm, v);
+  }
 }
 
 template <int EPI, typename YT>
@@ -1394,8 +1479,10 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   sp.chunks_per_split = cps_of(splits);
   sp.splits = (KC + sp.chunks_per_split - 1) / sp.chunks_per_split;
   TmaGeo geo{};
-  int cps = knobs().cps > 0 ? knobs().cps : TC_STAGE_CHUNKS / nacc;
-  cps = std::min(cps, 2 * TC_NCW);  // each consumer warp takes at most two chunks of a stage
+  // batched kernel: 32 KB of packed words per stage, each consumer warp at
+  // most two chunks of it; factored kernel: one chunk per consumer warp
+  int cps = knobs().cps > 0 ? knobs().cps : fx ? TC_NCW : TC_STAGE_CHUNKS / nacc;
+  cps = std::min(cps, fx ? TC_NCW : 2 * TC_NCW);
   while (cps > U && cps * kpc_of(bits) / group * 2 > 128) cps /= 2;  // scale-box row <= 128 B (swizzle span)
   cps = std::min(cps, sp.chunks_per_split);
   cps = std::max(U, cps / U * U);
@@ -1411,7 +1498,12 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   geo.stage_bytes = nacc * (geo.wset_bytes + 2 * geo.sset_bytes);
   geo.ring_off = round_up((int)xsb(sp.chunks_per_split), 1024);
   const int red_bytes = fx ? 0 : 2 * TC_NCW * 32 * nacc * MT * 4 * 4;  // double-buffered by tile
-  const size_t fixed = geo.ring_off + red_bytes + 2 * TC_MAX_NST * 8 + 1024 /* base alignment */ + 64;
+  tp.grid_x = std::max(1, std::min(sp.tiles, (nsm + sp.splits - 1) / sp.splits));
+  // factored kernel: fp32 accumulators for every output of the CTA's tiles
+  geo.acc_floats = fx ? ((sp.tiles + tp.grid_x - 1) / tp.grid_x) * 16 * M * nacc : 0;
+  const int acc_bytes = round_up(geo.acc_floats * 8, 16);  // 64-bit fixed point
+  if (acc_bytes > 48 * 1024) return tp;
+  const size_t fixed = geo.ring_off + red_bytes + acc_bytes + 2 * TC_MAX_NST * 8 + 1024 /* base alignment */ + 64;
   if (fixed >= TC_SMEM_BUDGET) return tp;
   int nst = (int)std::min<size_t>(TC_MAX_NST, (TC_SMEM_BUDGET - fixed) / geo.stage_bytes);
   if (knobs().nst > 0) nst = std::min(nst, knobs().nst);
@@ -1420,13 +1512,13 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   geo.pre_stages = knobs().pre >= 0 ? std::min(knobs().pre, nst) : nst;
   geo.pf_after = knobs().pf_after;
   geo.red_off = geo.ring_off + nst * geo.stage_bytes;
-  geo.bar_off = round_up(geo.red_off + red_bytes, 16);
+  geo.acc_off = geo.red_off + red_bytes;
+  geo.bar_off = round_up(geo.acc_off + acc_bytes, 16);
   geo.atomic_out = 0;
   geo.row_swz = 1;
   tp.smem = geo.bar_off + 2 * TC_MAX_NST * 8 + 1024;
   tp.sp = sp;
   tp.geo = geo;
-  tp.grid_x = std::max(1, std::min(sp.tiles, (nsm + sp.splits - 1) / sp.splits));
   tp.ok = true;
   return tp;
 }
@@ -1721,6 +1813,7 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
     p.y = static_cast<char*>(y) + (size_t)m0 * ldy * ysz;
     p.residual = residual ? residual + (size_t)m0 * ldr : nullptr;
     p.pf = (pf && m0 + mb == M) ? *pf : PrefetchList{};  // the last pass carries the prefetch
+    p.x_vec = aligned(p.x, 16) && ((size_t)ldx * xsz) % 16 == 0 && (!norm_w || aligned(norm_w, 16));
     TmaMaps maps;
     const TmaPlan* tp = nullptr;
     if (pp.tma && encode_maps(p, bits, nacc, &pp.tp.geo, &maps)) {

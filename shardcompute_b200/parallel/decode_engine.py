@@ -15,7 +15,7 @@ worker/executor.py:229-325), re-laid for B200:
   the transport's limit); rank 0 folds the residual into its partial so the
   all-reduce output *is* the new hidden state; greedy sampling gathers only
   (max, index) per rank instead of the vocab-split logits;
-* the residual stream is fp32, GEMV inputs fp16, KV cache fp16
+* the residual stream and every GEMV input are fp32 (the GEMV splits them into exact fp16 hi / lo parts), KV cache fp16
   ``[L, 2, B, Hkv/TP, Lmax, hd]``, preallocated;
 * positions and token ids live in device buffers, so one decode step is
   captured once in a CUDA graph and replayed; each replay reads the token the
@@ -135,8 +135,10 @@ class DecodeEngine:
             "part": torch.zeros(M, self.H, dtype=torch.float32, device=dev),
             "qkv": torch.zeros(M, (self.Hq + 2 * self.Hkv) * self.hd, dtype=torch.float32, device=dev),
             "q": torch.zeros(M, self.Hq * self.hd, dtype=torch.float32, device=dev),
-            "attn": torch.zeros(M, self.Hq * self.hd, dtype=torch.float16, device=dev),
-            "act": torch.zeros(M, self.F, dtype=torch.float16, device=dev),
+            # GEMV inputs stay fp32: the factored GEMV splits them into exact fp16
+            # hi / lo parts, so only the fp16 KV cache rounds activations
+            "attn": torch.zeros(M, self.Hq * self.hd, dtype=torch.float32, device=dev),
+            "act": torch.zeros(M, self.F, dtype=torch.float32, device=dev),
             "hlast": torch.zeros(B, self.H, dtype=torch.float32, device=dev),
             "logits": torch.zeros(B, self.Vl, dtype=torch.float32, device=dev),
             "val": torch.zeros(B, dtype=torch.float32, device=dev),
