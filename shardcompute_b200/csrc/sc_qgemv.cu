@@ -1038,6 +1038,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   __shared__ float s_part[TC_NCW][4];
   __shared__ float s_rms[4];
   __shared__ __align__(8) uint64_t s_xready;  // consumers have staged x (lets the producer run on)
+  __shared__ __align__(16) uint4 s_zero[XQ * 4];  // B fragments of lanes that feed no column
 
   const int M = p.M;
   const int split = blockIdx.y;
@@ -1058,6 +1059,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   // their order, so every run (and every replay) gives the same bits.
   unsigned long long* s_acc = reinterpret_cast<unsigned long long*>(sbase + geo.acc_off);
   for (int i = tid; i < geo.acc_floats; i += blockDim.x) s_acc[i] = 0ull;
+  if (tid < XQ * 4) s_zero[tid] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) {
     for (int s = 0; s < geo.nst; ++s) {
       mbar_init(&full[s], 1);
@@ -1166,6 +1168,16 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   const int fo_x = warp * CB + bx_off;
   const int fo_t = warp * CB + M * 2 * XQ * 64 + t * 16;
 
+  // Kernel-constant geometry in registers, and this lane's operand addresses
+  // in stage 0 of the ring (stage s adds s * stage_bytes).
+  const int nst = geo.nst, cps = geo.cps;
+  const uint32_t stage_bytes = (uint32_t)geo.stage_bytes;
+  const uint32_t wset = (uint32_t)geo.wset_bytes, sset = (uint32_t)geo.sset_bytes;
+  const uint32_t ring_w = smem_u32(ring) + fo_w;                        // weight words, set 0
+  const uint32_t ring_s = smem_u32(ring) + NACC * wset + fo_s;         // scale word, set 0
+  // lanes whose B column is unused read zeros instead of branching
+  const uint32_t zero_x = smem_u32(s_zero);
+
   // A stage's weight words and raw scale / bias words of this lane.  The
   // SwiGLU pair keeps only its words a stage ahead (96 registers): its scales
   // and biases are read from the held slot when they are used.
@@ -1174,42 +1186,41 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     uint4 w0[NACC], w1[NACC];
     uint32_t sb[PIPE_SB ? NACC : 1][4];  // scale(row g), scale(row g+8), bias(row g), bias(row g+8)
   };
-  auto ld_sb_raw = [&](const unsigned char* sp) -> uint32_t {
-    if (NGC >= 2) return *reinterpret_cast<const uint32_t*>(sp);  // groups grpA, grpA + 1
-    return (uint32_t)*reinterpret_cast<const uint16_t*>(sp);
+  auto ld_sb_raw = [&](uint32_t sp) -> uint32_t {
+    if (NGC >= 2) return lds_u32(sp);  // groups grpA, grpA + 1
+    return lds_u16(sp);
   };
-  auto ld_sb4 = [&](uint32_t (&d)[4], const unsigned char* st, int a) {
-    const unsigned char* sst = st + NACC * geo.wset_bytes + (a * 2) * geo.sset_bytes;
-    d[0] = ld_sb_raw(sst + fo_s);
-    d[1] = ld_sb_raw(sst + fo_s + s_r8);
-    d[2] = ld_sb_raw(sst + geo.sset_bytes + fo_s);
-    d[3] = ld_sb_raw(sst + geo.sset_bytes + fo_s + s_r8);
+  auto ld_sb4 = [&](uint32_t (&d)[4], uint32_t soff, int a) {  // soff: stage byte offset
+    const uint32_t sp = ring_s + soff + (a * 2) * sset;
+    d[0] = ld_sb_raw(sp);
+    d[1] = ld_sb_raw(sp + s_r8);
+    d[2] = ld_sb_raw(sp + sset);
+    d[3] = ld_sb_raw(sp + sset + s_r8);
   };
   // A stage holds cps chunks (fewer than TC_NCW for a short K or a narrow
   // scale box): warps past them read nothing, their offsets would leave the stage.
-  const bool has_chunk = warp < geo.cps;
-  auto ld_stage = [&](StageRegs& d, const unsigned char* st) {
+  const bool has_chunk = warp < cps;
+  auto ld_stage = [&](StageRegs& d, uint32_t soff) {
 #pragma unroll
     for (int a = 0; a < NACC; ++a) {
       if (!has_chunk) {
         d.w0[a] = d.w1[a] = make_uint4(0u, 0u, 0u, 0u);
         continue;
       }
-      const unsigned char* wst = st + a * geo.wset_bytes;
-      d.w0[a] = *reinterpret_cast<const uint4*>(wst + fo_w);
-      d.w1[a] = *reinterpret_cast<const uint4*>(wst + fo_w + w_r8);
-      if (PIPE_SB) ld_sb4(d.sb[PIPE_SB ? a : 0], st, a);
+      const uint32_t wp = ring_w + soff + a * wset;
+      d.w0[a] = lds_v4(wp);
+      d.w1[a] = lds_v4(wp + w_r8);
+      if (PIPE_SB) ld_sb4(d.sb[PIPE_SB ? a : 0], soff, a);
     }
   };
   // (group grpA, group grpA + 1) of a raw scale / bias word
-  auto sb_lo = [](uint32_t r) { return __half2float(__ushort_as_half((uint16_t)(r & 0xffffu))); };
-  auto sb_hi = [](uint32_t r) {
-    return NGC >= 2 ? __half2float(__ushort_as_half((uint16_t)(r >> 16))) : __half2float(__ushort_as_half((uint16_t)(r & 0xffffu)));
-  };
+  auto sb_lo = [](uint32_t r) { return __low2float(u32_as_h2(r)); };
+  auto sb_hi = [](uint32_t r) { return NGC >= 2 ? __high2float(u32_as_h2(r)) : __low2float(u32_as_h2(r)); };
 
   // This CTA's tiles (blockIdx.x, + gridDim.x, ...) and the stages of each.
   const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int spt = (kc1 - kc0 + geo.cps - 1) / geo.cps;
+  const int kspan = kc1 - kc0;
+  const int spt = (kspan + cps - 1) / cps;
   const int nq = my_tiles * spt;
   int s = 0;
   uint32_t ph = 0;
@@ -1217,7 +1228,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   StageRegs cur;
   if (nq > 0) {
     if (mbar_wait_bounded(&full[0], 0, &s_abort, TC_WAIT_NS))
-      ld_stage(cur, ring);
+      ld_stage(cur, 0u);
     else
       aborted = true;
   }
@@ -1227,29 +1238,25 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
 #pragma unroll
     for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
   int kst = 0, tl = 0;  // stage within the tile, tile of this CTA
+  uint32_t xst = smem_u32(xsb);  // staged x of the current stage's first chunk
+  const uint32_t xbase = xst;
   for (int q = 0; q < nq && !aborted; ++q) {
-    const int kcs = kc0 + kst * geo.cps;
-    const bool act = warp < min(kc1 - kcs, geo.cps);
+    const bool act = warp < min(kspan - kst * cps, cps);
     // ---- MMAs of the current stage (registers loaded one stage ahead)
     float ca[NACC][4], cz[NACC][4];
     float4 tb = make_float4(0.f, 0.f, 0.f, 0.f);
     if (act) {
-      const unsigned char* xst = xsb + (size_t)(kcs - kc0) * CB;
+      const uint32_t xb = bact ? xst + fo_x : zero_x;
       uint32_t bfr[NMMA][2];
-      if (bact) {
 #pragma unroll
-        for (int qq = 0; qq < XQ; ++qq) {
-          const uint4 v = *reinterpret_cast<const uint4*>(xst + fo_x + qq * 64);
-          bfr[2 * qq][0] = v.x;
-          bfr[2 * qq][1] = v.y;
-          bfr[2 * qq + 1][0] = v.z;
-          bfr[2 * qq + 1][1] = v.w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < NMMA; ++i) bfr[i][0] = bfr[i][1] = 0u;
+      for (int qq = 0; qq < XQ; ++qq) {
+        const uint4 v = lds_v4(xb + qq * 64);
+        bfr[2 * qq][0] = v.x;
+        bfr[2 * qq][1] = v.y;
+        bfr[2 * qq + 1][0] = v.z;
+        bfr[2 * qq + 1][1] = v.w;
       }
-      tb = *reinterpret_cast<const float4*>(xst + fo_t);
+      tb = lds_f4(xst + fo_t);
 #pragma unroll
       for (int a = 0; a < NACC; ++a) {
         const uint32_t r0[4] = {cur.w0[a].x, cur.w0[a].y, cur.w0[a].z, cur.w0[a].w};
@@ -1278,7 +1285,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     }
     // ---- the next stage's registers load while those MMAs run
     const int s_cur = s;
-    if (++s == geo.nst) {
+    if (++s == nst) {
       s = 0;
       ph ^= 1;
     }
@@ -1286,7 +1293,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     const bool more = q + 1 < nq;
     if (more) {
       if (mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS))
-        ld_stage(nxt, ring + (size_t)s * geo.stage_bytes);
+        ld_stage(nxt, (uint32_t)s * stage_bytes);
       else
         aborted = true;
     }
@@ -1299,7 +1306,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
 #pragma unroll
           for (int i = 0; i < 4; ++i) sbv[i] = cur.sb[PIPE_SB ? a : 0][i];
         } else {
-          ld_sb4(sbv, ring + (size_t)s_cur * geo.stage_bytes, a);
+          ld_sb4(sbv, (uint32_t)s_cur * stage_bytes, a);
         }
         acc[a][0] = fmaf(sb_lo(sbv[0]), ca[a][0] + cz[a][0], fmaf(sb_lo(sbv[2]), tb.z, acc[a][0]));
         acc[a][1] = fmaf(sb_hi(sbv[0]), ca[a][1] + cz[a][1], fmaf(sb_hi(sbv[2]), tb.w, acc[a][1]));
@@ -1312,6 +1319,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     // ---- tile done for this warp: reduce over k-lanes, add into the CTA's tile accumulators
     if (++kst == spt) {
       kst = 0;
+      xst = xbase;
       const int m = t / NGC;
 #pragma unroll
       for (int a = 0; a < NACC; ++a) {
@@ -1329,6 +1337,8 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
         for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
       }
       ++tl;
+    } else {
+      xst += (uint32_t)(cps * CB);
     }
     if (more) cur = nxt;
   }
