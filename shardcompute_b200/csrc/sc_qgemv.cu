@@ -876,7 +876,7 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
 #pragma unroll
     for (int b = 0; b < FXS_UB; ++b) {
       const int u = b0 + b * nthreads + tid;
-      const int m = u / upm, k0 = kb + (u - m * upm) * 8;
+      const int m = M == 1 ? 0 : u / upm, k0 = kb + (u - m * upm) * 8;
       if (u < nu && k0 < p.K) {
         ld_x8<XT>(p, m, k0, v[b]);
       } else {
@@ -893,7 +893,7 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
 #pragma unroll
       for (int b = 0; b < FXS_UB; ++b) {
         const int u = b0 + b * nthreads + tid;
-        const int m = u < nu ? u / upm : 0;
+        const int m = (M == 1 || u >= nu) ? 0 : u / upm;
         float q = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) q = fmaf(v[b][i], v[b][i], q);
@@ -923,7 +923,7 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
       const int u = b0 + b * nthreads + tid;
       if (b0 + b * nthreads >= nu) break;  // warp-uniform: no unit of this slot anywhere
       const bool ok = u < nu;
-      const int m = ok ? u / upm : 0;
+      const int m = (M == 1 || !ok) ? 0 : u / upm;
       const int ul = ok ? u - m * upm : 0;
       const int k0 = kb + ul * 8;
       const int cl = ul / UPC, uc = ul % UPC;
@@ -1240,8 +1240,12 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   int kst = 0, tl = 0;  // stage within the tile, tile of this CTA
   uint32_t xst = smem_u32(xsb);  // staged x of the current stage's first chunk
   const uint32_t xbase = xst;
-  for (int q = 0; q < nq && !aborted; ++q) {
-    const bool act = warp < min(kspan - kst * cps, cps);
+  const int last_nch = kspan - (spt - 1) * cps;  // chunks in a tile's last stage
+  // One stage: MMAs on `cur`, the next stage's operands into `nxt`.  With one
+  // weight set the loop runs two stages per trip with the register sets
+  // swapped, so no copies.
+  auto stage = [&](int q, StageRegs& cur, StageRegs& nxt) {
+    const bool act = kst == spt - 1 ? warp < last_nch : has_chunk;
     // ---- MMAs of the current stage (registers loaded one stage ahead)
     float ca[NACC][4], cz[NACC][4];
     float4 tb = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1289,7 +1293,6 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       s = 0;
       ph ^= 1;
     }
-    StageRegs nxt;
     const bool more = q + 1 < nq;
     if (more) {
       if (mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS))
@@ -1340,7 +1343,18 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     } else {
       xst += (uint32_t)(cps * CB);
     }
-    if (more) cur = nxt;
+  };
+  StageRegs alt;
+  if constexpr (NACC == 1) {
+    for (int q = 0; q < nq && !aborted; q += 2) {
+      stage(q, cur, alt);
+      if (q + 1 < nq && !aborted) stage(q + 1, alt, cur);
+    }
+  } else {  // the SwiGLU pair has no registers for a second set: one stage per trip
+    for (int q = 0; q < nq && !aborted; ++q) {
+      stage(q, cur, alt);
+      cur = alt;
+    }
   }
   if (aborted && lane == 0) atomicExch(&g_qgemv_error, 1);
   // ---- all warps' partial sums are in: the epilogue of every tile of this CTA
