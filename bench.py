@@ -63,12 +63,63 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: build this many decoder layers instead of the model's")
+    ap.add_argument("--kernel-gemv", default="",
+                    help="profiling only: N,K,epilogue (store|residual|swiglu) -- time --steps launches of one "
+                         "decode GEMV over 5 rotating weight sets and print one JSON line")
     return ap.parse_args()
+
+
+def run_gemv(args) -> int:
+    """Isolated decode-GEMV launches (the shape an ncu capture of the top kernel uses)."""
+    from shardcompute_b200 import _lib as L
+    from shardcompute_b200 import ops
+
+    n, k, mode = args.kernel_gemv.split(",")
+    N, K = int(n), int(k)
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    nseg = 2 if mode == "swiglu" else 1
+    ws = [[ops.quantize((torch.randn(N, K, device=dev) * 0.02).half(), args.group, args.bits) for _ in range(nseg)]
+          for _ in range(5)]
+    x = torch.randn(1, K, device=dev)
+    nw = torch.ones(K, device=dev, dtype=torch.float16) if mode != "residual" else None
+    y = torch.zeros(1, N, device=dev, dtype=torch.float32)
+
+    def one(i):
+        segs = ws[i % 5]
+        if mode == "swiglu":
+            ops.qlinear_fused(x, segs, args.group, args.bits, epilogue=L.SC_EPI_SWIGLU, norm_weight=nw, out=y)
+        elif mode == "residual":
+            ops.qlinear_fused(x, segs, args.group, args.bits, epilogue=L.SC_EPI_RESIDUAL, residual=y, out=y)
+        else:
+            ops.qlinear_fused(x, segs, args.group, args.bits, norm_weight=nw, out=y)
+
+    for i in range(args.warmup):
+        one(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        one(i)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    nbytes = nseg * (N * K * args.bits // 8 + N * (K // args.group) * 4) + K * 4 + N * 4
+    print(json.dumps({"kernel": "qgemv_fx", "N": N, "K": K, "epilogue": mode, "us_per_launch": us,
+                      "algorithmic_bytes": nbytes, "GB/s": nbytes / us / 1e3,
+                      "device_error": L.load().sc_qgemv_device_error(1)}), flush=True)
+    return 0
 
 
 def dist_env():
     return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
             int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# DRAM bytes (read + written) of the GEMV launches of one decode step, from the
+# ncu launch-list capture summarised in profiles/decode_step_llama3-8b_tp1_launches.md
+# (dram__bytes_read.sum + dram__bytes_write.sum, timed graph replays only).
+NCU_GEMV_TRAFFIC = {("llama3-8b", 1, 1, 4, 64, 2048): 4236.5e6}
 
 
 def load_peaks():
@@ -209,6 +260,8 @@ def main():
         return 2
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.kernel_gemv:
+        return run_gemv(args)
     if args.warmup < 3:
         print("--warmup must be >= 3", file=sys.stderr)
         return 2
@@ -312,7 +365,8 @@ def main():
     gemv_share = g_ms / args.steps / ms_step
     roofline = {"bound": "hbm", "kernel": "qgemv_tma (fused RMSNorm/dequant-GEMV/epilogue)", "achieved": achieved,
                 "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": None, "launches_per_step": g_n // args.steps,
+                "traffic": NCU_GEMV_TRAFFIC.get((args.model, world, args.batch, args.bits, args.group, args.ctx)),
+                "traffic_unit": "bytes per step (ncu capture, profiles/)", "launches_per_step": g_n // args.steps,
                 "algorithmic_bytes_per_step": g_bytes // args.steps, "ms_per_step": g_ms / args.steps,
                 "share_of_step": gemv_share}
     step_bytes = g_bytes / args.steps + eng.kv_bytes_per_step()

@@ -209,6 +209,11 @@ int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_c
  *   tickets: int32 [B*Hkv], zero before the first call and left zero by
  *   every call (the split merge counts arrivals in it). */
 size_t sc_attn_decode_workspace_bytes(int B, int Hq, int hd, int splits);
+/* Device-side error word of sc_attn_decode: nonzero after a CTA gave up
+ * waiting for its K/V tiles (bounded wait; its output is then undefined).
+ * Synchronises with the device; reset != 0 clears it.  No reference
+ * counterpart. */
+int sc_attn_device_error(int reset);
 int sc_attn_decode(const float* qkv, int B, int Hq, int Hkv, int hd, const int32_t* pos,
                    const float* cos_tab, const float* sin_tab, int max_pos,
                    uint16_t* k_cache, uint16_t* v_cache, int Lmax, float scale, int splits,

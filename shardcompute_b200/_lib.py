@@ -50,6 +50,7 @@ SIGNATURES = {
     "sc_flash_decode_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "sc_flash_decode": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _i, _vp, _sz, _vp]),
     "sc_attn_decode_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "sc_attn_device_error": (_i, [_i]),
     "sc_attn_decode": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _f, _i, _vp, _i, _vp, _sz, _vp,
                             _vp]),
     "sc_rmsnorm": (_i, [_vp, _i, _i, _i, _vp, _f, _vp, _i, _vp]),

@@ -281,15 +281,30 @@ static int dispatch_g(int G, const float* q, const __half* kc, const __half* vc,
 // k, append of k and v to the cache, split-KV online softmax over the cache,
 // and the merge of the splits -- one launch instead of three.
 //
-// grid (splits, Hkv, B), FD_WARPS warps.  Every CTA rotates its G query
-// heads itself (they are a few hundred floats); the CTA whose key range
-// holds the new position also rotates the new k, writes k and v into the
-// cache and uses those fp16 values for that key directly.  Each warp walks
-// its keys in batches of AD_BATCH warp-steps whose K/V loads are all issued
-// before any is used (the decode step is latency-bound, not bandwidth-bound,
-// at these sizes).  Partials go to the workspace; the last CTA of a
-// (sequence, kv head) -- an atomic ticket per pair -- merges the splits and
-// writes the output, then resets its ticket to zero for the next call.
+// grid (splits, Hkv, B), AD_WARPS warps.  A CTA's keys are one contiguous
+// range of the cache ([B][Hkv][Lmax][hd] rows), so they stream into shared
+// memory as 1-D bulk copies of AD_TK keys (K and V), AD_NB tiles in flight,
+// issued before anything else so the HBM latency overlaps the rotation work.
+// Every CTA rotates its G query heads itself (a few hundred floats); the CTA
+// whose key range holds the new position also rotates the new k, writes k
+// and v into the cache and uses those fp16 values for that key (its tile's
+// copy of that row may predate the write).  Partials go to the workspace; the
+// last CTA of a (sequence, kv head) -- an atomic ticket per pair -- merges the
+// splits and writes the output, then resets its ticket to zero for the next
+// call.  Tile waits are bounded; a timeout raises g_attn_error and the CTA
+// stops computing (its output is undefined).
+
+constexpr int AD_WARPS = 8;
+constexpr int AD_TK = 64;  // keys per tile
+constexpr int AD_NB = 2;   // tiles in flight
+__device__ int g_attn_error = 0;
+
+__host__ __device__ constexpr int ad_groups(int hd) { return AD_WARPS * (32 / (hd / 8)); }  // lane groups of a CTA
+__host__ __device__ constexpr size_t ad_kv_bytes(int hd) { return (size_t)AD_NB * 2 * AD_TK * hd * 2; }
+__host__ __device__ constexpr size_t ad_smem_bytes(int hd, int G) {
+  // the tile buffers, reused after the last tile for the lane groups' partial outputs
+  return ad_kv_bytes(hd) > (size_t)ad_groups(hd) * G * hd * 4 ? ad_kv_bytes(hd) : (size_t)ad_groups(hd) * G * hd * 4;
+}
 
 template <int HD>
 __device__ __forceinline__ void rope_pair(float x1, float x2, float c, float sn, float& o1, float& o2) {
@@ -299,7 +314,7 @@ __device__ __forceinline__ void rope_pair(float x1, float x2, float c, float sn,
 }
 
 template <int HD, int G, typename OT>
-__global__ void __launch_bounds__(FD_WARPS * 32)
+__global__ void __launch_bounds__(AD_WARPS * 32)
 attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ pos_ptr,
                    const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int max_pos, int Hq,
                    int Hkv, int Lmax, float scale, int splits, __half* __restrict__ kc, __half* __restrict__ vc,
@@ -309,7 +324,9 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   constexpr int LPK = HD / 8;    // lanes per key (8 halves each)
   constexpr int KPS = 32 / LPK;  // keys per warp step
   constexpr int HALF = HD / 2;
-  constexpr int AD_BATCH = G >= 8 ? 2 : 4;  // warp steps whose loads are in flight together
+  constexpr int NT = AD_WARPS * 32;
+  constexpr int STEP = AD_WARPS * KPS;  // keys per CTA step
+  constexpr int NGRP = ad_groups(HD);
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPK, dl = lane % LPK;
@@ -319,16 +336,40 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   const bool append = pos >= 0 && pos < Lmax && pos < max_pos;
   const int L = append ? pos + 1 : min(max(pos, 0), Lmax);
   const int chunk = (L + splits - 1) / splits;
-  const int k_beg = split * chunk;
+  const int k_beg = min(L, split * chunk);
   const int k_end = min(L, k_beg + chunk);
+  const int ntiles = (k_end - k_beg + AD_TK - 1) / AD_TK;
   const bool owner = append && pos >= k_beg && pos < k_end;
   const int width = (Hq + 2 * Hkv) * HD;
   const float* src = qkv + (size_t)b * width;
+  const __half* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  const __half* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
 
+  extern __shared__ __align__(128) unsigned char ad_smem[];
+  __half* s_kv = reinterpret_cast<__half*>(ad_smem);  // [AD_NB][2][AD_TK][HD]
+  __shared__ __align__(8) uint64_t s_full[AD_NB];
+  __shared__ int s_abort;
   __shared__ float s_q[G][HD];
   __shared__ __align__(16) __half s_knew[HD], s_vnew[HD];
-  // rotated queries (and, for the owner, the new key / value)
-  for (int e = threadIdx.x; e < G * HALF; e += FD_WARPS * 32) {
+
+  auto issue = [&](int t) {  // thread 0: bulk copies of tile t's K and V rows
+    const int kt = k_beg + t * AD_TK;
+    const uint32_t bytes = (uint32_t)(min(AD_TK, k_end - kt) * HD * 2);
+    const int bi = t % AD_NB;
+    __half* dk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
+    mbar_arrive_expect_tx(&s_full[bi], 2 * bytes);
+    bulk_load(dk, kbase + (size_t)kt * HD, bytes, &s_full[bi]);
+    bulk_load(dk + AD_TK * HD, vbase + (size_t)kt * HD, bytes, &s_full[bi]);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < AD_NB; ++i) mbar_init(&s_full[i], 1);
+    s_abort = 0;
+    fence_mbar_init();
+    for (int t = 0; t < min(AD_NB, ntiles); ++t) issue(t);
+  }
+
+  // rotated queries (and, for the owner, the new key / value) while the tiles stream in
+  for (int e = threadIdx.x; e < G * HALF; e += NT) {
     const int g = e / HALF, d = e % HALF;
     const float* qh = src + (size_t)(kvh * G + g) * HD;
     float o1 = qh[d], o2 = qh[d + HALF];
@@ -342,7 +383,7 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
     const float* vh = src + (size_t)(Hq + Hkv + kvh) * HD;
     __half* kdst = kc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
     __half* vdst = vc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
-    for (int d = threadIdx.x; d < HALF; d += FD_WARPS * 32) {
+    for (int d = threadIdx.x; d < HALF; d += NT) {
       float o1, o2;
       rope_pair<HD>(kh[d], kh[d + HALF], cos_tab[(size_t)pos * HALF + d], sin_tab[(size_t)pos * HALF + d], o1, o2);
       const __half h1 = __float2half_rn(o1), h2 = __float2half_rn(o2);
@@ -351,7 +392,7 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
       kdst[d] = h1;
       kdst[d + HALF] = h2;
     }
-    for (int d = threadIdx.x; d < HD; d += FD_WARPS * 32) {
+    for (int d = threadIdx.x; d < HD; d += NT) {
       const __half hv = __float2half_rn(vh[d]);
       s_vnew[d] = hv;
       vdst[d] = hv;
@@ -372,32 +413,29 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
   }
-  const __half* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
-  const __half* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
-  constexpr int STEP = FD_WARPS * KPS;  // keys per CTA step
-  for (int k0 = k_beg + warp * KPS; k0 < k_end; k0 += STEP * AD_BATCH) {
-    uint4 kv4[AD_BATCH], vv4[AD_BATCH];
-#pragma unroll
-    for (int j = 0; j < AD_BATCH; ++j) {
-      const int key = k0 + j * STEP + sub;
-      kv4[j] = vv4[j] = make_uint4(0, 0, 0, 0);
-      if (key < k_end) {
-        if (owner && key == pos) {
-          kv4[j] = *reinterpret_cast<const uint4*>(s_knew + d0);
-          vv4[j] = *reinterpret_cast<const uint4*>(s_vnew + d0);
-        } else {
-          kv4[j] = *reinterpret_cast<const uint4*>(kbase + (size_t)key * HD + d0);
-          vv4[j] = *reinterpret_cast<const uint4*>(vbase + (size_t)key * HD + d0);
-        }
+  int t = 0;
+  for (; t < ntiles; ++t) {
+    const int bi = t % AD_NB;
+    mbar_wait_bounded(&s_full[bi], (t / AD_NB) & 1, &s_abort, 1000000000ull);  // a timeout raises s_abort
+    __syncthreads();  // every thread's wait has ended: the abort decision below is uniform
+    if (s_abort) break;
+    const int kt = k_beg + t * AD_TK;
+    const int nk = min(AD_TK, k_end - kt);
+    const __half* tk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
+    const __half* tv = tk + AD_TK * HD;
+#pragma unroll 2
+    for (int kk = warp * KPS + sub; kk < AD_TK; kk += STEP) {
+      const bool valid = kk < nk;
+      const int key = kt + kk;
+      uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        const bool fresh = owner && key == pos;
+        kv4 = *reinterpret_cast<const uint4*>((fresh ? s_knew : tk + (size_t)kk * HD) + d0);
+        vv4 = *reinterpret_cast<const uint4*>((fresh ? s_vnew : tv + (size_t)kk * HD) + d0);
       }
-    }
-#pragma unroll
-    for (int j = 0; j < AD_BATCH; ++j) {
-      const int key = k0 + j * STEP + sub;
-      const bool valid = key < k_end;
       float kf[8], vf[8];
-      const uint32_t kw[4] = {kv4[j].x, kv4[j].y, kv4[j].z, kv4[j].w};
-      const uint32_t vw[4] = {vv4[j].x, vv4[j].y, vv4[j].z, vv4[j].w};
+      const uint32_t kw[4] = {kv4.x, kv4.y, kv4.z, kv4.w};
+      const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 a = __half22float2(u32_as_h2(kw[i]));
@@ -424,11 +462,24 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
         }
       }
     }
+    __syncthreads();  // every warp is done with buffer bi
+    if (threadIdx.x == 0 && t + AD_NB < ntiles) issue(t + AD_NB);
+  }
+  if (s_abort) {
+    if (threadIdx.x == 0) {
+      atomicExch(&g_attn_error, 1);
+      // let the copies still in flight (tiles t .. t + AD_NB - 1) land before the CTA exits
+      for (int u = t; u < min(t + AD_NB, ntiles); ++u) {
+        int dummy = 0;
+        mbar_wait_bounded(&s_full[u % AD_NB], (u / AD_NB) & 1, (volatile int*)&dummy, 250000000ull);
+      }
+    }
+    return;  // every thread returns: no barrier below is left waiting
   }
 
-  // merge the lane groups of the CTA
-  __shared__ float sm_m[FD_WARPS * KPS][G], sm_l[FD_WARPS * KPS][G];
-  __shared__ float sm_o[FD_WARPS * KPS][G][HD];
+  // merge the lane groups of the CTA (their outputs reuse the tile buffers)
+  __shared__ float sm_m[NGRP][G], sm_l[NGRP][G];
+  float* sm_o = reinterpret_cast<float*>(ad_smem);  // [NGRP][G][HD]
   const int grp = warp * KPS + sub;
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -437,20 +488,20 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
       sm_l[grp][g] = l[g];
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sm_o[grp][g][d0 + i] = o[g][i];
+    for (int i = 0; i < 8; ++i) sm_o[((size_t)grp * G + g) * HD + d0 + i] = o[g][i];
   }
   __syncthreads();
   float* pbase = part + (((size_t)b * Hkv + kvh) * splits) * G * (HD + 2);
-  for (int e = threadIdx.x; e < G * HD; e += FD_WARPS * 32) {
+  for (int e = threadIdx.x; e < G * HD; e += NT) {
     const int g = e / HD, d = e % HD;
     float M = -INFINITY;
-    for (int r = 0; r < FD_WARPS * KPS; ++r) M = fmaxf(M, sm_m[r][g]);
+    for (int r = 0; r < NGRP; ++r) M = fmaxf(M, sm_m[r][g]);
     float Ls = 0.f, O = 0.f;
     if (M != -INFINITY) {
-      for (int r = 0; r < FD_WARPS * KPS; ++r) {
+      for (int r = 0; r < NGRP; ++r) {
         const float w = expf(sm_m[r][g] - M);
         Ls = fmaf(sm_l[r][g], w, Ls);
-        O = fmaf(sm_o[r][g][d], w, O);
+        O = fmaf(sm_o[((size_t)r * G + g) * HD + d], w, O);
       }
     }
     if (splits == 1) {
@@ -471,15 +522,15 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const int t = atomicAdd(&tickets[b * Hkv + kvh], 1);
-    s_last = (t == splits - 1);
+    const int tk = atomicAdd(&tickets[b * Hkv + kvh], 1);
+    s_last = (tk == splits - 1);
     if (s_last) __threadfence();
   }
   __syncthreads();
   if (!s_last) return;
   __shared__ float s_w[FD_MAX_SPLITS][G], s_l[FD_MAX_SPLITS][G], s_inv[G];
-  merge_partials<HD, G, FD_WARPS * 32, OT>(pbase, (size_t)G * (HD + 2), HD + 2, splits,
-                                           out + (size_t)b * Hq * HD + (size_t)kvh * G * HD, s_w, s_l, s_inv);
+  merge_partials<HD, G, NT, OT>(pbase, (size_t)G * (HD + 2), HD + 2, splits,
+                                out + (size_t)b * Hq * HD + (size_t)kvh * G * HD, s_w, s_l, s_inv);
   if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
 }
 
@@ -487,8 +538,15 @@ template <int HD, int G, typename OT>
 static int launch_ad(const float* qkv, const int32_t* pos, const float* cos_tab, const float* sin_tab, int max_pos,
                      int B, int Hq, int Hkv, int Lmax, float scale, int splits, __half* kc, __half* vc, float* part,
                      int* tickets, OT* out, cudaStream_t stream) {
-  ::sc::launch(attn_decode_kernel<HD, G, OT>, dim3(splits, Hkv, B), FD_WARPS * 32, 0, stream, qkv, pos, cos_tab,
-               sin_tab, max_pos, Hq, Hkv, Lmax, scale, splits, kc, vc, part, tickets, out);
+  auto kern = attn_decode_kernel<HD, G, OT>;
+  const size_t smem = ad_smem_bytes(HD, G);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = true;
+  }
+  ::sc::launch(kern, dim3(splits, Hkv, B), AD_WARPS * 32, smem, stream, qkv, pos, cos_tab, sin_tab, max_pos, Hq, Hkv,
+               Lmax, scale, splits, kc, vc, part, tickets, out);
   return check_launch("attn_decode");
 }
 
@@ -559,6 +617,16 @@ int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_c
 size_t sc_attn_decode_workspace_bytes(int B, int Hq, int hd, int splits) {
   if (splits <= 1) return 0;
   return (size_t)B * Hq * splits * (hd + 2) * sizeof(float);
+}
+
+int sc_attn_device_error(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, sc::g_attn_error, sizeof(int));
+  if (reset) {
+    const int z = 0;
+    cudaMemcpyToSymbol(sc::g_attn_error, &z, sizeof(int));
+  }
+  return v;
 }
 
 int sc_attn_decode(const float* qkv, int B, int Hq, int Hkv, int hd, const int32_t* pos, const float* cos_tab,

@@ -84,6 +84,8 @@ class DecodeEngine:
         self.tok = torch.zeros(self.B, dtype=torch.int32, device=dev)  # decode input / sampled output
         self.tickets = torch.zeros(self.B * self.Hkv, dtype=torch.int32, device=dev)  # attention split merge
         self.fused_attn = os.environ.get("SC_ATTN_FUSED", "1") != "0"
+        if attn_splits is None and os.environ.get("SC_ATTN_SPLITS"):
+            attn_splits = int(os.environ["SC_ATTN_SPLITS"])
         if attn_splits is None:
             attn_splits = max(1, min(64, math.ceil(2 * 148 / max(1, self.Hkv * self.B)), math.ceil(self.Lmax / 64)))
         self.splits = attn_splits
