@@ -872,6 +872,7 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
   const int kb = kc0 * TR::KPC;
   const int nbatch = (nu + FXS_UB * nthreads - 1) / (FXS_UB * nthreads);
   float v[FXS_UB][8];
+  uint4 nwr[NORM ? FXS_UB : 1];  // raw fp16 norm weights of each unit, loaded with x (one round trip)
   auto load_batch = [&](int b0) {
 #pragma unroll
     for (int b = 0; b < FXS_UB; ++b) {
@@ -879,9 +880,16 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
       const int m = M == 1 ? 0 : u / upm, k0 = kb + (u - m * upm) * 8;
       if (u < nu && k0 < p.K) {
         ld_x8<XT>(p, m, k0, v[b]);
+        if (NORM) {
+          const uint16_t* nwp = p.norm_w + k0;
+          nwr[NORM ? b : 0] = p.x_vec ? *reinterpret_cast<const uint4*>(nwp)
+                                      : make_uint4(nwp[0] | ((uint32_t)nwp[1] << 16), nwp[2] | ((uint32_t)nwp[3] << 16),
+                                                   nwp[4] | ((uint32_t)nwp[5] << 16), nwp[6] | ((uint32_t)nwp[7] << 16));
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[b][i] = 0.f;
+        if (NORM) nwr[NORM ? b : 0] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
   };
@@ -930,23 +938,15 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
       float x[8];
       if (NORM) {
         float nw[8];
-        if (ok && k0 < p.K) {
-          if (p.x_vec) {
-            const uint4 nwv = *reinterpret_cast<const uint4*>(p.norm_w + k0);
-            const uint32_t nww[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
+        {
+          const uint4 nwv = nwr[NORM ? b : 0];
+          const uint32_t nww[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float2 f = __half22float2(u32_as_h2(nww[i]));
-              nw[2 * i] = f.x;
-              nw[2 * i + 1] = f.y;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) nw[i] = __half2float(__ushort_as_half(p.norm_w[k0 + i]));
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(u32_as_h2(nww[i]));
+            nw[2 * i] = f.x;
+            nw[2 * i + 1] = f.y;
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) nw[i] = 0.f;
         }
         const float r = s_rms[m];
 #pragma unroll
@@ -1134,6 +1134,20 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   // ============================ consumers ============================
   const int g = lane >> 2, t = lane & 3;
   pdl_wait();
+  // The epilogue's global reads (residual, bias) do not depend on this
+  // kernel's results: when every consumer thread owns at most one output of
+  // the CTA, issue them now, beside the x loads, so the kernel ends in writes.
+  const int n_out = (int)blockIdx.x < p.tiles ? ((p.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1) * 16 * M : 0;
+  const bool pre_epi = !DUAL && p.splits == 1 && !geo.atomic_out && n_out <= NC;
+  float pre_bias = 0.f, pre_res = 0.f;
+  if (pre_epi && tid < n_out) {
+    const int rl = (tid % (16 * M)) / M, mm = tid % M;
+    const int row = ((int)blockIdx.x + (tid / (16 * M)) * (int)gridDim.x) * 16 + rl;
+    if (row < p.N) {
+      if (p.bias) pre_bias = __half2float(__ushort_as_half(p.bias[row]));
+      if (EPI == SC_EPI_RESIDUAL) pre_res = p.residual[(size_t)mm * p.ldr + row];
+    }
+  }
   stage_x_fx<BITS, NGC, NORM, XT>(p, xsb, s_part, s_rms, kc0, kc1, tid, NC, 1);
   if (tid == 0) mbar_arrive(&s_xready);
   const int CB = fx_chunk_bytes(BITS, M);
@@ -1368,7 +1382,11 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     float v[2];
 #pragma unroll
     for (int a = 0; a < NACC; ++a) v[a] = fx_from_fixed(s_acc[idx * NACC + a]);
-    if (row < p.N) epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, mm, v);
+    if (row >= p.N) continue;
+    if (pre_epi)  // bias / residual already read; same sums, same order as epilogue()
+      reinterpret_cast<YT*>(p.y)[(size_t)mm * p.ldy + row] = from_f32<YT>((v[0] + pre_bias) + pre_res);
+    else
+      epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, mm, v);
   }
 }
 
