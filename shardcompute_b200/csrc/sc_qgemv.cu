@@ -847,38 +847,65 @@ __device__ __forceinline__ void ld_x8(const QGemvParams& p, int m, int k0, float
   }
 }
 
-// Stage normalised x for chunks [kc0, kc1) (consumer threads only).
-// Work unit: 8 consecutive values of one row m -- one packed word at 4 bits,
-// two at 8 bits -- which fill exactly one 16-byte B-fragment unit per part
-// (hi / lo).  Consecutive lanes take consecutive units, so a column-group's
-// units sit in aligned lane groups and its sums reduce by shuffles.  A thread
-// loads all its units (up to FXS_UB per batch) before using any, and with
-// RMSNorm keeps them in registers across the norm reduction when one batch
-// covers the slice (one L2 round trip instead of two).
-constexpr int FXS_UB = 4;
+// Per-warp x staging for the factored kernel: consumer warp w stages exactly
+// the chunks it consumes (w, w + cps, w + 2 cps, ... of the K slice), so it
+// needs no CTA barrier before its first stage -- a __syncwarp orders its own
+// lanes' writes.  Lanes take (chunk, unit) pairs, UPC units per chunk, so a
+// column-group's units are an aligned lane group and its sums reduce by
+// shuffles.  With RMSNorm the staged values are x * norm_weight (unscaled):
+// the product is linear in x, so the kernel divides its outputs by the row's
+// rms at the end instead; this warp's share of sum(x^2) over the whole row
+// (a contiguous K / TC_NCW slice, whatever K slice the CTA stages) goes to
+// s_ss[warp][m] and is summed in warp order at the end (deterministic).
+constexpr int FXW_PASSES = 4;  // (chunk, unit) passes a warp keeps in registers per batch
 
 template <int BITS, int NGC, bool NORM, typename XT>
-__device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* xsb, float (*s_part)[4], float* s_rms,
-                                           int kc0, int kc1, int tid, int nthreads, int bar_id) {
+__device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned char* xsb, float (*s_ss)[4],
+                                                int kc0, int kc1, int cps, int warp, int lane) {
   using TR = QTraits<BITS>;
   constexpr int XQ = TR::NMMA / 2;
   constexpr int UPC = TR::KPC / 8;       // units per chunk
   constexpr int GU = TR::KPC / NGC / 8;  // units of one column-group inside a chunk (>= 4)
+  constexpr int CPP = 32 / UPC;          // chunks per pass
   const int M = p.M;
-  const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
   const int CB = fx_chunk_bytes(BITS, M);
-  const int upm = (kc1 - kc0) * UPC;  // units per row of x
-  const int nu = upm * M;
-  const int kb = kc0 * TR::KPC;
-  const int nbatch = (nu + FXS_UB * nthreads - 1) / (FXS_UB * nthreads);
-  float v[FXS_UB][8];
-  uint4 nwr[NORM ? FXS_UB : 1];  // raw fp16 norm weights of each unit, loaded with x (one round trip)
-  auto load_batch = [&](int b0) {
+  const int nkc = kc1 - kc0;
+  // this warp's chunks: cl = warp + j * cps (the consumer of chunk cl is warp cl % cps)
+  const int nj = (warp < cps && warp < nkc) ? (nkc - warp + cps - 1) / cps : 0;
+  const int npass = (nj + CPP - 1) / CPP * M;                     // (pass, row) items
+  const int jl = lane / UPC, uc = lane % UPC;                      // chunk within a pass, unit
+  if (NORM) {
+    // sum(x^2) over this warp's contiguous slice of the full row, 8 values per lane per step
+    const int per = ((p.K + TC_NCW - 1) / TC_NCW + 7) / 8 * 8;  // 8-aligned slices: vector loads
+    const int k_lo = min(p.K, warp * per), k_hi = min(p.K, k_lo + per);
+    for (int m = 0; m < M; ++m) {
+      float ss = 0.f;
+      for (int k0 = k_lo + lane * 8; k0 < k_hi; k0 += 256) {
+        float v[8];
+        if (k0 + 8 <= k_hi) {
+          ld_x8<XT>(p, m, k0, v);
+        } else {
 #pragma unroll
-    for (int b = 0; b < FXS_UB; ++b) {
-      const int u = b0 + b * nthreads + tid;
-      const int m = M == 1 ? 0 : u / upm, k0 = kb + (u - m * upm) * 8;
-      if (u < nu && k0 < p.K) {
+          for (int i = 0; i < 8; ++i) v[i] = k0 + i < k_hi ? ld_x<XT>(p.x, (size_t)m * p.ldx + k0 + i) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) s_ss[warp][m] = ss;
+    }
+  }
+  for (int it0 = 0; it0 < npass; it0 += FXW_PASSES) {
+    float v[FXW_PASSES][8];
+    uint4 nwr[NORM ? FXW_PASSES : 1];
+#pragma unroll
+    for (int b = 0; b < FXW_PASSES; ++b) {
+      const int it = it0 + b;
+      const int m = it % M, j = (it / M) * CPP + jl;
+      const int cl = warp + j * cps;
+      const int k0 = (kc0 + cl) * TR::KPC + uc * 8;
+      if (it < npass && j < nj && k0 < p.K) {
         ld_x8<XT>(p, m, k0, v[b]);
         if (NORM) {
           const uint16_t* nwp = p.norm_w + k0;
@@ -892,79 +919,33 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
         if (NORM) nwr[NORM ? b : 0] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-  };
-  if (NORM) {
-    float ss[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int bi = 0; bi < nbatch; ++bi) {
-      const int b0 = bi * FXS_UB * nthreads;
-      load_batch(b0);
 #pragma unroll
-      for (int b = 0; b < FXS_UB; ++b) {
-        const int u = b0 + b * nthreads + tid;
-        const int m = (M == 1 || u >= nu) ? 0 : u / upm;
-        float q = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) q = fmaf(v[b][i], v[b][i], q);
-#pragma unroll
-        for (int mm = 0; mm < 4; ++mm) ss[mm] += (mm == m) ? q : 0.f;
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-#pragma unroll
-      for (int o = 16; o; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
-      if (lane == 0) s_part[warp][m] = ss[m];
-    }
-    named_bar_sync(bar_id, nthreads);
-    if (tid < M) {
-      float sum = 0.f;
-      for (int w = 0; w < nwarps; ++w) sum += s_part[w][tid];
-      s_rms[tid] = sqrtf(sum / (float)p.K + p.eps);
-    }
-    named_bar_sync(bar_id, nthreads);
-  }
-  for (int bi = 0; bi < nbatch; ++bi) {
-    const int b0 = bi * FXS_UB * nthreads;
-    if (!NORM || nbatch > 1) load_batch(b0);
-#pragma unroll
-    for (int b = 0; b < FXS_UB; ++b) {
-      const int u = b0 + b * nthreads + tid;
-      if (b0 + b * nthreads >= nu) break;  // warp-uniform: no unit of this slot anywhere
-      const bool ok = u < nu;
-      const int m = (M == 1 || !ok) ? 0 : u / upm;
-      const int ul = ok ? u - m * upm : 0;
-      const int k0 = kb + ul * 8;
-      const int cl = ul / UPC, uc = ul % UPC;
+    for (int b = 0; b < FXW_PASSES; ++b) {
+      const int it = it0 + b;
+      if (it >= npass) break;  // warp-uniform
+      const int m = it % M, j = (it / M) * CPP + jl;
+      const bool ok = j < nj;
+      const int cl = warp + (ok ? j : 0) * cps;
       float x[8];
       if (NORM) {
-        float nw[8];
-        {
-          const uint4 nwv = nwr[NORM ? b : 0];
-          const uint32_t nww[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
+        const uint32_t nww[4] = {nwr[NORM ? b : 0].x, nwr[NORM ? b : 0].y, nwr[NORM ? b : 0].z, nwr[NORM ? b : 0].w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(u32_as_h2(nww[i]));
-            nw[2 * i] = f.x;
-            nw[2 * i + 1] = f.y;
-          }
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(u32_as_h2(nww[i]));
+          x[2 * i] = v[b][2 * i] * f.x;
+          x[2 * i + 1] = v[b][2 * i + 1] * f.y;
         }
-        const float r = s_rms[m];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = (v[b][i] / r) * nw[i];
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) x[i] = v[b][i];
       }
-      // hi / lo halves in B-fragment order: 4-bit [x0 x4 x1 x5 x2 x6 x3 x7]
-      // (odd codes arrive as 16 q, so their slots carry x / 16), 8-bit
-      // [x0 x2 x1 x3 x4 x6 x5 x7]
       __half hi[8], lo[8];
       float sh = 0.f, sl = 0.f, sx = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         __half h = __float2half_rn(x[e]);
         __half l = __float2half_rn(x[e] - __half2float(h));
-        if (BITS == 4 && (e & 1)) {
+        if (BITS == 4 && (e & 1)) {  // odd codes arrive as 16 q: their x slots carry x / 16
           h = __hmul(h, __float2half_rn(0.0625f));
           l = __hmul(l, __float2half_rn(0.0625f));
         }
@@ -976,7 +957,6 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
         hi[pos] = h;
         lo[pos] = l;
       }
-      // reduce over the lanes of one column-group (aligned lane groups of GU)
 #pragma unroll
       for (int o = 1; o < GU; o <<= 1) {
         sh += __shfl_xor_sync(0xffffffffu, sh, o);
@@ -995,32 +975,30 @@ __device__ __forceinline__ void stage_x_fx(const QGemvParams& p, unsigned char* 
         o.y = h2_as_u32(__halves2half2(src[2], src[3]));
         o.z = h2_as_u32(__halves2half2(src[4], src[5]));
         o.w = h2_as_u32(__halves2half2(src[6], src[7]));
-        const int unit = ((m * 2 + part) * XQ + q) * 4 + t;
-        *reinterpret_cast<uint4*>(cb + unit * 16) = o;
+        *reinterpret_cast<uint4*>(cb + (((m * 2 + part) * XQ + q) * 4 + t) * 16) = o;
       }
       if (uc % GU == 0) {
-        const int grp = uc / GU;  // column-group within the chunk
+        const int grp = uc / GU;
         float* tab = reinterpret_cast<float*>(cb + M * 2 * XQ * 64);
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
           const int col = (m * 2 + part) * NGC + grp;  // < 8
-          const int tl = col >> 1, hl = col & 1;
-          tab[tl * 4 + hl] = -1024.f * (part ? sl : sh);
-          tab[tl * 4 + 2 + hl] = part ? 0.f : sx;
+          tab[(col >> 1) * 4 + (col & 1)] = -1024.f * (part ? sl : sh);
+          tab[(col >> 1) * 4 + 2 + (col & 1)] = part ? 0.f : sx;
         }
       }
     }
   }
-  // columns no (m, part, group) maps to: zero table entries
-  for (int idx = tid; idx < (kc1 - kc0) * 8; idx += nthreads) {
-    const int cl = idx >> 3, col = idx & 7;
+  // columns no (m, part, group) maps to: zero table entries of this warp's chunks
+  for (int idx = lane; idx < nj * 8; idx += 32) {
+    const int cl = warp + (idx >> 3) * cps, col = idx & 7;
     if (col >= M * 2 * NGC) {
       float* tab = reinterpret_cast<float*>(xsb + (size_t)cl * CB + M * 2 * XQ * 64);
       tab[(col >> 1) * 4 + (col & 1)] = 0.f;
       tab[(col >> 1) * 4 + 2 + (col & 1)] = 0.f;
     }
   }
-  named_bar_sync(bar_id, nthreads);
+  __syncwarp();
 }
 
 template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
@@ -1036,7 +1014,6 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   extern __shared__ __align__(128) unsigned char smem_tma[];
   __shared__ int s_abort;
   __shared__ float s_part[TC_NCW][4];
-  __shared__ float s_rms[4];
   __shared__ __align__(8) uint64_t s_xready;  // consumers have staged x (lets the producer run on)
   __shared__ __align__(16) uint4 s_zero[XQ * 4];  // B fragments of lanes that feed no column
 
@@ -1065,7 +1042,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], TC_NCW);
     }
-    mbar_init(&s_xready, 1);
+    mbar_init(&s_xready, TC_NCW);
     s_abort = 0;
     fence_mbar_init();
   }
@@ -1148,8 +1125,8 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       if (EPI == SC_EPI_RESIDUAL) pre_res = p.residual[(size_t)mm * p.ldr + row];
     }
   }
-  stage_x_fx<BITS, NGC, NORM, XT>(p, xsb, s_part, s_rms, kc0, kc1, tid, NC, 1);
-  if (tid == 0) mbar_arrive(&s_xready);
+  stage_x_fx_warp<BITS, NGC, NORM, XT>(p, xsb, s_part, kc0, kc1, geo.cps, warp, lane);
+  if (lane == 0) mbar_arrive(&s_xready);
   const int CB = fx_chunk_bytes(BITS, M);
 
   // B-fragment column of this lane and whether its words' group feeds it
@@ -1382,6 +1359,14 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     float v[2];
 #pragma unroll
     for (int a = 0; a < NACC; ++a) v[a] = fx_from_fixed(s_acc[idx * NACC + a]);
+    if (NORM) {  // staged x was x * norm_weight: divide by the row's rms (warp partials in warp order)
+      float ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < TC_NCW; ++w) ss += s_part[w][mm];
+      const float r = sqrtf(ss / (float)p.K + p.eps);
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) v[a] = v[a] / r;
+    }
     if (row >= p.N) continue;
     if (pre_epi)  // bias / residual already read; same sums, same order as epilogue()
       reinterpret_cast<YT*>(p.y)[(size_t)mm * p.ldy + row] = from_f32<YT>((v[0] + pre_bias) + pre_res);
