@@ -198,16 +198,23 @@ __device__ __forceinline__ void merge_partials(const float* pbase, size_t sstrid
     s_l[sp][g] = __ldcg(pp + 1);
   }
   __syncthreads();
-  if (threadIdx.x < G) {
+  if (threadIdx.x < G) {  // the head's maximum over the splits (cheap: no exp)
     const int g = threadIdx.x;
     float M = -INFINITY;
     for (int sp = 0; sp < splits; ++sp) M = fmaxf(M, s_w[sp][g]);
+    s_inv[g] = M;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < splits * G; i += NT) {  // the splits' weights, in parallel
+    const int sp = i / G, g = i % G;
+    const float mw = s_w[sp][g];
+    s_w[sp][g] = mw == -INFINITY ? 0.f : expf(mw - s_inv[g]);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
     float Ls = 0.f;
-    for (int sp = 0; sp < splits; ++sp) {
-      const float w = s_w[sp][g] == -INFINITY ? 0.f : expf(s_w[sp][g] - M);
-      s_w[sp][g] = w;
-      Ls = fmaf(s_l[sp][g], w, Ls);
-    }
+    for (int sp = 0; sp < splits; ++sp) Ls = fmaf(s_l[sp][g], s_w[sp][g], Ls);
     s_inv[g] = 1.f / Ls;
   }
   __syncthreads();
@@ -400,19 +407,26 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   }
   __syncthreads();
 
+  // Per tile: (1) scores of all its keys into s_s, (2) one softmax update per
+  // head (running max / sum in shared memory, probabilities back into s_s),
+  // (3) o += p . V with the tile's rescale applied once.  Every lane group
+  // shares the running max, so the groups' outputs merge by a plain sum.
+  __shared__ float s_s[G][AD_TK];
+  __shared__ float s_rm[G], s_rl[G], s_corr[G];  // running max / sum per head
+  if (threadIdx.x < G) {
+    s_rm[threadIdx.x] = -INFINITY;
+    s_rl[threadIdx.x] = 0.f;
+  }
   float qr[G][8];
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int i = 0; i < 8; ++i) qr[g][i] = s_q[g][d0 + i];
-  float m[G], l[G], o[G][8];
+  float o[G][8];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
+  for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
-  }
   int t = 0;
   for (; t < ntiles; ++t) {
     const int bi = t % AD_NB;
@@ -423,25 +437,19 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
     const int nk = min(AD_TK, k_end - kt);
     const __half* tk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
     const __half* tv = tk + AD_TK * HD;
-#pragma unroll 2
+    // (1) scores
+#pragma unroll
     for (int kk = warp * KPS + sub; kk < AD_TK; kk += STEP) {
       const bool valid = kk < nk;
-      const int key = kt + kk;
-      uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
-      if (valid) {
-        const bool fresh = owner && key == pos;
-        kv4 = *reinterpret_cast<const uint4*>((fresh ? s_knew : tk + (size_t)kk * HD) + d0);
-        vv4 = *reinterpret_cast<const uint4*>((fresh ? s_vnew : tv + (size_t)kk * HD) + d0);
-      }
-      float kf[8], vf[8];
+      uint4 kv4 = make_uint4(0, 0, 0, 0);
+      if (valid) kv4 = *reinterpret_cast<const uint4*>((owner && kt + kk == pos ? s_knew : tk + (size_t)kk * HD) + d0);
+      float kf[8];
       const uint32_t kw[4] = {kv4.x, kv4.y, kv4.z, kv4.w};
-      const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 a = __half22float2(u32_as_h2(kw[i]));
-        const float2 c = __half22float2(u32_as_h2(vw[i]));
-        kf[2 * i] = a.x; kf[2 * i + 1] = a.y;
-        vf[2 * i] = c.x; vf[2 * i + 1] = c.y;
+        kf[2 * i] = a.x;
+        kf[2 * i + 1] = a.y;
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -450,19 +458,69 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
         for (int i = 0; i < 8; ++i) dot = fmaf(qr[g][i], kf[i], dot);
 #pragma unroll
         for (int off = LPK / 2; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-        if (valid) {
-          const float sc = dot * scale;
-          const float mn = fmaxf(m[g], sc);
-          const float corr = expf(m[g] - mn);
-          const float pr = expf(sc - mn);
-          l[g] = l[g] * corr + pr;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) o[g][i] = fmaf(pr, vf[i], o[g][i] * corr);
-          m[g] = mn;
-        }
+        if (dl == 0) s_s[g][kk] = valid ? dot * scale : -INFINITY;
       }
     }
-    __syncthreads();  // every warp is done with buffer bi
+    __syncthreads();
+    // (2) softmax update: warp g owns head g
+    if (warp < G) {
+      const int g = warp;
+      float v[AD_TK / 32];
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < AD_TK / 32; ++j) {
+        v[j] = s_s[g][lane + 32 * j];
+        mt = fmaxf(mt, v[j]);
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float m_old = s_rm[g];
+      const float mn = fmaxf(m_old, mt);
+      const bool none = mn == -INFINITY;  // no key so far: keep zeros, no NaN
+      float lt = 0.f;
+#pragma unroll
+      for (int j = 0; j < AD_TK / 32; ++j) {
+        const float pj = none ? 0.f : expf(v[j] - mn);
+        s_s[g][lane + 32 * j] = pj;
+        lt += pj;
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+      if (lane == 0) {
+        const float corr = none ? 1.f : expf(m_old - mn);
+        s_corr[g] = corr;
+        s_rl[g] = s_rl[g] * corr + lt;
+        s_rm[g] = mn;
+      }
+    }
+    __syncthreads();
+    // (3) o = o * corr + p . V
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float c = s_corr[g];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[g][i] *= c;
+    }
+#pragma unroll
+    for (int kk = warp * KPS + sub; kk < AD_TK; kk += STEP) {
+      if (kk >= nk) break;  // keys ascend with kk for this lane
+      const uint4 vv4 = *reinterpret_cast<const uint4*>((owner && kt + kk == pos ? s_vnew : tv + (size_t)kk * HD) + d0);
+      float vf[8];
+      const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 c = __half22float2(u32_as_h2(vw[i]));
+        vf[2 * i] = c.x;
+        vf[2 * i + 1] = c.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pr = s_s[g][kk];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[g][i] = fmaf(pr, vf[i], o[g][i]);
+      }
+    }
+    __syncthreads();  // every warp is done with buffer bi and with s_s
     if (threadIdx.x == 0 && t + AD_NB < ntiles) issue(t + AD_NB);
   }
   if (s_abort) {
@@ -477,33 +535,20 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
     return;  // every thread returns: no barrier below is left waiting
   }
 
-  // merge the lane groups of the CTA (their outputs reuse the tile buffers)
-  __shared__ float sm_m[NGRP][G], sm_l[NGRP][G];
+  // sum the lane groups' outputs (they reuse the tile buffers)
   float* sm_o = reinterpret_cast<float*>(ad_smem);  // [NGRP][G][HD]
   const int grp = warp * KPS + sub;
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (dl == 0) {
-      sm_m[grp][g] = m[g];
-      sm_l[grp][g] = l[g];
-    }
+  for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int i = 0; i < 8; ++i) sm_o[((size_t)grp * G + g) * HD + d0 + i] = o[g][i];
-  }
   __syncthreads();
   float* pbase = part + (((size_t)b * Hkv + kvh) * splits) * G * (HD + 2);
   for (int e = threadIdx.x; e < G * HD; e += NT) {
     const int g = e / HD, d = e % HD;
-    float M = -INFINITY;
-    for (int r = 0; r < NGRP; ++r) M = fmaxf(M, sm_m[r][g]);
-    float Ls = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int r = 0; r < NGRP; ++r) {
-        const float w = expf(sm_m[r][g] - M);
-        Ls = fmaf(sm_l[r][g], w, Ls);
-        O = fmaf(sm_o[((size_t)r * G + g) * HD + d], w, O);
-      }
-    }
+    float O = 0.f;
+    for (int r = 0; r < NGRP; ++r) O += sm_o[((size_t)r * G + g) * HD + d];
+    const float M = s_rm[g], Ls = s_rl[g];
     if (splits == 1) {
       out[(size_t)b * Hq * HD + (size_t)(kvh * G + g) * HD + d] = from_f32<OT>(O / Ls);
     } else {
