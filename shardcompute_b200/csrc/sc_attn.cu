@@ -248,6 +248,81 @@ __device__ __forceinline__ void merge_partials(const float* pbase, size_t sstrid
   }
 }
 
+// Split merge of the fused decode kernel in one round of loads, by one CTA of
+// NT threads.  Partials are {m, l, -, -, o[HD]} per (split, head): 16-byte
+// aligned, so a thread's 8 dims of one split are two 16-byte loads.  Thread
+// (unit, subset) owns 8 output dims of one head and the splits congruent to
+// its subset modulo S; it issues all their loads (up to MR_BATCH) at once,
+// folds them in with a running maximum, and the S subsets are folded through
+// shared memory (`s_red`, NT * 10 floats).  Output = sum(w o) / sum(w l).
+constexpr int MR_BATCH = 8;
+constexpr int AD_PSTRIDE_PAD = 4;  // floats before o[] in a fused-kernel partial
+
+template <int HD, int G, int NT, typename OT>
+__device__ __forceinline__ void merge_partials_1r(const float* pbase, int splits, OT* outp, float* s_red) {
+  constexpr int UNITS = G * HD / 8;
+  constexpr int S = NT / UNITS;
+  constexpr int PS = HD + AD_PSTRIDE_PAD;  // floats per (split, head)
+  static_assert(S >= 1, "one thread per 8 output dims at least");
+  const int u = threadIdx.x % UNITS, j = threadIdx.x / UNITS;
+  const int g = u / (HD / 8), d8 = (u % (HD / 8)) * 8;
+  float M = -INFINITY, Ls = 0.f, acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  if (j < S) {
+    for (int s0 = j; s0 < splits; s0 += S * MR_BATCH) {
+      float2 ml[MR_BATCH];
+      float4 oa[MR_BATCH], ob[MR_BATCH];
+#pragma unroll
+      for (int r = 0; r < MR_BATCH; ++r) {
+        const int sp = s0 + r * S;
+        ml[r] = make_float2(-INFINITY, 0.f);
+        oa[r] = ob[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (sp < splits) {
+          const float* pp = pbase + ((size_t)sp * G + g) * PS;
+          ml[r] = __ldcg(reinterpret_cast<const float2*>(pp));
+          oa[r] = __ldcg(reinterpret_cast<const float4*>(pp + AD_PSTRIDE_PAD + d8));
+          ob[r] = __ldcg(reinterpret_cast<const float4*>(pp + AD_PSTRIDE_PAD + d8 + 4));
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < MR_BATCH; ++r) {
+        if (ml[r].x == -INFINITY) continue;  // an empty split (or past the last)
+        const float mn = fmaxf(M, ml[r].x);
+        const float co = M == -INFINITY ? 0.f : expf(M - mn);
+        const float w = expf(ml[r].x - mn);
+        Ls = Ls * co + ml[r].y * w;
+        const float ov[8] = {oa[r].x, oa[r].y, oa[r].z, oa[r].w, ob[r].x, ob[r].y, ob[r].z, ob[r].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = acc[i] * co + ov[i] * w;
+        M = mn;
+      }
+    }
+  }
+  float* me = s_red + (size_t)threadIdx.x * 10;
+  me[0] = M;
+  me[1] = Ls;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) me[2 + i] = acc[i];
+  __syncthreads();
+  if (j == 0) {
+    for (int jj = 1; jj < S; ++jj) {
+      const float* o = s_red + (size_t)(jj * UNITS + u) * 10;
+      if (o[0] == -INFINITY) continue;
+      const float mn = fmaxf(M, o[0]);
+      const float co = M == -INFINITY ? 0.f : expf(M - mn);
+      const float w = expf(o[0] - mn);
+      Ls = Ls * co + o[1] * w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = acc[i] * co + o[2 + i] * w;
+      M = mn;
+    }
+    const float inv = 1.f / Ls;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) outp[(size_t)g * HD + d8 + i] = from_f32<OT>(acc[i] * inv);
+  }
+}
+
 template <int HD, typename OT>
 __global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq, int splits, OT* __restrict__ out) {
   pdl_trigger();
@@ -543,7 +618,8 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
 #pragma unroll
     for (int i = 0; i < 8; ++i) sm_o[((size_t)grp * G + g) * HD + d0 + i] = o[g][i];
   __syncthreads();
-  float* pbase = part + (((size_t)b * Hkv + kvh) * splits) * G * (HD + 2);
+  constexpr int PS = HD + AD_PSTRIDE_PAD;
+  float* pbase = part + (((size_t)b * Hkv + kvh) * splits) * G * PS;
   for (int e = threadIdx.x; e < G * HD; e += NT) {
     const int g = e / HD, d = e % HD;
     float O = 0.f;
@@ -552,8 +628,8 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
     if (splits == 1) {
       out[(size_t)b * Hq * HD + (size_t)(kvh * G + g) * HD + d] = from_f32<OT>(O / Ls);
     } else {
-      float* pp = pbase + ((size_t)split * G + g) * (HD + 2);
-      pp[2 + d] = O;
+      float* pp = pbase + ((size_t)split * G + g) * PS;
+      pp[AD_PSTRIDE_PAD + d] = O;
       if (d == 0) {
         pp[0] = M;
         pp[1] = Ls;
@@ -573,9 +649,8 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   }
   __syncthreads();
   if (!s_last) return;
-  __shared__ float s_w[FD_MAX_SPLITS][G], s_l[FD_MAX_SPLITS][G], s_inv[G];
-  merge_partials<HD, G, NT, OT>(pbase, (size_t)G * (HD + 2), HD + 2, splits,
-                                out + (size_t)b * Hq * HD + (size_t)kvh * G * HD, s_w, s_l, s_inv);
+  merge_partials_1r<HD, G, NT, OT>(pbase, splits, out + (size_t)b * Hq * HD + (size_t)kvh * G * HD,
+                                   reinterpret_cast<float*>(ad_smem));
   if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
 }
 
@@ -661,7 +736,7 @@ int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_c
 
 size_t sc_attn_decode_workspace_bytes(int B, int Hq, int hd, int splits) {
   if (splits <= 1) return 0;
-  return (size_t)B * Hq * splits * (hd + 2) * sizeof(float);
+  return (size_t)B * Hq * splits * (hd + sc::AD_PSTRIDE_PAD) * sizeof(float);
 }
 
 int sc_attn_device_error(int reset) {
