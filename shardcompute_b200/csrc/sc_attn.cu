@@ -409,6 +409,7 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   constexpr int NT = AD_WARPS * 32;
   constexpr int STEP = AD_WARPS * KPS;  // keys per CTA step
   constexpr int NGRP = ad_groups(HD);
+  static_assert(G <= LPK, "the score butterfly needs a lane per head in a key's lane group");
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPK, dl = lane % LPK;
@@ -512,9 +513,12 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
     const int nk = min(AD_TK, k_end - kt);
     const __half* tk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
     const __half* tv = tk + AD_TK * HD;
-    // (1) scores
-#pragma unroll
-    for (int kk = warp * KPS + sub; kk < AD_TK; kk += STEP) {
+    // (1) scores: only the steps that hold keys; the G per-lane dot products
+    // are summed over the LPK lanes of a key with a transposing butterfly
+    // (G - 1 + log2(LPK / G) shuffles instead of G * log2(LPK))
+    const int steps = (nk + STEP - 1) / STEP;
+    for (int st = 0; st < steps; ++st) {
+      const int kk = st * STEP + warp * KPS + sub;
       const bool valid = kk < nk;
       uint4 kv4 = make_uint4(0, 0, 0, 0);
       if (valid) kv4 = *reinterpret_cast<const uint4*>((owner && kt + kk == pos ? s_knew : tk + (size_t)kk * HD) + d0);
@@ -526,15 +530,29 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
         kf[2 * i] = a.x;
         kf[2 * i + 1] = a.y;
       }
+      float dv[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         float dot = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) dot = fmaf(qr[g][i], kf[i], dot);
-#pragma unroll
-        for (int off = LPK / 2; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-        if (dl == 0) s_s[g][kk] = valid ? dot * scale : -INFINITY;
+        dv[g] = dot;
       }
+      int h = 0;  // head whose sum this lane ends up holding
+#pragma unroll
+      for (int half = G / 2, off = LPK / 2; half >= 1; half >>= 1, off >>= 1) {
+        const bool up = (dl & off) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float send = up ? dv[i] : dv[i + half];
+          const float keep = up ? dv[i + half] : dv[i];
+          dv[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+        h += up ? half : 0;
+      }
+#pragma unroll
+      for (int off = LPK / (2 * G); off >= 1; off >>= 1) dv[0] += __shfl_xor_sync(0xffffffffu, dv[0], off);
+      if ((dl & (LPK / G - 1)) == 0) s_s[h][kk] = valid ? dv[0] * scale : -INFINITY;
     }
     __syncthreads();
     // (2) softmax update: warp g owns head g
@@ -544,7 +562,7 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
       float mt = -INFINITY;
 #pragma unroll
       for (int j = 0; j < AD_TK / 32; ++j) {
-        v[j] = s_s[g][lane + 32 * j];
+        v[j] = lane + 32 * j < nk ? s_s[g][lane + 32 * j] : -INFINITY;  // slots past nk were not written
         mt = fmaxf(mt, v[j]);
       }
 #pragma unroll

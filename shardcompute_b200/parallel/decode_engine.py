@@ -86,8 +86,8 @@ class DecodeEngine:
         self.fused_attn = os.environ.get("SC_ATTN_FUSED", "1") != "0"
         if attn_splits is None and os.environ.get("SC_ATTN_SPLITS"):
             attn_splits = int(os.environ["SC_ATTN_SPLITS"])
-        if attn_splits is None:  # ~2 CTAs per SM, at most 32 splits (the split merge reads 32 in one round)
-            attn_splits = max(1, min(32, math.ceil(2 * 148 / max(1, self.Hkv * self.B)), math.ceil(self.Lmax / 64)))
+        if attn_splits is None:  # ~2 CTAs per SM
+            attn_splits = max(1, min(64, math.ceil(2 * 148 / max(1, self.Hkv * self.B)), math.ceil(self.Lmax / 64)))
         self.splits = attn_splits
         self._bufs = {}
         # L2 prefetch of the next GEMV's weights (bytes per GEMV; 0 = off)
