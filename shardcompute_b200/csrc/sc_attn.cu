@@ -255,7 +255,7 @@ __device__ __forceinline__ void merge_partials(const float* pbase, size_t sstrid
 // its subset modulo S; it issues all their loads (up to MR_BATCH) at once,
 // folds them in with a running maximum, and the S subsets are folded through
 // shared memory (`s_red`, NT * 10 floats).  Output = sum(w o) / sum(w l).
-constexpr int MR_BATCH = 8;
+constexpr int MR_BATCH = 10;
 constexpr int AD_PSTRIDE_PAD = 4;  // floats before o[] in a fused-kernel partial
 
 template <int HD, int G, int NT, typename OT>
