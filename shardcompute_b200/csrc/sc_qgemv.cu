@@ -1239,9 +1239,9 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     const bool act = kst == spt - 1 ? warp < last_nch : has_chunk;
     // ---- MMAs of the current stage (registers loaded one stage ahead)
     float ca[NACC][4], cz[NACC][4];
-    float4 tb = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (act) {
-      const uint32_t xb = bact ? xst + fo_x : zero_x;
+    float4 tb;
+    {  // no branch: a warp without a chunk in this stage multiplies zeros
+      const uint32_t xb = (bact && act) ? xst + fo_x : zero_x;
       uint32_t bfr[NMMA][2];
 #pragma unroll
       for (int qq = 0; qq < XQ; ++qq) {
@@ -1251,7 +1251,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
         bfr[2 * qq + 1][0] = v.z;
         bfr[2 * qq + 1][1] = v.w;
       }
-      tb = lds_f4(xst + fo_t);
+      tb = lds_f4(act ? xst + fo_t : zero_x);
 #pragma unroll
       for (int a = 0; a < NACC; ++a) {
         const uint32_t r0[4] = {cur.w0[a].x, cur.w0[a].y, cur.w0[a].z, cur.w0[a].w};
