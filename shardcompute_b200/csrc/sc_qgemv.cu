@@ -793,8 +793,10 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
 // runs the epilogue.  No CTA-wide barrier sits in the streaming loop.
 
 // 64-bit two's-complement fixed point with 32 fraction bits (|v| < 2^31).
+// v * 2^32 is exact in fp32 (a power-of-two scale), so one float -> int64
+// conversion rounds exactly as the same product in double would.
 __device__ __forceinline__ unsigned long long fx_to_fixed(float v) {
-  return (unsigned long long)__double2ll_rn((double)v * 4294967296.0);
+  return (unsigned long long)__float2ll_rn(v * 4294967296.0f);
 }
 __device__ __forceinline__ float fx_from_fixed(unsigned long long u) {
   return (float)((double)(long long)u * (1.0 / 4294967296.0));
@@ -870,8 +872,10 @@ __device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned c
   const int M = p.M;
   const int CB = fx_chunk_bytes(BITS, M);
   const int nkc = kc1 - kc0;
-  // this warp's chunks: cl = warp + j * cps (the consumer of chunk cl is warp cl % cps)
-  const int nj = (warp < cps && warp < nkc) ? (nkc - warp + cps - 1) / cps : 0;
+  // this warp's chunks: cl = warp + j * cps (the consumer of chunk cl is warp cl % cps), one
+  // per stage of a tile; slots past the slice's last chunk (a tile's last stage
+  // may be partly empty) are staged as zeros, so their weights add nothing
+  const int nj = warp < cps ? (nkc + cps - 1) / cps : 0;
   const int npass = (nj + CPP - 1) / CPP * M;                     // (pass, row) items
   const int jl = lane / UPC, uc = lane % UPC;                      // chunk within a pass, unit
   if (NORM) {
@@ -905,7 +909,7 @@ __device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned c
       const int m = it % M, j = (it / M) * CPP + jl;
       const int cl = warp + j * cps;
       const int k0 = (kc0 + cl) * TR::KPC + uc * 8;
-      if (it < npass && j < nj && k0 < p.K) {
+      if (it < npass && j < nj && cl < nkc && k0 < p.K) {
         ld_x8<XT>(p, m, k0, v[b]);
         if (NORM) {
           const uint16_t* nwp = p.norm_w + k0;
@@ -1040,7 +1044,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   if (tid == 0) {
     for (int s = 0; s < geo.nst; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], TC_NCW);
+      mbar_init(&empty[s], 32 * geo.cps);  // every lane of the warps that own a chunk
     }
     mbar_init(&s_xready, TC_NCW);
     s_abort = 0;
@@ -1189,15 +1193,12 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     d[3] = ld_sb_raw(sp + sset + s_r8);
   };
   // A stage holds cps chunks (fewer than TC_NCW for a short K or a narrow
-  // scale box): warps past them read nothing, their offsets would leave the stage.
+  // scale box): warps past them own no chunk and sit the stream out (their
+  // offsets would leave the stage); the empty barriers count only the others.
   const bool has_chunk = warp < cps;
   auto ld_stage = [&](StageRegs& d, uint32_t soff) {
 #pragma unroll
     for (int a = 0; a < NACC; ++a) {
-      if (!has_chunk) {
-        d.w0[a] = d.w1[a] = make_uint4(0u, 0u, 0u, 0u);
-        continue;
-      }
       const uint32_t wp = ring_w + soff + a * wset;
       d.w0[a] = lds_v4(wp);
       d.w1[a] = lds_v4(wp + w_r8);
@@ -1209,10 +1210,12 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   auto sb_hi = [](uint32_t r) { return NGC >= 2 ? __high2float(u32_as_h2(r)) : __low2float(u32_as_h2(r)); };
 
   // This CTA's tiles (blockIdx.x, + gridDim.x, ...) and the stages of each.
+  // Every stage of a tile is full: the chunk slots past the K slice hold zero
+  // x (staged so), which zeroes whatever weights and scales sit there.
   const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int kspan = kc1 - kc0;
   const int spt = (kspan + cps - 1) / cps;
-  const int nq = my_tiles * spt;
+  const int nq = has_chunk ? my_tiles * spt : 0;
   int s = 0;
   uint32_t ph = 0;
   bool aborted = false;
@@ -1229,91 +1232,89 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
 #pragma unroll
     for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
   int kst = 0, tl = 0;  // stage within the tile, tile of this CTA
-  uint32_t xst = smem_u32(xsb);  // staged x of the current stage's first chunk
-  const uint32_t xbase = xst;
-  const int last_nch = kspan - (spt - 1) * cps;  // chunks in a tile's last stage
+  const uint32_t xbase = smem_u32(xsb);
+  // B-fragment and table addresses of this lane in stage 0 of a tile; a lane
+  // whose B column is unused reads zeros
+  const uint32_t xb0 = bact ? xbase + fo_x : zero_x;
+  const uint32_t xstep = bact ? (uint32_t)(cps * CB) : 0u;
+  uint32_t xb = xb0, xt = xbase + fo_t;
   // One stage: MMAs on `cur`, the next stage's operands into `nxt`.  With one
   // weight set the loop runs two stages per trip with the register sets
   // swapped, so no copies.
   auto stage = [&](int q, StageRegs& cur, StageRegs& nxt) {
-    const bool act = kst == spt - 1 ? warp < last_nch : has_chunk;
+    const int s_cur = s;
+    // With one weight set every ring read of this stage (words, scales,
+    // biases) went into registers during the previous stage: free the slot now.
+    if (PIPE_SB) mbar_arrive(&empty[s_cur]);
     // ---- MMAs of the current stage (registers loaded one stage ahead)
     float ca[NACC][4], cz[NACC][4];
-    float4 tb;
-    {  // no branch: a warp without a chunk in this stage multiplies zeros
-      const uint32_t xb = (bact && act) ? xst + fo_x : zero_x;
-      uint32_t bfr[NMMA][2];
+    uint32_t bfr[NMMA][2];
 #pragma unroll
-      for (int qq = 0; qq < XQ; ++qq) {
-        const uint4 v = lds_v4(xb + qq * 64);
-        bfr[2 * qq][0] = v.x;
-        bfr[2 * qq][1] = v.y;
-        bfr[2 * qq + 1][0] = v.z;
-        bfr[2 * qq + 1][1] = v.w;
-      }
-      tb = lds_f4(act ? xst + fo_t : zero_x);
+    for (int qq = 0; qq < XQ; ++qq) {
+      const uint4 v = lds_v4(xb + qq * 64);
+      bfr[2 * qq][0] = v.x;
+      bfr[2 * qq][1] = v.y;
+      bfr[2 * qq + 1][0] = v.z;
+      bfr[2 * qq + 1][1] = v.w;
+    }
+    const float4 tb = lds_f4(xt);
 #pragma unroll
-      for (int a = 0; a < NACC; ++a) {
-        const uint32_t r0[4] = {cur.w0[a].x, cur.w0[a].y, cur.w0[a].z, cur.w0[a].w};
-        const uint32_t r1[4] = {cur.w1[a].x, cur.w1[a].y, cur.w1[a].z, cur.w1[a].w};
-        ca[a][0] = tb.x;
-        ca[a][1] = tb.y;
-        ca[a][2] = tb.x;
-        ca[a][3] = tb.y;
+    for (int a = 0; a < NACC; ++a) {
+      const uint32_t r0[4] = {cur.w0[a].x, cur.w0[a].y, cur.w0[a].z, cur.w0[a].w};
+      const uint32_t r1[4] = {cur.w1[a].x, cur.w1[a].y, cur.w1[a].z, cur.w1[a].w};
+      ca[a][0] = tb.x;
+      ca[a][1] = tb.y;
+      ca[a][2] = tb.x;
+      ca[a][3] = tb.y;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) cz[a][r] = 0.f;
+      for (int r = 0; r < 4; ++r) cz[a][r] = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t A0[4], A1[4];
-          unpack_off<BITS>(r0[j], A0);
-          unpack_off<BITS>(r1[j], A1);
-          if (BITS == 4) {
-            mma_16816(ca[a], A0[0], A1[0], A0[1], A1[1], bfr[2 * j][0], bfr[2 * j][1]);
-            mma_16816(cz[a], A0[2], A1[2], A0[3], A1[3], bfr[2 * j + 1][0], bfr[2 * j + 1][1]);
-          } else if (j & 1) {
-            mma_16816(cz[a], A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
-          } else {
-            mma_16816(ca[a], A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
-          }
+      for (int j = 0; j < 4; ++j) {
+        uint32_t A0[4], A1[4];
+        unpack_off<BITS>(r0[j], A0);
+        unpack_off<BITS>(r1[j], A1);
+        if (BITS == 4) {
+          mma_16816(ca[a], A0[0], A1[0], A0[1], A1[1], bfr[2 * j][0], bfr[2 * j][1]);
+          mma_16816(cz[a], A0[2], A1[2], A0[3], A1[3], bfr[2 * j + 1][0], bfr[2 * j + 1][1]);
+        } else if (j & 1) {
+          mma_16816(cz[a], A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
+        } else {
+          mma_16816(ca[a], A0[0], A1[0], A0[1], A1[1], bfr[j][0], bfr[j][1]);
         }
       }
     }
     // ---- the next stage's registers load while those MMAs run
-    const int s_cur = s;
     if (++s == nst) {
       s = 0;
       ph ^= 1;
     }
-    const bool more = q + 1 < nq;
-    if (more) {
+    if (q + 1 < nq) {
       if (mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS))
         ld_stage(nxt, (uint32_t)s * stage_bytes);
       else
         aborted = true;
     }
-    // ---- scales / biases of the current stage; then its slot is free
-    if (act) {
+    // ---- scales / biases of the current stage
 #pragma unroll
-      for (int a = 0; a < NACC; ++a) {
-        uint32_t sbv[4];
-        if (PIPE_SB) {
+    for (int a = 0; a < NACC; ++a) {
+      uint32_t sbv[4];
+      if (PIPE_SB) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) sbv[i] = cur.sb[PIPE_SB ? a : 0][i];
-        } else {
-          ld_sb4(sbv, (uint32_t)s_cur * stage_bytes, a);
-        }
-        acc[a][0] = fmaf(sb_lo(sbv[0]), ca[a][0] + cz[a][0], fmaf(sb_lo(sbv[2]), tb.z, acc[a][0]));
-        acc[a][1] = fmaf(sb_hi(sbv[0]), ca[a][1] + cz[a][1], fmaf(sb_hi(sbv[2]), tb.w, acc[a][1]));
-        acc[a][2] = fmaf(sb_lo(sbv[1]), ca[a][2] + cz[a][2], fmaf(sb_lo(sbv[3]), tb.z, acc[a][2]));
-        acc[a][3] = fmaf(sb_hi(sbv[1]), ca[a][3] + cz[a][3], fmaf(sb_hi(sbv[3]), tb.w, acc[a][3]));
+        for (int i = 0; i < 4; ++i) sbv[i] = cur.sb[PIPE_SB ? a : 0][i];
+      } else {
+        ld_sb4(sbv, (uint32_t)s_cur * stage_bytes, a);
       }
+      acc[a][0] = fmaf(sb_lo(sbv[0]), ca[a][0] + cz[a][0], fmaf(sb_lo(sbv[2]), tb.z, acc[a][0]));
+      acc[a][1] = fmaf(sb_hi(sbv[0]), ca[a][1] + cz[a][1], fmaf(sb_hi(sbv[2]), tb.w, acc[a][1]));
+      acc[a][2] = fmaf(sb_lo(sbv[1]), ca[a][2] + cz[a][2], fmaf(sb_lo(sbv[3]), tb.z, acc[a][2]));
+      acc[a][3] = fmaf(sb_hi(sbv[1]), ca[a][3] + cz[a][3], fmaf(sb_hi(sbv[3]), tb.w, acc[a][3]));
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s_cur]);
+    if (!PIPE_SB) mbar_arrive(&empty[s_cur]);  // the scale reads above were the slot's last
     // ---- tile done for this warp: reduce over k-lanes, add into the CTA's tile accumulators
     if (++kst == spt) {
       kst = 0;
-      xst = xbase;
+      xb = xb0;
+      xt = xbase + fo_t;
       const int m = t / NGC;
 #pragma unroll
       for (int a = 0; a < NACC; ++a) {
@@ -1332,7 +1333,8 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       }
       ++tl;
     } else {
-      xst += (uint32_t)(cps * CB);
+      xb += xstep;
+      xt += (uint32_t)(cps * CB);
     }
   };
   StageRegs alt;
@@ -1523,7 +1525,8 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   geo.wset_bytes = 16 * geo.nblk * 128;
   geo.sset_bytes = round_up(16 * geo.ngs * 2, 1024);
   geo.stage_bytes = nacc * (geo.wset_bytes + 2 * geo.sset_bytes);
-  geo.ring_off = round_up((int)xsb(sp.chunks_per_split), 1024);
+  // the factored kernel stages x for whole stages (a tile's last one zero-padded)
+  geo.ring_off = round_up((int)xsb(fx ? round_up(sp.chunks_per_split, cps) : sp.chunks_per_split), 1024);
   const int red_bytes = fx ? 0 : 2 * TC_NCW * 32 * nacc * MT * 4 * 4;  // double-buffered by tile
   tp.grid_x = std::max(1, std::min(sp.tiles, (nsm + sp.splits - 1) / sp.splits));
   // factored kernel: fp32 accumulators for every output of the CTA's tiles
