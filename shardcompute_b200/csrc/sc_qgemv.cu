@@ -419,7 +419,10 @@ struct TmaGeo {
   int pre_stages;   // factored kernel: stages the producer issues before x is staged
   int pf_after;     // factored kernel: L2 prefetch waits until this CTA's last stage has landed
   int acc_off;      // factored kernel: byte offset of the per-tile output accumulators
-  int acc_floats;   // factored kernel: their count (tiles of a CTA x 16 rows x M x sets), 8 bytes each
+  int acc_floats;   // factored kernel: their count (tiles of a CTA x 16 rows x M x sets)
+  int warp_slots;   // factored kernel: 1 = an fp32 slot per consumer warp and output, summed in
+                    // warp order by the epilogue; 0 = one 64-bit fixed-point slot per output
+                    // that the warps add into with shared atomics (when the slots do not fit)
 };
 
 struct TmaMaps {
@@ -788,9 +791,11 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
 // A lane's B value is x where its words' group matches the column, else 0.
 //
 // Each consumer warp accumulates its chunks of a tile in registers, reduces
-// over its k-lanes, and adds the tile's 16 row sums into a shared-memory
-// slot with shared atomics; the warp that arrives last on the slot's counter
-// runs the epilogue.  No CTA-wide barrier sits in the streaming loop.
+// over its k-lanes, and stores the tile's 16 row sums into its own fp32 slot
+// of the tile (no atomics); the CTA's epilogue sums a row's slots in warp
+// order after one barrier.  When the slots of all the CTA's tiles do not fit,
+// the warps instead add 64-bit fixed-point sums with shared atomics.  No
+// CTA-wide barrier sits in the streaming loop.
 
 // 64-bit two's-complement fixed point with 32 fraction bits (|v| < 2^31).
 // v * 2^32 is exact in fp32 (a power-of-two scale), so one float -> int64
@@ -1038,8 +1043,14 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   // Per-output accumulators of the CTA's tiles in 64-bit fixed point
   // (2^-32 units): integer atomics make the sum over warps independent of
   // their order, so every run (and every replay) gives the same bits.
+  // Per-output partial sums of the CTA's tiles, deterministic either way:
+  // warp slots [tile][row][m][set][warp] (fp32, every owning warp writes each
+  // of its tiles once), or 64-bit fixed point (2^-32 units) added with integer
+  // atomics, whose sum does not depend on the order of the adds.
   unsigned long long* s_acc = reinterpret_cast<unsigned long long*>(sbase + geo.acc_off);
-  for (int i = tid; i < geo.acc_floats; i += blockDim.x) s_acc[i] = 0ull;
+  float* s_slot = reinterpret_cast<float*>(sbase + geo.acc_off);
+  if (!geo.warp_slots)
+    for (int i = tid; i < geo.acc_floats; i += blockDim.x) s_acc[i] = 0ull;
   if (tid < XQ * 4) s_zero[tid] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) {
     for (int s = 0; s < geo.nst; ++s) {
@@ -1238,6 +1249,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   const uint32_t xb0 = bact ? xbase + fo_x : zero_x;
   const uint32_t xstep = bact ? (uint32_t)(cps * CB) : 0u;
   uint32_t xb = xb0, xt = xbase + fo_t;
+  const bool warp_slots = geo.warp_slots != 0;
   // One stage: MMAs on `cur`, the next stage's operands into `nxt`.  With one
   // weight set the loop runs two stages per trip with the register sets
   // swapped, so no copies.
@@ -1325,8 +1337,14 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
           vg8 += __shfl_xor_sync(0xffffffffu, vg8, o);
         }
         if ((t % NGC) == 0 && m < M) {
-          atomicAdd(&s_acc[((tl * 16 + pr0) * M + m) * NACC + a], fx_to_fixed(vg));
-          atomicAdd(&s_acc[((tl * 16 + pr0 + 8) * M + m) * NACC + a], fx_to_fixed(vg8));
+          if (warp_slots) {
+            float* sl = s_slot + (((tl * 16 + pr0) * M + m) * NACC + a) * TC_NCW + warp;
+            sl[0] = vg;
+            sl[8 * M * NACC * TC_NCW] = vg8;
+          } else {
+            atomicAdd(&s_acc[((tl * 16 + pr0) * M + m) * NACC + a], fx_to_fixed(vg));
+            atomicAdd(&s_acc[((tl * 16 + pr0 + 8) * M + m) * NACC + a], fx_to_fixed(vg8));
+          }
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
@@ -1359,8 +1377,28 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     const int rl = rem / M, mm = rem - rl * M;
     const int row = ((int)blockIdx.x + tli * (int)gridDim.x) * 16 + rl;
     float v[2];
+    if (geo.warp_slots) {  // warp order: the same bits on every run
 #pragma unroll
-    for (int a = 0; a < NACC; ++a) v[a] = fx_from_fixed(s_acc[idx * NACC + a]);
+      for (int a = 0; a < NACC; ++a) {
+        const float4* sl = reinterpret_cast<const float4*>(s_slot + (idx * NACC + a) * TC_NCW);
+        float w16[TC_NCW];
+#pragma unroll
+        for (int i = 0; i < TC_NCW / 4; ++i) {
+          const float4 f = sl[i];
+          w16[4 * i] = f.x;
+          w16[4 * i + 1] = f.y;
+          w16[4 * i + 2] = f.z;
+          w16[4 * i + 3] = f.w;
+        }
+        float sum = w16[0];
+#pragma unroll
+        for (int w = 1; w < TC_NCW; ++w) sum += w < cps ? w16[w] : 0.f;  // slots of warps without a chunk are unset
+        v[a] = sum;
+      }
+    } else {
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) v[a] = fx_from_fixed(s_acc[idx * NACC + a]);
+    }
     if (NORM) {  // staged x was x * norm_weight: divide by the row's rms (warp partials in warp order)
       float ss = 0.f;
 #pragma unroll
@@ -1437,6 +1475,7 @@ static SplitPlan plan_splits(int M, int K, int N, int bits, int nacc) {
 
 // ---- TMA pipeline plan
 constexpr size_t TC_SMEM_BUDGET = 220 * 1024;
+constexpr int TC_SLOT_BUDGET = 64 * 1024;  // factored kernel: per-warp output slots
 constexpr size_t TC_XS_BUDGET = 64 * 1024;
 constexpr int TC_STAGE_CHUNKS = 32;  // 16 rows x 32 chunks x 64 B = 32 KB of packed words per stage
 
@@ -1531,8 +1570,10 @@ static TmaPlan plan_tma(int M, int K, int N, int bits, int group, int nacc, int 
   tp.grid_x = std::max(1, std::min(sp.tiles, (nsm + sp.splits - 1) / sp.splits));
   // factored kernel: fp32 accumulators for every output of the CTA's tiles
   geo.acc_floats = fx ? ((sp.tiles + tp.grid_x - 1) / tp.grid_x) * 16 * M * nacc : 0;
-  const int acc_bytes = round_up(geo.acc_floats * 8, 16);  // 64-bit fixed point
-  if (acc_bytes > 48 * 1024) return tp;
+  // fp32 slots per consumer warp when they fit (no atomics), else 64-bit fixed point
+  geo.warp_slots = fx && geo.acc_floats * TC_NCW * 4 <= TC_SLOT_BUDGET;
+  const int acc_bytes = round_up(geo.acc_floats * (geo.warp_slots ? TC_NCW * 4 : 8), 16);
+  if (acc_bytes > TC_SLOT_BUDGET) return tp;
   const size_t fixed = geo.ring_off + red_bytes + acc_bytes + 2 * TC_MAX_NST * 8 + 1024 /* base alignment */ + 64;
   if (fixed >= TC_SMEM_BUDGET) return tp;
   int nst = (int)std::min<size_t>(TC_MAX_NST, (TC_SMEM_BUDGET - fixed) / geo.stage_bytes);
