@@ -264,6 +264,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// The same wait for a whole warp (every lane passes the same barrier and
+// parity): the result is a vote, identical on all lanes, so the caller's
+// branches on it stay warp-uniform.  The first poll is the fast path.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               uint64_t limit_ns) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort, limit_ns));
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

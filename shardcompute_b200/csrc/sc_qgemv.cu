@@ -807,20 +807,28 @@ __device__ __forceinline__ float fx_from_fixed(unsigned long long u) {
   return (float)((double)(long long)u * (1.0 / 4294967296.0));
 }
 
+// (w & MASK) | 0x64006400 as one three-input logic op: written in C++ the
+// compiler splits it in two when the results feed mma operands.
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t and_or_mag(uint32_t w) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(d) : "r"(w), "n"(MASK), "n"(0x64006400u));
+  return d;
+}
+
 template <int BITS>
 __device__ __forceinline__ void unpack_off(uint32_t w, uint32_t (&a)[4]) {
   // fp16 pairs, exact: 4-bit (e0,e4) = 1024 + q, (e1,e5) = 1024 + 16 q, (e2,e6) = 1024 + q,
   // (e3,e7) = 1024 + 16 q -- the x slots of the odd codes hold x / 16; 8-bit (e0,e2) (e1,e3) = 1024 + q
-  const uint32_t MAG = 0x64006400u;
   if (BITS == 4) {
     const uint32_t w8 = w >> 8;
-    a[0] = (w & 0x000F000Fu) | MAG;
-    a[1] = (w & 0x00F000F0u) | MAG;
-    a[2] = (w8 & 0x000F000Fu) | MAG;
-    a[3] = (w8 & 0x00F000F0u) | MAG;
+    a[0] = and_or_mag<0x000F000Fu>(w);
+    a[1] = and_or_mag<0x00F000F0u>(w);
+    a[2] = and_or_mag<0x000F000Fu>(w8);
+    a[3] = and_or_mag<0x00F000F0u>(w8);
   } else {
-    a[0] = (w & 0x00FF00FFu) | MAG;
-    a[1] = ((w >> 8) & 0x00FF00FFu) | MAG;
+    a[0] = and_or_mag<0x00FF00FFu>(w);
+    a[1] = and_or_mag<0x00FF00FFu>(w >> 8);
     a[2] = a[3] = 0u;
   }
 }
@@ -1033,7 +1041,8 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   const int KC = (KW + 15) / 16;
   const int kc1 = min(KC, kc0 + p.chunks_per_split);
   const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
+  // warp index through a shuffle: the compiler then knows it is warp-uniform
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0), lane = tid & 31;
   unsigned char* sbase = smem_tma + ((1024 - (smem_u32(smem_tma) & 1023)) & 1023);
   unsigned char* xsb = sbase;
   unsigned char* ring = sbase + geo.ring_off;
@@ -1232,7 +1241,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   bool aborted = false;
   StageRegs cur;
   if (nq > 0) {
-    if (mbar_wait_bounded(&full[0], 0, &s_abort, TC_WAIT_NS))
+    if (mbar_wait_warp(&full[0], 0, &s_abort, TC_WAIT_NS))
       ld_stage(cur, 0u);
     else
       aborted = true;
@@ -1301,7 +1310,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       ph ^= 1;
     }
     if (q + 1 < nq) {
-      if (mbar_wait_bounded(&full[s], ph, &s_abort, TC_WAIT_NS))
+      if (mbar_wait_warp(&full[s], ph, &s_abort, TC_WAIT_NS))
         ld_stage(nxt, (uint32_t)s * stage_bytes);
       else
         aborted = true;
