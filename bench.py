@@ -119,7 +119,7 @@ def dist_env():
 # DRAM bytes (read + written) of the GEMV launches of one decode step, from the
 # ncu launch-list capture summarised in profiles/decode_step_llama3-8b_tp1_launches.md
 # (dram__bytes_read.sum + dram__bytes_write.sum, timed graph replays only).
-NCU_GEMV_TRAFFIC = {("llama3-8b", 1, 1, 4, 64, 2048): 4236.5e6}
+NCU_GEMV_TRAFFIC = {("llama3-8b", 1, 1, 4, 64, 2048): 4235.6e6}
 
 
 def load_peaks():
