@@ -870,8 +870,10 @@ __device__ __forceinline__ void ld_x8(const QGemvParams& p, int m, int k0, float
 // shuffles.  With RMSNorm the staged values are x * norm_weight (unscaled):
 // the product is linear in x, so the kernel divides its outputs by the row's
 // rms at the end instead; this warp's share of sum(x^2) over the whole row
-// (a contiguous K / TC_NCW slice, whatever K slice the CTA stages) goes to
-// s_ss[warp][m] and is summed in warp order at the end (deterministic).
+// goes to s_ss[warp][m] and is summed in warp order at the end
+// (deterministic).  When the CTA stages the whole row (one K split) that
+// share is taken from the values the warp stages anyway (one round trip to
+// L2); otherwise from a contiguous K / TC_NCW slice of the row.
 constexpr int FXW_PASSES = 4;  // (chunk, unit) passes a warp keeps in registers per batch
 
 template <int BITS, int NGC, bool NORM, typename XT>
@@ -891,7 +893,9 @@ __device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned c
   const int nj = warp < cps ? (nkc + cps - 1) / cps : 0;
   const int npass = (nj + CPP - 1) / CPP * M;                     // (pass, row) items
   const int jl = lane / UPC, uc = lane % UPC;                      // chunk within a pass, unit
-  if (NORM) {
+  const bool ss_in_pass = NORM && p.splits == 1;  // the warps' chunks cover the whole row
+  float ssm[4] = {0.f, 0.f, 0.f, 0.f};             // this lane's sum(x^2) per batch row
+  if (NORM && !ss_in_pass) {
     // sum(x^2) over this warp's contiguous slice of the full row, 8 values per lane per step
     const int per = ((p.K + TC_NCW - 1) / TC_NCW + 7) / 8 * 8;  // 8-aligned slices: vector loads
     const int k_lo = min(p.K, warp * per), k_hi = min(p.K, k_lo + per);
@@ -944,6 +948,14 @@ __device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned c
       const bool ok = j < nj;
       const int cl = warp + (ok ? j : 0) * cps;
       float x[8];
+      if (NORM && ss_in_pass) {
+        float sq = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sq = fmaf(v[b][i], v[b][i], sq);
+#pragma unroll
+        for (int mm = 0; mm < 4; ++mm)
+          if (mm == m) ssm[mm] += sq;
+      }
       if (NORM) {
         const uint32_t nww[4] = {nwr[NORM ? b : 0].x, nwr[NORM ? b : 0].y, nwr[NORM ? b : 0].z, nwr[NORM ? b : 0].w};
 #pragma unroll
@@ -957,23 +969,30 @@ __device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned c
         for (int i = 0; i < 8; ++i) x[i] = v[b][i];
       }
       __half hi[8], lo[8];
-      float sh = 0.f, sl = 0.f, sx = 0.f;
+      float shp[4], slp[4], sxp[4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        __half h = __float2half_rn(x[e]);
-        __half l = __float2half_rn(x[e] - __half2float(h));
-        if (BITS == 4 && (e & 1)) {  // odd codes arrive as 16 q: their x slots carry x / 16
-          h = __hmul(h, __float2half_rn(0.0625f));
-          l = __hmul(l, __float2half_rn(0.0625f));
+      for (int i = 0; i < 4; ++i) {  // element pairs (even, odd), converted two at a time
+        // odd codes arrive as 16 q: their x slots carry x / 16 (an exact scale)
+        const float a = x[2 * i], b = BITS == 4 ? x[2 * i + 1] * 0.0625f : x[2 * i + 1];
+        const __half2 hp = __floats2half2_rn(a, b);
+        const float2 hf = __half22float2(hp);
+        const __half2 lp = __floats2half2_rn(a - hf.x, b - hf.y);
+        const float2 lf = __half22float2(lp);
+        shp[i] = hf.x + hf.y;
+        slp[i] = lf.x + lf.y;
+        sxp[i] = x[2 * i] + x[2 * i + 1];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int e = 2 * i + u;
+          const int pos = BITS == 4 ? 4 * ((e >> 1) & 1) + 2 * (e & 1) + (e >> 2)
+                                    : 4 * (e >> 2) + 2 * (e & 1) + ((e >> 1) & 1);
+          hi[pos] = u ? __high2half(hp) : __low2half(hp);
+          lo[pos] = u ? __high2half(lp) : __low2half(lp);
         }
-        sh += __half2float(h);
-        sl += __half2float(l);
-        sx += x[e];
-        const int pos = BITS == 4 ? 4 * ((e >> 1) & 1) + 2 * (e & 1) + (e >> 2)
-                                  : 4 * (e >> 2) + 2 * (e & 1) + ((e >> 1) & 1);
-        hi[pos] = h;
-        lo[pos] = l;
       }
+      float sh = (shp[0] + shp[1]) + (shp[2] + shp[3]);
+      float sl = (slp[0] + slp[1]) + (slp[2] + slp[3]);
+      float sx = (sxp[0] + sxp[1]) + (sxp[2] + sxp[3]);
 #pragma unroll
       for (int o = 1; o < GU; o <<= 1) {
         sh += __shfl_xor_sync(0xffffffffu, sh, o);
@@ -1004,6 +1023,16 @@ __device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned c
           tab[(col >> 1) * 4 + 2 + (col & 1)] = part ? 0.f : sx;
         }
       }
+    }
+  }
+  if (NORM && ss_in_pass) {
+#pragma unroll
+    for (int mm = 0; mm < 4; ++mm) {
+      if (mm >= M) break;  // warp-uniform
+      float ss = ssm[mm];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) s_ss[warp][mm] = ss;
     }
   }
   // columns no (m, part, group) maps to: zero table entries of this warp's chunks
