@@ -126,10 +126,19 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
-# DRAM bytes (read + written) of the GEMV launches of one decode step, from the
-# ncu launch-list capture summarised in profiles/decode_step_llama3-8b_tp1_launches.md
-# (dram__bytes_read.sum + dram__bytes_write.sum, timed graph replays only).
+# DRAM bytes (read + written) of the GEMV launches of one decode step, measured
+# by ncu (dram__bytes_read.sum + dram__bytes_write.sum over the timed graph
+# replays of `python bench.py --steps 2 --warmup 3 --no-cpu-baseline`).
 NCU_GEMV_TRAFFIC = {("llama3-8b", 1, 1, 4, 64, 2048): 4235.6e6}
+
+
+def probe_mlx() -> str:
+    """Whether the reference's CPU backend (MLX) imports on this host."""
+    try:
+        import mlx.core  # noqa: F401
+        return "importable"
+    except Exception as e:  # noqa: BLE001 - any failure means the reference path cannot run
+        return f"not importable: {type(e).__name__}: {e}"
 
 
 def load_peaks():
@@ -210,8 +219,8 @@ def cpu_sample(args, world: int, budget_s: float):
     n = max(1, min(64, int(budget_s / max(t1, 1e-3))))
     sec = s.time_samples(n)
     desc = (f"{n} samples of 1/{sh.layers} token (one decoder layer + 1/{sh.layers} of the tied head) at "
-            f"ctx {sh.ctx}, batch {sh.batch}, TP shard 1/{world}; torch fp32 on {s.threads} threads; tok/s = "
-            f"batch / ({sh.layers} x s/sample)")
+            f"ctx {sh.ctx}, batch {sh.batch}, one TP{world} rank shard; torch fp32 on {s.threads} threads, every "
+            f"weight dequantized to fp32 on every step; tok/s = batch / ({sh.layers} x {world} shards x s/sample)")
     return s.tokens_per_s(sec), s.threads, desc, s, sec
 
 
@@ -227,8 +236,9 @@ def run_reference(args, rank: int, world: int):
     s = CpuDecodeSample(sh)
     threads = s.threads
     desc = (f"each step = 1/{sh.layers} token (one decoder layer + 1/{sh.layers} of the tied head) at ctx {sh.ctx}, "
-            f"batch {sh.batch}, TP shard 1/{world}, torch fp32 on {threads} threads; tok/s = batch / "
-            f"({sh.layers} x s/step)")
+            f"batch {sh.batch}, one TP{world} rank shard, torch fp32 on {threads} threads, every weight dequantized "
+            f"to fp32 on every step; all {world} shards run on this host: tok/s = batch / "
+            f"({sh.layers} x {world} x s/step)")
     for _ in range(args.warmup):
         s.run()
     times = []
@@ -245,8 +255,9 @@ def run_reference(args, rank: int, world: int):
             "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "MLX (the reference's CPU backend) is not installed; the oracle's torch-fp32 restatement of the "
-                    "same per-token work is timed instead"}
+            "mlx": probe_mlx(),
+            "note": "MLX (the reference's CPU backend) does not import here; the oracle's torch-fp32 restatement "
+                    "of the same per-token work is timed instead"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -310,7 +321,7 @@ def main():
     cfg = ModelConfig.from_dict(mdict)
     weights = RankWeights.synthetic(cfg, world, rank, bits=args.bits, group=args.group, device=dev, seed=0)
     B = args.batch
-    n_replays = 1 + 2 * (args.warmup + args.steps) + args.steps + 8
+    n_replays = 1 + 2 * (args.warmup + args.steps) + args.steps + 8 + 8
     eng = DecodeEngine(weights, comm, max_batch=B, max_seq=args.ctx + n_replays + 16, device=dev)
     gen = torch.Generator().manual_seed(2)
     prompt = torch.randint(0, cfg.vocab_size, (B, args.ctx), generator=gen, dtype=torch.int64).to(torch.int32)
@@ -323,6 +334,16 @@ def main():
     launches_per_step = int(_lib.load().sc_launch_count() - c0)
     eng.capture()
 
+    # ---- the first greedy tokens after the prompt (untimed), for cross-N agreement
+    host_in = torch.zeros(B, dtype=torch.int32).pin_memory()
+    host_out = torch.zeros(B, dtype=torch.int32).pin_memory()
+    host_out.copy_(eng.tok[:B])
+    first = [int(host_out[0])]
+    for _ in range(7):
+        host_in.copy_(host_out)
+        eng.decode_host(host_in, host_out)
+        first.append(int(host_out[0]))
+
     # ---- timed region: K graph replays, inputs resident on the device
     for _ in range(args.warmup):
         eng.replay()
@@ -331,6 +352,9 @@ def main():
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream(dev)  # graph replays launch on the current stream
+    # one untimed replay right before e0: its collectives line the ranks up on
+    # the device, so no rank's window includes waiting for a late peer
+    eng.replay()
     torch.cuda.nvtx.range_push("timed")
     e0.record(stream)
     for _ in range(args.steps):
@@ -344,8 +368,6 @@ def main():
     value = B * args.steps / (ms / 1e3)
 
     # ---- end to end: host token in (pinned), device step, host token out, each step
-    host_in = torch.zeros(B, dtype=torch.int32).pin_memory()
-    host_out = torch.zeros(B, dtype=torch.int32).pin_memory()
     host_out.copy_(eng.tok[:B])
     for _ in range(3):
         host_in.copy_(host_out)
@@ -394,7 +416,8 @@ def main():
                 "vs_baseline": None, "dtype": "f16", "weights": f"u{args.bits} g{args.group} affine",
                 "data": "synthetic (random-init N(0,0.02) weights, uniform random prompt ids)",
                 "config": workload_config(args, world), "clocks": clk, "e2e": e2e,
-                "gpu_launches": launches_per_step * args.steps, "roofline": roofline, "cpu_baseline": cpu}
+                "gpu_launches": launches_per_step * args.steps, "roofline": roofline, "cpu_baseline": cpu,
+                "first_tokens": first}
         print(json.dumps(line), flush=True)
     eng.graph = None
     eng._probe_graph = None

@@ -89,8 +89,8 @@ int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx,
  * 4 MiB array the library allocates statically on each device.  No
  * counterpart in the reference.  For callers that cannot allocate on the
  * call path (an FFI binding with no device allocator of its own; a serving
- * loop whose HBM is fully reserved).  Shapes whose workspace bound
- * (sc_qlinear_workspace_bytes) exceeds 4 MiB are refused with
+ * loop whose HBM is fully reserved).  Shapes whose split-K plan (for
+ * their own group size) needs more than 4 MiB are refused with
  * SC_ERR_WORKSPACE before any launch.  The first call on a device looks the
  * scratch up; make it before any stream capture.  One scratch per device:
  * calls overlapping in time on one device race. */
@@ -101,8 +101,9 @@ int sc_qlinear_noalloc(const void* x, int x_dtype, int M, int K, int ldx,
 
 /* Device-side error word of the quantized-linear kernels: nonzero after a
  * kernel gave up on a bounded wait (it then stops without touching the
- * output).  Synchronises with the device; reset != 0 clears it.  No
- * reference counterpart (the reference has no device code). */
+ * output; while the word is set, split-K passes leave y untouched too).
+ * Synchronises with the device; reset != 0 clears it.  No reference
+ * counterpart (the reference has no device code). */
 int sc_qgemv_device_error(int reset);
 
 /* Fused form used by the decode engine (no reference counterpart as one

@@ -12,9 +12,13 @@ in torch fp32 on all host threads: every step dequantizes each linear's packed
 words group-wise (``s*q + b``) and multiplies, runs softmax attention over a
 KV cache of ``ctx`` positions, and dequantizes its share of the tied head.
 
-One *sample* is 1/L of a token: one decoder layer plus 1/L of the LM-head
-rows (L = number of layers).  Tokens/s of the full model is therefore
-``1 / (L * seconds_per_sample)``.  Packed words are uniform random (the
+One *sample* is 1/L of a token on one rank's shard: one decoder layer plus
+1/L of the LM-head rows (L = number of layers).  At TP degree N the host
+runs all N ranks' shards one after another on the same cores (the reference
+would need N hosts), so tokens/s of the full model is
+``batch / (L * N * seconds_per_sample)``.  Unlike MLX's fused
+``quantized_matmul``, this stand-in dequantizes every weight to fp32 on
+every step, which makes it slower than MLX would be.  Packed words are uniform random (the
 timing does not depend on the values); scales/biases are small fp16 numbers.
 """
 
@@ -120,4 +124,5 @@ class CpuDecodeSample:
         return (time.perf_counter() - t0) / n
 
     def tokens_per_s(self, sec_per_sample: float) -> float:
-        return self.sh.batch / (self.sh.layers * sec_per_sample)
+        """Whole-model tokens/s on this host: L layers x N rank shards per token."""
+        return self.sh.batch / (self.sh.layers * self.sh.world * sec_per_sample)

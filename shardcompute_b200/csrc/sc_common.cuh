@@ -37,6 +37,9 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 bool pdl_enabled();
+// Split-K scratch of sc_qlinear for this exact shape and group (one weight
+// set, store epilogue); tma_ok: the weight pointers are 16-byte aligned.
+size_t qlinear_workspace_need(int M, int K, int N, int group, int bits, bool tma_ok);
 // Records a failed launch for the next check_launch() on this thread.
 void note_launch_status(cudaError_t e);
 

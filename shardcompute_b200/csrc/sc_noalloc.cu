@@ -10,8 +10,8 @@
 // sc_qlinear with the scratch below.
 //
 // Limits and rules:
-//   * the scratch holds NOALLOC_SCRATCH_BYTES (4 MiB); a shape whose
-//     workspace bound (sc_qlinear_workspace_bytes) exceeds it is refused with
+//   * the scratch holds NOALLOC_SCRATCH_BYTES (4 MiB); a shape whose split-K
+//     plan (for its own group size) needs more is refused with
 //     SC_ERR_WORKSPACE before anything is launched;
 //   * nothing in the scratch has to start at zero: the split-K partials are
 //     each written once before the reduce kernel reads them, so no clearing
@@ -58,7 +58,10 @@ extern "C" {
 int sc_qlinear_noalloc(const void* x, int x_dtype, int M, int K, int ldx, const uint32_t* wq,
                        const uint16_t* scales, const uint16_t* biases, int N, int group_size, int bits,
                        const uint16_t* bias, void* y, int y_dtype, int ldy, cudaStream_t stream) {
-  const size_t need = sc_qlinear_workspace_bytes(M, K, N, bits);
+  // the real plan of this shape and group (what sc_qlinear would ask for), so
+  // no shape that fits is refused; computed before anything is launched
+  const bool tma_ok = ((uintptr_t)wq % 16 == 0) && ((uintptr_t)scales % 16 == 0) && ((uintptr_t)biases % 16 == 0);
+  const size_t need = sc::qlinear_workspace_need(M, K, N, group_size, bits, tma_ok);
   SC_REQUIRE(need <= sc::NOALLOC_SCRATCH_BYTES, SC_ERR_WORKSPACE,
              "qlinear_noalloc: shape M=%d K=%d N=%d bits=%d may need %zu bytes of scratch; the static scratch "
              "holds %zu (use sc_qlinear with a caller workspace)",

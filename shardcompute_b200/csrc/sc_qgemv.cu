@@ -1457,6 +1457,10 @@ template <int EPI, typename YT>
 __global__ void qgemv_splitk_reduce(const QGemvParams p) {
   pdl_trigger();
   pdl_wait();
+  // A GEMV CTA whose bounded wait gave up returned without writing its
+  // partials: the workspace then holds stale values, so leave y untouched
+  // (the error word stays set until sc_qgemv_device_error(1) clears it).
+  if (*reinterpret_cast<volatile int*>(&g_qgemv_error)) return;
   const size_t total = (size_t)p.M * p.N;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
     const int col = (int)(e / p.N), row = (int)(e % p.N);
@@ -1961,6 +1965,25 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
     if (st != SC_OK) return st;
   }
   return SC_OK;
+}
+
+// Scratch the plain (one weight set, store epilogue) quantized linear needs
+// for this exact shape and group: the widest pass over its M split, for the
+// tensor-map plan when the weight pointers allow one and for the direct-load
+// plan it falls back to when the driver refuses the tensor maps.
+size_t qlinear_workspace_need(int M, int K, int N, int group, int bits, bool tma_ok) {
+  // shapes sc_qlinear rejects need nothing: it refuses them before any launch
+  if (M < 1 || K < 1 || N < 1 || (bits != 4 && bits != 8)) return 0;
+  if ((group != 32 && group != 64 && group != 128) || K % group) return 0;
+  size_t best = 0;
+  for (int m0 = 0; m0 < M; m0 += 16) {
+    const int mb = std::min(16, M - m0);
+    for (int tma = 0; tma < (tma_ok ? 2 : 1); ++tma) {
+      PassPlan pp = plan_pass(mb, K, N, bits, group, 1, tma != 0, false);
+      best = std::max(best, pass_workspace(pp, mb, N, 1));
+    }
+  }
+  return best;
 }
 
 }  // namespace sc

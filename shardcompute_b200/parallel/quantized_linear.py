@@ -182,11 +182,11 @@ class QuantizedRowParallelLinear:
                     if bi.dim() == 2:
                         bi = bi[:, sl].contiguous()
                 elif full != expected:
-                    logger.warning("QuantizedRowParallelLinear scales shape %s does not match expected groups %d; "
-                                   "leaving scales/biases unchanged", tuple(sc.shape), expected)
+                    logger.warning("row-parallel shard: %d scale columns fit neither this rank's %d groups nor the "
+                                   "full-K count; using the scales and biases as given", full, expected)
             else:
-                logger.warning("QuantizedRowParallelLinear input shard %d not divisible by group_size %d; "
-                               "leaving scales/biases unchanged", local_k, self.group_size)
+                logger.warning("row-parallel shard: local K=%d is not a whole number of %d-wide groups; "
+                               "using the scales and biases as given", local_k, self.group_size)
         self.quantized_weight, self.scales, self.biases_quant = qw, sc, bi
         if self.has_bias and linear_bias is not None and self.rank == 0:
             self.bias = as_device(linear_bias, torch.float16)

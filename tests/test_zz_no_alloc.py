@@ -45,6 +45,11 @@ def test_noalloc_matches_workspace_entry_point(cuda, M, K, N, bits, group):
     xd, wd, sd, bd = _dev(x, cuda), _dev(wq, cuda), _dev(s, cuda), _dev(b, cuda)
     ref = ops.qlinear(xd, wd, sd, bd, group, bits, out_dtype=torch.float32).cpu().numpy()
     exact = qa.quantized_matmul(x, wq, s, b, group, bits)
+    # a call with other activations first, so the static scratch holds stale,
+    # nonzero partials: a partial the checked calls failed to write would show
+    stale = _dev(rng.standard_normal((M, K)).astype(np.float16) * 3, cuda)
+    junk = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    assert _noalloc(stale, wd, sd, bd, group, bits, junk) == L.SC_OK, L.load().sc_last_error()
     for _ in range(2):  # two calls in a row reuse the same static scratch
         y = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
         st = _noalloc(xd, wd, sd, bd, group, bits, y)
@@ -56,8 +61,22 @@ def test_noalloc_matches_workspace_entry_point(cuda, M, K, N, bits, group):
 
 
 def test_noalloc_uses_the_scratch_for_split_k(cuda):
-    # the first shape above plans split-K partials, so the static scratch is exercised
-    assert 0 < L.load().sc_qlinear_workspace_bytes(1, 14336, 1024, 4) <= SCRATCH
+    """The first shape above is planned as split-K: its call enqueues the GEMV
+    and the reduce kernel (two launches), and its partials live in the static
+    scratch (a nonzero need that fits)."""
+    lib = L.load()
+    M, K, N, bits, group = 1, 14336, 1024, 4, 64
+    assert 0 < lib.sc_qlinear_workspace_bytes(M, K, N, bits) <= SCRATCH
+    rng = np.random.default_rng(3)
+    wq, s, b = qa.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float16), group, bits)
+    xd, wd, sd, bd = (_dev(a, cuda) for a in (rng.standard_normal((M, K)).astype(np.float16), wq, s, b))
+    y = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    n0 = lib.sc_launch_count()
+    assert _noalloc(xd, wd, sd, bd, group, bits, y) == L.SC_OK, lib.sc_last_error()
+    assert lib.sc_launch_count() - n0 == 2, "expected a split-K GEMV plus its reduce kernel"
+    torch.cuda.synchronize()
+    exact = qa.quantized_matmul(xd.cpu().numpy(), wq, s, b, group, bits)
+    assert rel_l2(y.cpu().numpy(), exact) <= 1e-3
 
 
 def test_noalloc_refuses_oversize_before_launch(cuda):
@@ -73,6 +92,6 @@ def test_noalloc_refuses_oversize_before_launch(cuda):
     st = _noalloc(x, wq, s, b, group, bits, y)
     assert st == L.SC_ERR_WORKSPACE
     msg = L.load().sc_last_error().decode()
-    assert "static scratch" in msg and str(need) in msg
+    assert "static scratch" in msg and f"M={M} K={K} N={N}" in msg
     torch.cuda.synchronize()
     assert bool((y == 7.0).all())
