@@ -183,10 +183,11 @@ int sc_quantize(const uint16_t* w, int rows, int K, int group_size, int bits,
  *   sequence goes to position *pos + s (all sequences share one length).
  *   Positions at or past Lmax / max_pos are not written.
  *   cos_tab/sin_tab: fp32 [max_pos, hd/2].
- *   q_out: fp32 [B*S, Hq*hd]; k_cache/v_cache: fp16 [B, Hkv, Lmax, hd]. */
+ *   q_out: fp32 [B*S, Hq*hd]; k_cache/v_cache: fp32 [B, Hkv, Lmax, hd] (fp32 as the
+ *   reference's cache is: RoPE's fp32 tables promote k, and v follows the fp32 hidden state). */
 int sc_rope_append(const float* qkv, int B, int S, int Hq, int Hkv, int hd,
                    const int32_t* pos, const float* cos_tab, const float* sin_tab, int max_pos,
-                   float* q_out, uint16_t* k_cache, uint16_t* v_cache, int Lmax,
+                   float* q_out, float* k_cache, float* v_cache, int Lmax,
                    cudaStream_t stream);
 
 /* Split-KV GQA flash-decode over the preallocated cache.  Replaces
@@ -194,7 +195,7 @@ int sc_rope_append(const float* qkv, int B, int S, int Hq, int Hkv, int hd,
  * softmax, @v).  Query s of sequence b sees keys [0, min(*pos + s, Lmax-1)].
  *   q: fp32 [B*S, Hq*hd]; out: fp16 or fp32 [B*S, Hq*hd]; splits 1..64. */
 size_t sc_flash_decode_workspace_bytes(int B, int S, int Hq, int hd, int splits);
-int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+int sc_flash_decode(const float* q, const float* k_cache, const float* v_cache,
                     const int32_t* pos, int B, int S, int Hq, int Hkv, int hd, int Lmax,
                     float scale, int splits, void* out, int out_dtype,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
@@ -204,7 +205,7 @@ int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_c
  * split-KV attention over positions [0, *pos] with the splits merged by the
  * last CTA of each (sequence, kv head) -- the work of sc_rope_append +
  * sc_flash_decode (parallel/attention.py:421-466) in one launch.
- *   qkv: fp32 [B, (Hq + 2*Hkv) * hd]; caches fp16 [B, Hkv, Lmax, hd];
+ *   qkv: fp32 [B, (Hq + 2*Hkv) * hd]; caches fp32 [B, Hkv, Lmax, hd];
  *   out: fp16 or fp32 [B, Hq*hd]; splits 1..64; workspace:
  *   sc_attn_decode_workspace_bytes;
  *   tickets: int32 [B*Hkv], zero before the first call and left zero by
@@ -217,7 +218,7 @@ size_t sc_attn_decode_workspace_bytes(int B, int Hq, int hd, int splits);
 int sc_attn_device_error(int reset);
 int sc_attn_decode(const float* qkv, int B, int Hq, int Hkv, int hd, const int32_t* pos,
                    const float* cos_tab, const float* sin_tab, int max_pos,
-                   uint16_t* k_cache, uint16_t* v_cache, int Lmax, float scale, int splits,
+                   float* k_cache, float* v_cache, int Lmax, float scale, int splits,
                    void* out, int out_dtype, void* workspace, size_t workspace_bytes,
                    int32_t* tickets, cudaStream_t stream);
 

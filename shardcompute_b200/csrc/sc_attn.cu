@@ -1,14 +1,18 @@
 // K4: RoPE + KV-cache append, and split-KV GQA flash-decode.
 //
-// KV cache layout (per layer, per rank): fp16 [B, Hkv, Lmax, hd], preallocated
+// KV cache layout (per layer, per rank): fp32 [B, Hkv, Lmax, hd], preallocated
 // once; token positions come from a device counter so one captured CUDA graph
-// serves every decode step.
+// serves every decode step.  The cache is fp32 because the reference's is:
+// RoPE multiplies q and k by fp32 cos/sin tables and the hidden state is fp32
+// after the first residual, so MLX's type promotion caches fp32 keys and
+// values (parallel/attention.py:427-436); an fp16 cache moved the hidden state
+// of a 32-layer Llama-3-8B about 6e-3 (relative L2) away from the reference.
 //
 // Flash-decode: grid (splits, Hkv, B*S).  A CTA owns one KV head and the G =
 // Hq/Hkv query heads that share it (GQA packed: K/V are read once for the
 // whole group, never repeated), and a contiguous range of keys.  Inside the
 // CTA, 4 warps interleave over key steps; a key row (hd fp16) is spread over
-// hd/8 lanes with one 16-byte load each, so a warp covers 32*8/hd keys per
+// hd/8 lanes with two 16-byte loads each, so a warp covers 32*8/hd keys per
 // step.  Each lane group keeps an online-softmax state (max, sum, o[8]) per
 // query head; the states are merged in shared memory and written as one
 // (max, sum, o[hd]) partial per split, which a second kernel merges.
@@ -18,10 +22,23 @@
 
 namespace sc {
 
+// 8 consecutive fp32 values (two 16-byte loads), zeros for a null pointer.
+__device__ __forceinline__ void ld_f8(const float* p, float (&v)[8]) {
+  if (!p) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    return;
+  }
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 __global__ void rope_append_kernel(const float* __restrict__ qkv, int S, int Hq, int Hkv, int hd,
                                    const int32_t* __restrict__ pos_ptr, const float* __restrict__ cos_tab,
                                    const float* __restrict__ sin_tab, int max_pos, float* __restrict__ q_out,
-                                   __half* __restrict__ kc, __half* __restrict__ vc, int Lmax) {
+                                   float* __restrict__ kc, float* __restrict__ vc, int Lmax) {
   pdl_trigger();
   pdl_wait();
   const int tok = blockIdx.x;  // b*S + s
@@ -46,14 +63,14 @@ __global__ void rope_append_kernel(const float* __restrict__ qkv, int S, int Hq,
         q_out[(size_t)tok * Hq * hd + h * hd + d + half] = o2;
       } else if (pos_ok) {
         const int kh = h - Hq;
-        __half* dst = kc + (((size_t)b * Hkv + kh) * Lmax + pos) * hd;
-        dst[d] = __float2half_rn(o1);
-        dst[d + half] = __float2half_rn(o2);
+        float* dst = kc + (((size_t)b * Hkv + kh) * Lmax + pos) * hd;
+        dst[d] = o1;
+        dst[d + half] = o2;
       }
     } else if (pos_ok) {
       const int r = it - (Hq + Hkv) * half;
       const int vh = r / hd, d = r % hd;
-      vc[(((size_t)b * Hkv + vh) * Lmax + pos) * hd + d] = __float2half_rn(src[(Hq + Hkv) * hd + vh * hd + d]);
+      vc[(((size_t)b * Hkv + vh) * Lmax + pos) * hd + d] = src[(Hq + Hkv) * hd + vh * hd + d];
     }
   }
 }
@@ -62,7 +79,7 @@ constexpr int FD_WARPS = 4;
 
 template <int HD, int G, typename OT>
 __global__ void __launch_bounds__(FD_WARPS * 32)
-flash_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
+flash_decode_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                     const int32_t* __restrict__ pos_ptr, int S, int Hq, int Hkv, int Lmax, float scale,
                     int splits, float* __restrict__ part, OT* __restrict__ out) {
   pdl_trigger();
@@ -98,29 +115,15 @@ flash_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
   }
-  const __half* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
-  const __half* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  const float* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  const float* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
 
   for (int k0 = k_beg + warp * KPS; k0 < k_end; k0 += FD_WARPS * KPS) {
     const int key = k0 + sub;
     const bool valid = key < k_end;
-    uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
-    if (valid) {
-      kv4 = *reinterpret_cast<const uint4*>(kbase + (size_t)key * HD + d0);
-      vv4 = *reinterpret_cast<const uint4*>(vbase + (size_t)key * HD + d0);
-    }
     float kf[8], vf[8];
-    {
-      const uint32_t kw[4] = {kv4.x, kv4.y, kv4.z, kv4.w};
-      const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = __half22float2(u32_as_h2(kw[i]));
-        const float2 c = __half22float2(u32_as_h2(vw[i]));
-        kf[2 * i] = a.x; kf[2 * i + 1] = a.y;
-        vf[2 * i] = c.x; vf[2 * i + 1] = c.y;
-      }
-    }
+    ld_f8(valid ? kbase + (size_t)key * HD + d0 : nullptr, kf);
+    ld_f8(valid ? vbase + (size_t)key * HD + d0 : nullptr, vf);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float dot = 0.f;
@@ -334,7 +337,7 @@ __global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq
 }
 
 template <int HD, int G, typename OT>
-static int launch_fd(const float* q, const __half* kc, const __half* vc, const int32_t* pos, int B, int S, int Hq,
+static int launch_fd(const float* q, const float* kc, const float* vc, const int32_t* pos, int B, int S, int Hq,
                      int Hkv, int Lmax, float scale, int splits, float* part, OT* out, cudaStream_t stream) {
   dim3 grid(splits, Hkv, B * S);
   ::sc::launch(flash_decode_kernel<HD, G, OT>, grid, FD_WARPS * 32, 0, stream, q, kc, vc, pos, S, Hq, Hkv, Lmax, scale, splits,
@@ -346,7 +349,7 @@ static int launch_fd(const float* q, const __half* kc, const __half* vc, const i
 }
 
 template <int HD, typename OT>
-static int dispatch_g(int G, const float* q, const __half* kc, const __half* vc, const int32_t* pos, int B, int S,
+static int dispatch_g(int G, const float* q, const float* kc, const float* vc, const int32_t* pos, int B, int S,
                       int Hq, int Hkv, int Lmax, float scale, int splits, float* part, OT* out, cudaStream_t stream) {
   switch (G) {
     case 1: return launch_fd<HD, 1, OT>(q, kc, vc, pos, B, S, Hq, Hkv, Lmax, scale, splits, part, out, stream);
@@ -377,12 +380,12 @@ static int dispatch_g(int G, const float* q, const __half* kc, const __half* vc,
 // stops computing (its output is undefined).
 
 constexpr int AD_WARPS = 8;
-constexpr int AD_TK = 64;  // keys per tile
+constexpr int AD_TK = 32;  // keys per tile (fp32 K and V: 32 KB per tile pair)
 constexpr int AD_NB = 2;   // tiles in flight
 __device__ int g_attn_error = 0;
 
 __host__ __device__ constexpr int ad_groups(int hd) { return AD_WARPS * (32 / (hd / 8)); }  // lane groups of a CTA
-__host__ __device__ constexpr size_t ad_kv_bytes(int hd) { return (size_t)AD_NB * 2 * AD_TK * hd * 2; }
+__host__ __device__ constexpr size_t ad_kv_bytes(int hd) { return (size_t)AD_NB * 2 * AD_TK * hd * 4; }
 __host__ __device__ constexpr size_t ad_smem_bytes(int hd, int G) {
   // the tile buffers, reused after the last tile for the lane groups' partial outputs
   return ad_kv_bytes(hd) > (size_t)ad_groups(hd) * G * hd * 4 ? ad_kv_bytes(hd) : (size_t)ad_groups(hd) * G * hd * 4;
@@ -399,7 +402,7 @@ template <int HD, int G, typename OT>
 __global__ void __launch_bounds__(AD_WARPS * 32)
 attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ pos_ptr,
                    const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int max_pos, int Hq,
-                   int Hkv, int Lmax, float scale, int splits, __half* __restrict__ kc, __half* __restrict__ vc,
+                   int Hkv, int Lmax, float scale, int splits, float* __restrict__ kc, float* __restrict__ vc,
                    float* __restrict__ part, int* __restrict__ tickets, OT* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
@@ -425,21 +428,21 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   const bool owner = append && pos >= k_beg && pos < k_end;
   const int width = (Hq + 2 * Hkv) * HD;
   const float* src = qkv + (size_t)b * width;
-  const __half* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
-  const __half* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  const float* kbase = kc + ((size_t)b * Hkv + kvh) * Lmax * HD;
+  const float* vbase = vc + ((size_t)b * Hkv + kvh) * Lmax * HD;
 
   extern __shared__ __align__(128) unsigned char ad_smem[];
-  __half* s_kv = reinterpret_cast<__half*>(ad_smem);  // [AD_NB][2][AD_TK][HD]
+  float* s_kv = reinterpret_cast<float*>(ad_smem);  // [AD_NB][2][AD_TK][HD]
   __shared__ __align__(8) uint64_t s_full[AD_NB];
   __shared__ int s_abort;
   __shared__ float s_q[G][HD];
-  __shared__ __align__(16) __half s_knew[HD], s_vnew[HD];
+  __shared__ __align__(16) float s_knew[HD], s_vnew[HD];
 
   auto issue = [&](int t) {  // thread 0: bulk copies of tile t's K and V rows
     const int kt = k_beg + t * AD_TK;
-    const uint32_t bytes = (uint32_t)(min(AD_TK, k_end - kt) * HD * 2);
+    const uint32_t bytes = (uint32_t)(min(AD_TK, k_end - kt) * HD * 4);
     const int bi = t % AD_NB;
-    __half* dk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
+    float* dk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
     mbar_arrive_expect_tx(&s_full[bi], 2 * bytes);
     bulk_load(dk, kbase + (size_t)kt * HD, bytes, &s_full[bi]);
     bulk_load(dk + AD_TK * HD, vbase + (size_t)kt * HD, bytes, &s_full[bi]);
@@ -464,21 +467,20 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
   if (owner) {
     const float* kh = src + (size_t)(Hq + kvh) * HD;
     const float* vh = src + (size_t)(Hq + Hkv + kvh) * HD;
-    __half* kdst = kc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
-    __half* vdst = vc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
+    float* kdst = kc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
+    float* vdst = vc + (((size_t)b * Hkv + kvh) * Lmax + pos) * HD;
     for (int d = threadIdx.x; d < HALF; d += NT) {
       float o1, o2;
       rope_pair<HD>(kh[d], kh[d + HALF], cos_tab[(size_t)pos * HALF + d], sin_tab[(size_t)pos * HALF + d], o1, o2);
-      const __half h1 = __float2half_rn(o1), h2 = __float2half_rn(o2);
-      s_knew[d] = h1;
-      s_knew[d + HALF] = h2;
-      kdst[d] = h1;
-      kdst[d + HALF] = h2;
+      s_knew[d] = o1;
+      s_knew[d + HALF] = o2;
+      kdst[d] = o1;
+      kdst[d + HALF] = o2;
     }
     for (int d = threadIdx.x; d < HD; d += NT) {
-      const __half hv = __float2half_rn(vh[d]);
-      s_vnew[d] = hv;
-      vdst[d] = hv;
+      const float v = vh[d];
+      s_vnew[d] = v;
+      vdst[d] = v;
     }
   }
   __syncthreads();
@@ -511,8 +513,8 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
     if (s_abort) break;
     const int kt = k_beg + t * AD_TK;
     const int nk = min(AD_TK, k_end - kt);
-    const __half* tk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
-    const __half* tv = tk + AD_TK * HD;
+    const float* tk = s_kv + (size_t)(bi * 2) * AD_TK * HD;
+    const float* tv = tk + AD_TK * HD;
     // (1) scores: only the steps that hold keys; the G per-lane dot products
     // are summed over the LPK lanes of a key with a transposing butterfly
     // (G - 1 + log2(LPK / G) shuffles instead of G * log2(LPK))
@@ -520,16 +522,8 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
     for (int st = 0; st < steps; ++st) {
       const int kk = st * STEP + warp * KPS + sub;
       const bool valid = kk < nk;
-      uint4 kv4 = make_uint4(0, 0, 0, 0);
-      if (valid) kv4 = *reinterpret_cast<const uint4*>((owner && kt + kk == pos ? s_knew : tk + (size_t)kk * HD) + d0);
       float kf[8];
-      const uint32_t kw[4] = {kv4.x, kv4.y, kv4.z, kv4.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = __half22float2(u32_as_h2(kw[i]));
-        kf[2 * i] = a.x;
-        kf[2 * i + 1] = a.y;
-      }
+      ld_f8(valid ? (owner && kt + kk == pos ? s_knew : tk + (size_t)kk * HD) + d0 : nullptr, kf);
       float dv[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -597,15 +591,8 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
 #pragma unroll
     for (int kk = warp * KPS + sub; kk < AD_TK; kk += STEP) {
       if (kk >= nk) break;  // keys ascend with kk for this lane
-      const uint4 vv4 = *reinterpret_cast<const uint4*>((owner && kt + kk == pos ? s_vnew : tv + (size_t)kk * HD) + d0);
       float vf[8];
-      const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 c = __half22float2(u32_as_h2(vw[i]));
-        vf[2 * i] = c.x;
-        vf[2 * i + 1] = c.y;
-      }
+      ld_f8((owner && kt + kk == pos ? s_vnew : tv + (size_t)kk * HD) + d0, vf);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float pr = s_s[g][kk];
@@ -674,7 +661,7 @@ attn_decode_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ po
 
 template <int HD, int G, typename OT>
 static int launch_ad(const float* qkv, const int32_t* pos, const float* cos_tab, const float* sin_tab, int max_pos,
-                     int B, int Hq, int Hkv, int Lmax, float scale, int splits, __half* kc, __half* vc, float* part,
+                     int B, int Hq, int Hkv, int Lmax, float scale, int splits, float* kc, float* vc, float* part,
                      int* tickets, OT* out, cudaStream_t stream) {
   auto kern = attn_decode_kernel<HD, G, OT>;
   const size_t smem = ad_smem_bytes(HD, G);
@@ -690,7 +677,7 @@ static int launch_ad(const float* qkv, const int32_t* pos, const float* cos_tab,
 
 template <int HD, typename OT>
 static int dispatch_ad(int G, const float* qkv, const int32_t* pos, const float* cos_tab, const float* sin_tab,
-                       int max_pos, int B, int Hq, int Hkv, int Lmax, float scale, int splits, __half* kc, __half* vc,
+                       int max_pos, int B, int Hq, int Hkv, int Lmax, float scale, int splits, float* kc, float* vc,
                        float* part, int* tickets, OT* out, cudaStream_t stream) {
   switch (G) {
     case 1: return launch_ad<HD, 1, OT>(qkv, pos, cos_tab, sin_tab, max_pos, B, Hq, Hkv, Lmax, scale, splits, kc, vc, part, tickets, out, stream);
@@ -707,14 +694,14 @@ static int dispatch_ad(int G, const float* qkv, const int32_t* pos, const float*
 extern "C" {
 
 int sc_rope_append(const float* qkv, int B, int S, int Hq, int Hkv, int hd, const int32_t* pos,
-                   const float* cos_tab, const float* sin_tab, int max_pos, float* q_out, uint16_t* k_cache,
-                   uint16_t* v_cache, int Lmax, cudaStream_t stream) {
+                   const float* cos_tab, const float* sin_tab, int max_pos, float* q_out, float* k_cache,
+                   float* v_cache, int Lmax, cudaStream_t stream) {
   SC_REQUIRE(hd > 0 && hd % 2 == 0, SC_ERR_SHAPE, "rope_append: head_dim must be even");
   SC_REQUIRE(Hq > 0 && Hkv > 0 && B > 0 && S > 0, SC_ERR_SHAPE, "rope_append: empty shape");
   SC_REQUIRE(qkv && pos && cos_tab && sin_tab && q_out && k_cache && v_cache, SC_ERR_ARG,
              "rope_append: null pointer");
   ::sc::launch(sc::rope_append_kernel, B * S, 256, 0, stream, qkv, S, Hq, Hkv, hd, pos, cos_tab, sin_tab, max_pos, q_out,
-                                                    (__half*)k_cache, (__half*)v_cache, Lmax);
+                                                    k_cache, v_cache, Lmax);
   return sc::check_launch("rope_append");
 }
 
@@ -723,7 +710,7 @@ size_t sc_flash_decode_workspace_bytes(int B, int S, int Hq, int hd, int splits)
   return (size_t)B * S * Hq * splits * (hd + 2) * sizeof(float);
 }
 
-int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos, int B,
+int sc_flash_decode(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos, int B,
                     int S, int Hq, int Hkv, int hd, int Lmax, float scale, int splits, void* out, int out_dtype,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   SC_REQUIRE(hd == 64 || hd == 128, SC_ERR_UNSUPPORTED, "flash_decode: head_dim %d unsupported (64, 128)", hd);
@@ -736,8 +723,8 @@ int sc_flash_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_c
   SC_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), SC_ERR_WORKSPACE,
              "flash_decode: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
   const int G = Hq / Hkv;
-  const __half* kc = (const __half*)k_cache;
-  const __half* vc = (const __half*)v_cache;
+  const float* kc = k_cache;
+  const float* vc = v_cache;
   float* part = (float*)workspace;
   if (hd == 128) {
     if (out_dtype == SC_F16)
@@ -768,7 +755,7 @@ int sc_attn_device_error(int reset) {
 }
 
 int sc_attn_decode(const float* qkv, int B, int Hq, int Hkv, int hd, const int32_t* pos, const float* cos_tab,
-                   const float* sin_tab, int max_pos, uint16_t* k_cache, uint16_t* v_cache, int Lmax, float scale,
+                   const float* sin_tab, int max_pos, float* k_cache, float* v_cache, int Lmax, float scale,
                    int splits, void* out, int out_dtype, void* workspace, size_t workspace_bytes, int32_t* tickets,
                    cudaStream_t stream) {
   SC_REQUIRE(hd == 64 || hd == 128, SC_ERR_UNSUPPORTED, "attn_decode: head_dim %d unsupported (64, 128)", hd);
@@ -783,8 +770,8 @@ int sc_attn_decode(const float* qkv, int B, int Hq, int Hkv, int hd, const int32
              "attn_decode: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
   SC_REQUIRE(splits == 1 || tickets, SC_ERR_ARG, "attn_decode: split-KV needs the ticket array");
   const int G = Hq / Hkv;
-  __half* kc = (__half*)k_cache;
-  __half* vc = (__half*)v_cache;
+  float* kc = k_cache;
+  float* vc = v_cache;
   float* part = (float*)workspace;
   if (hd == 128) {
     if (out_dtype == SC_F16)

@@ -54,7 +54,9 @@ struct QSeg {
 struct QGemvParams {
   const void* x;
   int ldx;
-  int M;   // rows of x in this pass (<= 16)
+  int M;   // rows of the B tile in this pass (<= 16): 2 * Mr when hilo
+  int Mr;  // rows of x in this pass
+  int hilo;  // batched kernel: B rows [0, Mr) carry fp16(x), rows [Mr, 2 Mr) the fp16 remainder x - fp16(x)
   int K;
   const uint16_t* norm_w;
   float eps;
@@ -123,11 +125,11 @@ template <int BITS, bool NORM, typename XT>
 __device__ __forceinline__ void stage_x(const QGemvParams& p, __half* xs, float* s_rms, int kc0, int kc1, int tid,
                                         int nthreads, int bar_id) {
   using TR = QTraits<BITS>;
-  const int M = p.M;
+  const int M = p.M, Mr = p.Mr;
   const int rowlen = M * TR::NMMA * 4 + 8;
   const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
   if (NORM) {
-    for (int m = warp; m < M; m += nwarps) {
+    for (int m = warp; m < Mr; m += nwarps) {
       float ss = 0.f;
       for (int k = lane; k < p.K; k += 32) {
         const float v = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
@@ -142,7 +144,7 @@ __device__ __forceinline__ void stage_x(const QGemvParams& p, __half* xs, float*
   const int nkc = kc1 - kc0;
   const int k0 = kc0 * TR::KPC;
   const int span = nkc * TR::KPC;
-  for (int idx = tid; idx < span * M; idx += nthreads) {
+  for (int idx = tid; idx < span * Mr; idx += nthreads) {
     const int m = idx / span, kl = idx % span;
     const int k = k0 + kl;
     float v = 0.f;
@@ -150,7 +152,9 @@ __device__ __forceinline__ void stage_x(const QGemvParams& p, __half* xs, float*
       v = ld_x<XT>(p.x, (size_t)m * p.ldx + k);
       if (NORM) v = (v / s_rms[m]) * __half2float(__ushort_as_half(p.norm_w[k]));
     }
-    xs[xslot<BITS>(kl, m, M)] = __float2half_rn(v);
+    const __half h = __float2half_rn(v);
+    xs[xslot<BITS>(kl, m, M)] = h;
+    if (p.hilo) xs[xslot<BITS>(kl, m + Mr, M)] = __float2half_rn(v - __half2float(h));
   }
   // zero the padding halves so no uninitialised value is ever read
   for (int r = tid; r < nkc * 4; r += nthreads)
@@ -172,8 +176,8 @@ __device__ __forceinline__ void epilogue(const QGemvParams& p, int split, bool a
     return;
   }
   if (p.splits > 1) {
-    p.partial[(((size_t)0 * p.splits + split) * p.M + col) * p.N + row] = v[0];
-    if (DUAL) p.partial[(((size_t)1 * p.splits + split) * p.M + col) * p.N + row] = v[DUAL ? 1 : 0];
+    p.partial[(((size_t)0 * p.splits + split) * p.Mr + col) * p.N + row] = v[0];
+    if (DUAL) p.partial[(((size_t)1 * p.splits + split) * p.Mr + col) * p.N + row] = v[DUAL ? 1 : 0];
     return;
   }
   float out;
@@ -362,14 +366,21 @@ qgemv_kernel(const QGemvParams p) {
       const int mt = rr >> 2, r = rr & 3;
       const int row = n0 + (l >> 2) + 8 * (r >> 1);
       const int col = mt * 8 + 2 * (l & 3) + (r & 1);
-      if (row >= p.N || col >= M) continue;
+      if (row >= p.N || col >= p.Mr) continue;
+      // the remainder column of a hi / lo pass: same tile row, B column col + Mr
+      const int cl = col + p.Mr;
+      const int l2 = (l & ~3) | ((cl & 7) >> 1), mt2 = cl >> 3, r2 = (r & 2) | (cl & 1);
       float v[NACC];
 #pragma unroll
       for (int a = 0; a < NACC; ++a) {
-        float sacc = 0.f;
+        float sacc = 0.f, slo = 0.f;
 #pragma unroll
         for (int w = 0; w < QG_WARPS; ++w) sacc += red[(w * 32 + l) * RPL + (a * MT + mt) * 4 + r];
-        v[a] = sacc;
+        if (p.hilo) {
+#pragma unroll
+          for (int w = 0; w < QG_WARPS; ++w) slo += red[(w * 32 + l2) * RPL + (a * MT + mt2) * 4 + r2];
+        }
+        v[a] = sacc + slo;
       }
       epilogue<EPI, YT>(p, split, false, row, col, v);
     }
@@ -757,14 +768,21 @@ qgemv_tma_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ 
       const int mt = rr >> 2, r = rr & 3;
       const int row = n0 + tile_row((l >> 2) + 8 * (r >> 1));
       const int col = mt * 8 + 2 * (l & 3) + (r & 1);
-      if (row >= p.N || col >= M) continue;
+      if (row >= p.N || col >= p.Mr) continue;
+      // the remainder column of a hi / lo pass: same tile row, B column col + Mr
+      const int cl = col + p.Mr;
+      const int l2 = (l & ~3) | ((cl & 7) >> 1), mt2 = cl >> 3, r2 = (r & 2) | (cl & 1);
       float v[NACC];
 #pragma unroll
       for (int a = 0; a < NACC; ++a) {
-        float sacc = 0.f;
+        float sacc = 0.f, slo = 0.f;
 #pragma unroll
         for (int w = 0; w < TC_NCW; ++w) sacc += rb[(w * 32 + l) * RPL + (a * MT + mt) * 4 + r];
-        v[a] = sacc;
+        if (p.hilo) {
+#pragma unroll
+          for (int w = 0; w < TC_NCW; ++w) slo += rb[(w * 32 + l2) * RPL + (a * MT + mt2) * 4 + r2];
+        }
+        v[a] = sacc + slo;
       }
       epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, col, v);
     }
@@ -1461,13 +1479,13 @@ __global__ void qgemv_splitk_reduce(const QGemvParams p) {
   // partials: the workspace then holds stale values, so leave y untouched
   // (the error word stays set until sc_qgemv_device_error(1) clears it).
   if (*reinterpret_cast<volatile int*>(&g_qgemv_error)) return;
-  const size_t total = (size_t)p.M * p.N;
+  const size_t total = (size_t)p.Mr * p.N;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
     const int col = (int)(e / p.N), row = (int)(e % p.N);
     float v[2] = {0.f, 0.f};
     const int nacc = (EPI == SC_EPI_SWIGLU) ? 2 : 1;
     for (int a = 0; a < nacc; ++a)
-      for (int s = 0; s < p.splits; ++s) v[a] += p.partial[(((size_t)a * p.splits + s) * p.M + col) * p.N + row];
+      for (int s = 0; s < p.splits; ++s) v[a] += p.partial[(((size_t)a * p.splits + s) * p.Mr + col) * p.N + row];
     float out;
     if (EPI == SC_EPI_SWIGLU) {
       out = silu_f32(v[0]) * v[1];
@@ -1742,7 +1760,7 @@ static int launch_qgemv(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, 
     int st = check_launch("qgemv");
     if (st != SC_OK || p.splits == 1) return st;
   }
-  const size_t total = (size_t)p.M * p.N;
+  const size_t total = (size_t)p.Mr * p.N;
   const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)4 * sm_count());
   ::sc::launch(qgemv_splitk_reduce<EPI, YT>, rb, 256, 0, stream, p);
   return check_launch("qgemv_splitk_reduce");
@@ -1760,7 +1778,7 @@ static int launch_qgemv_fx(QGemvParams& p, const TmaPlan* tp, const TmaMaps* map
   ::sc::launch(kern, grid, TC_THREADS, tp->smem, stream, p, tp->geo, *maps);
   int st = check_launch("qgemv_fx");
   if (st != SC_OK || p.splits == 1 || tp->geo.atomic_out) return st;
-  const size_t total = (size_t)p.M * p.N;
+  const size_t total = (size_t)p.Mr * p.N;
   const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)4 * sm_count());
   ::sc::launch(qgemv_splitk_reduce<EPI, YT>, rb, 256, 0, stream, p);
   return check_launch("qgemv_splitk_reduce");
@@ -1837,11 +1855,12 @@ struct PassPlan {
 
 static bool aligned(const void* ptr, size_t a) { return ((uintptr_t)ptr % a) == 0; }
 
-static PassPlan plan_pass(int mb, int K, int N, int bits, int group, int nacc, bool tma_ok, bool atomic_ok) {
+static PassPlan plan_pass(int mb, int K, int N, int bits, int group, int nacc, bool tma_ok, bool atomic_ok,
+                          bool allow_fx = true) {
   PassPlan pp{};
   const int MT = mb > 8 ? 2 : 1;
   if (tma_ok && !knobs().ldg) {
-    pp.fx = fx_eligible(mb, bits, group) && !knobs().nofx;
+    pp.fx = allow_fx && fx_eligible(mb, bits, group) && !knobs().nofx;
     pp.tp = plan_tma(mb, K, N, bits, group, nacc, MT, pp.fx);
     if (!pp.tp.ok && pp.fx) {
       pp.fx = false;
@@ -1860,9 +1879,34 @@ static PassPlan plan_pass(int mb, int K, int N, int bits, int group, int nacc, b
   return pp;
 }
 
+// mb: rows of x in the pass (partials are kept per row of x, after the hi /
+// lo columns of a batched pass were added)
 static size_t pass_workspace(const PassPlan& pp, int mb, int N, int nacc) {
   if (pp.sp.splits <= 1 || (pp.tma && pp.tp.geo.atomic_out)) return 0;
   return (size_t)nacc * pp.sp.splits * mb * N * sizeof(float);
+}
+
+// One pass over the weights: up to 16 rows of x through the factored decode
+// kernel when it is eligible; otherwise up to 8 rows through the batched
+// kernel, whose B tile then carries each row twice -- fp16(x) and the fp16
+// remainder x - fp16(x) -- so activations keep ~22 bits there too.
+struct RowPass {
+  int mb;     // rows of x
+  bool hilo;  // batched pass with hi / lo rows
+  PassPlan pp;
+};
+
+static RowPass plan_rows(int rem, int K, int N, int bits, int group, int nacc, bool tma_ok, bool atomic_ok) {
+  RowPass r;
+  r.mb = std::min(16, rem);
+  r.pp = plan_pass(r.mb, K, N, bits, group, nacc, tma_ok, atomic_ok);
+  r.hilo = false;
+  if (!r.pp.fx) {
+    r.mb = std::min(8, rem);
+    r.hilo = true;
+    r.pp = plan_pass(2 * r.mb, K, N, bits, group, nacc, tma_ok, atomic_ok, false);
+  }
+  return r;
 }
 
 static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_w, float eps,
@@ -1918,10 +1962,13 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
   const bool atomic_ok = epi == SC_EPI_RESIDUAL && y_dtype == SC_F32 && (const void*)residual == (const void*)y &&
                          ldr == ldy;
 
-  for (int m0 = 0; m0 < M; m0 += 16) {
-    const int mb = std::min(16, M - m0);
-    PassPlan pp = plan_pass(mb, K, N, bits, group, nacc, tma_ok, atomic_ok);
-    p.M = mb;
+  for (int m0 = 0; m0 < M;) {
+    const RowPass rp = plan_rows(M - m0, K, N, bits, group, nacc, tma_ok, atomic_ok);
+    const int mb = rp.mb;
+    PassPlan pp = rp.pp;
+    p.Mr = mb;
+    p.hilo = rp.hilo ? 1 : 0;
+    p.M = rp.hilo ? 2 * mb : mb;
     p.x = static_cast<const char*>(x) + (size_t)m0 * ldx * xsz;
     p.y = static_cast<char*>(y) + (size_t)m0 * ldy * ysz;
     p.residual = residual ? residual + (size_t)m0 * ldr : nullptr;
@@ -1933,7 +1980,12 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
       tp = &pp.tp;
     } else if (pp.tma) {
       // tensor maps unavailable: plan this pass for the direct-load kernel
-      pp = plan_pass(mb, K, N, bits, group, nacc, false, false);
+      // (hi / lo rows when they fit its 16-row B tile)
+      if (!p.hilo && 2 * mb <= 16) {
+        p.hilo = 1;
+        p.M = 2 * mb;
+      }
+      pp = plan_pass(p.M, K, N, bits, group, nacc, false, false, false);
     }
     p.splits = pp.sp.splits;
     p.chunks_per_split = pp.sp.chunks_per_split;
@@ -1957,12 +2009,13 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
         st = ngc == 1 ? dispatch_fx<8, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
                       : dispatch_fx<8, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
     } else if (bits == 4)
-      st = mb > 8 ? dispatch_epi<4, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
-                  : dispatch_epi<4, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
+      st = p.M > 8 ? dispatch_epi<4, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
+                   : dispatch_epi<4, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
     else
-      st = mb > 8 ? dispatch_epi<8, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
-                  : dispatch_epi<8, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
+      st = p.M > 8 ? dispatch_epi<8, 2>(p, tp, &maps, epi, x_dtype, y_dtype, stream)
+                   : dispatch_epi<8, 1>(p, tp, &maps, epi, x_dtype, y_dtype, stream);
     if (st != SC_OK) return st;
+    m0 += mb;
   }
   return SC_OK;
 }
@@ -1976,12 +2029,17 @@ size_t qlinear_workspace_need(int M, int K, int N, int group, int bits, bool tma
   if (M < 1 || K < 1 || N < 1 || (bits != 4 && bits != 8)) return 0;
   if ((group != 32 && group != 64 && group != 128) || K % group) return 0;
   size_t best = 0;
-  for (int m0 = 0; m0 < M; m0 += 16) {
-    const int mb = std::min(16, M - m0);
+  for (int m0 = 0; m0 < M;) {
+    int step = 16;
     for (int tma = 0; tma < (tma_ok ? 2 : 1); ++tma) {
-      PassPlan pp = plan_pass(mb, K, N, bits, group, 1, tma != 0, false);
-      best = std::max(best, pass_workspace(pp, mb, N, 1));
+      const RowPass rp = plan_rows(M - m0, K, N, bits, group, 1, tma != 0, false);
+      best = std::max(best, pass_workspace(rp.pp, rp.mb, N, 1));
+      // the direct-load plan a pass falls back to when the tensor maps are refused
+      const int mv = (rp.hilo || 2 * rp.mb <= 16) ? 2 * rp.mb : rp.mb;
+      best = std::max(best, pass_workspace(plan_pass(mv, K, N, bits, group, 1, false, false, false), rp.mb, N, 1));
+      step = std::min(step, rp.mb);
     }
+    m0 += step;
   }
   return best;
 }
@@ -1999,8 +2057,11 @@ size_t sc_qlinear_workspace_bytes(int M, int K, int N, int bits) {
     for (int group : {32, 64, 128})
       for (int tma = 0; tma < 2; ++tma) {
         if (K % group) continue;
-        sc::PassPlan pp = sc::plan_pass(mm, K, N, bits, group, 2, tma != 0, false);
-        best = std::max(best, sc::pass_workspace(pp, mm, N, 2));
+        const sc::RowPass rp = sc::plan_rows(mm, K, N, bits, group, 2, tma != 0, false);
+        best = std::max(best, sc::pass_workspace(rp.pp, rp.mb, N, 2));
+        const int mv = 2 * rp.mb <= 16 ? 2 * rp.mb : rp.mb;
+        best = std::max(best, sc::pass_workspace(sc::plan_pass(mv, K, N, bits, group, 2, false, false, false), rp.mb,
+                                                 N, 2));
       }
   return best;
 }

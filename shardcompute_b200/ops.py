@@ -35,6 +35,12 @@ def _cuda(*ts: Optional[torch.Tensor]) -> None:
             raise RuntimeError("libsc_b200 ops take CUDA tensors only (no CPU path)")
 
 
+def _f32_cache(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t.dtype != torch.float32:
+            raise ValueError(f"KV cache must be float32 (the reference caches fp32 keys/values), got {t.dtype}")
+
+
 def _p(t: Optional[torch.Tensor]):
     return None if t is None else t.data_ptr()
 
@@ -194,6 +200,7 @@ def rope_append(qkv: torch.Tensor, B: int, S: int, Hq: int, Hkv: int, hd: int, p
                 cos_tab: torch.Tensor, sin_tab: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor,
                 v_cache: torch.Tensor) -> None:
     _cuda(qkv, pos, cos_tab, sin_tab, q_out, k_cache, v_cache)
+    _f32_cache(k_cache, v_cache)
     Lmax = k_cache.shape[2]
     L.call("sc_rope_append", _p(qkv), B, S, Hq, Hkv, hd, _p(pos), _p(cos_tab), _p(sin_tab), cos_tab.shape[0],
            _p(q_out), _p(k_cache), _p(v_cache), Lmax, stream_handle(qkv.device))
@@ -207,6 +214,7 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
                  Hq: int, Hkv: int, hd: int, splits: int, out: torch.Tensor,
                  workspace: Optional[torch.Tensor] = None, scale: Optional[float] = None) -> torch.Tensor:
     _cuda(q, k_cache, v_cache, pos, out)
+    _f32_cache(k_cache, v_cache)
     nbytes = flash_decode_workspace_bytes(B, S, Hq, hd, splits)
     if workspace is None:
         workspace = Workspace.get(nbytes, q.device)
@@ -229,6 +237,7 @@ def attn_decode(qkv: torch.Tensor, B: int, Hq: int, Hkv: int, hd: int, pos: torc
     (+ merge) in one launch.  ``tickets`` is int32 [B*Hkv], zero on entry
     and left zero."""
     _cuda(qkv, pos, cos_tab, sin_tab, k_cache, v_cache, out, tickets, workspace)
+    _f32_cache(k_cache, v_cache)
     nbytes = attn_decode_workspace_bytes(B, Hq, hd, splits)
     if workspace is None:
         workspace = Workspace.get(nbytes, qkv.device)

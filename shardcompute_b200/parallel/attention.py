@@ -13,7 +13,8 @@ segments), ``sc_rope_append`` (RoPE + cache write), ``sc_flash_decode``
 (split-KV online softmax) and the o_proj GEMV.
 
 The cache is a ``KVCache`` handle over preallocated ``[B, Hkv/TP, Lmax, hd]``
-fp16 buffers with the position kept on the device; ``cache[0]`` / ``cache[1]``
+fp32 buffers (the reference caches fp32: RoPE's fp32 tables promote k) with
+the position kept on the device; ``cache[0]`` / ``cache[1]``
 return the filled ``[B, Hkv/TP, L, hd]`` views, so code that reads
 ``past_key_value[0].shape[2]`` as the cached length keeps working.
 """
@@ -81,7 +82,7 @@ class KVCache:
     """Preallocated per-layer KV cache with a device-side length counter."""
 
     def __init__(self, batch: int, kv_heads: int, max_len: int, head_dim: int, device: torch.device):
-        self.k = torch.zeros(batch, kv_heads, max_len, head_dim, dtype=torch.float16, device=device)
+        self.k = torch.zeros(batch, kv_heads, max_len, head_dim, dtype=torch.float32, device=device)
         self.v = torch.zeros_like(self.k)
         self.pos = torch.zeros(1, dtype=torch.int32, device=device)
         self.length = 0
@@ -197,14 +198,14 @@ class ParallelAttention:
         q = torch.empty(B * S, self.local_hidden, dtype=torch.float32, device=dev)
         ops.rope_append(qkv, B, S, self.local_num_heads, self.local_num_kv_heads, self.head_dim, cache.pos, cos, sin,
                         q, cache.k, cache.v)
-        attn = torch.empty(B * S, self.local_hidden, dtype=torch.float16, device=dev)
+        attn = torch.empty(B * S, self.local_hidden, dtype=torch.float32, device=dev)
         splits = 1 if S > 1 else max(1, min(64, math.ceil(296 / max(1, self.local_num_kv_heads * B)),
                                             math.ceil((cache.length + 1) / 64)))
         ops.flash_decode(q, cache.k, cache.v, cache.pos, B, S, self.local_num_heads, self.local_num_kv_heads,
                          self.head_dim, splits, attn, scale=self.scale)
         cache.advance(S)
         attn = attn.view(B, S, self.local_hidden)
-        part = self.o_proj.forward_partial(attn if self.use_quantized else attn.float())
+        part = self.o_proj.forward_partial(attn)
         return part, (cache if use_cache else None)
 
     async def forward(self, hidden_states: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,

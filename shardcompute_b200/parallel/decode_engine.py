@@ -15,8 +15,8 @@ worker/executor.py:229-325), re-laid for B200:
   the transport's limit); rank 0 folds the residual into its partial so the
   all-reduce output *is* the new hidden state; greedy sampling gathers only
   (max, index) per rank instead of the vocab-split logits;
-* the residual stream and every GEMV input are fp32 (the GEMV splits them into exact fp16 hi / lo parts), KV cache fp16
-  ``[L, 2, B, Hkv/TP, Lmax, hd]``, preallocated;
+* the residual stream and every GEMV input are fp32 (the GEMV splits them into exact fp16 hi / lo parts), KV cache fp32
+  ``[L, 2, B, Hkv/TP, Lmax, hd]`` (as the reference's: RoPE's fp32 tables promote k), preallocated;
 * positions and token ids live in device buffers, so one decode step is
   captured once in a CUDA graph and replayed; each replay reads the token the
   previous replay wrote and advances the position counter on the device.
@@ -75,7 +75,7 @@ class DecodeEngine:
         self.bits, self.group = weights.bits, weights.group
         self.eps = cfg.rms_norm_eps
         nl = cfg.num_layers
-        self.kv = torch.zeros(nl, 2, self.B, self.Hkv, self.Lmax, self.hd, dtype=torch.float16, device=dev)
+        self.kv = torch.zeros(nl, 2, self.B, self.Hkv, self.Lmax, self.hd, dtype=torch.float32, device=dev)
         cos, sin = rope_table(self.hd, self.Lmax, cfg.rope_theta)
         self.cos = torch.from_numpy(cos).to(dev)
         self.sin = torch.from_numpy(sin).to(dev)
@@ -294,7 +294,7 @@ class DecodeEngine:
 
     def kv_bytes_per_step(self) -> int:
         """KV-cache bytes one decode step reads at the current length (all layers)."""
-        return self.cfg.num_layers * 2 * self.B * self.Hkv * self.host_pos * self.hd * 2
+        return self.cfg.num_layers * 2 * self.B * self.Hkv * self.host_pos * self.hd * self.kv.element_size()
 
     def prefill(self, input_ids: torch.Tensor):
         """Run the prompt ``[B, S]`` through the model; the first generated

@@ -48,7 +48,8 @@ def ref_exact(x, wq, s, b, group, bits):
 
 def assert_kernel_close(y, refs, tol):
     """The decode kernel (M * groups-per-chunk <= 4) keeps the weights exact;
-    the batched kernel rounds them once to fp16.  ``refs`` holds the float64
+    the batched kernel rounds them once to fp16 (``mx.dequantize``).  Both
+    carry x to ~22 bits (fp16 high + low parts).  ``refs`` holds the float64
     product for each definition; the output must match one of them."""
     y = np.asarray(y)
     rows = y.reshape(-1, y.shape[-1])
@@ -113,12 +114,10 @@ def test_qlinear_fused_segments_norm_residual(cuda, rng, bits, rows):
     y = ops.qlinear_fused(to_dev(h, cuda), [tuple(to_dev(a, cuda) for a in sg) for sg in segs], group, bits,
                           norm_weight=to_dev(nw, cuda), eps=eps).cpu().numpy()
     xn64 = otp.rmsnorm(h, nw, eps)
-    xn = xn64.astype(np.float16).astype(np.float64)
-    ref = np.concatenate([xn @ qa.dequantize(*sg, group, bits).astype(np.float64).T for sg in segs], axis=1)
+    ref = np.concatenate([ref16(xn64, *sg, group, bits) for sg in segs], axis=1)
     ref_x = np.concatenate([ref_exact(xn64, *sg, group, bits) for sg in segs], axis=1)
-    # the batched kernel normalises in fp32 before rounding x to fp16; the
-    # float64 reference can land one fp16 ulp away on a few elements
-    assert_kernel_close(y, [ref, ref_x], 1e-4)
+    # x is normalised in fp32 and carried as fp16 high + low parts
+    assert_kernel_close(y, [ref, ref_x], 2e-5)
     # residual epilogue, in place
     for K2 in (256, 4096):
         wq, s, b = make_q(rng, K, K2, bits, group)
@@ -142,6 +141,31 @@ def test_qlinear_swiglu(cuda, rng, M, K, F):
                           group, bits, epilogue=L.SC_EPI_SWIGLU, out_dtype=torch.float32).cpu().numpy()
     refs = [otp.silu(f(x, *g, group, bits)) * f(x, *u, group, bits) for f in (ref16, ref_exact)]
     assert_kernel_close(y, refs, 5e-5)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M", [3, 8, 16, 21])
+def test_batched_kernel_fp32_input_keeps_x(cuda, rng, bits, M):
+    """fp32 activations through the batched kernel (weights rounded once to
+    fp16 as ``mx.dequantize`` does, x carried as fp16 high + low parts): the
+    product matches the float64 one of the fp16-rounded weights to ~1e-5,
+    where rounding x to fp16 alone sits near 3e-4."""
+    K, N, group = 4096, 512, 64
+    wq, s, b = make_q(rng, N, K, bits, group)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    for epi in ("store", "residual"):
+        if epi == "store":
+            y = ops.qlinear_fused(to_dev(x, cuda), [(to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda))], group,
+                                  bits, out_dtype=torch.float32).cpu().numpy()
+            ref = ref16(x, wq, s, b, group, bits)
+        else:
+            res = rng.standard_normal((M, N)).astype(np.float32)
+            r_dev = to_dev(res, cuda)
+            ops.qlinear_fused(to_dev(x, cuda), [(to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda))], group, bits,
+                              epilogue=L.SC_EPI_RESIDUAL, residual=r_dev, out=r_dev)
+            y, ref = r_dev.cpu().numpy(), res + ref16(x, wq, s, b, group, bits)
+        assert rel_l2(y, ref) <= 2e-5, epi
+    assert L.load().sc_qgemv_device_error(1) == 0
 
 
 @pytest.mark.parametrize("bits", [4, 8])
@@ -212,10 +236,10 @@ def test_quantize_bit_exact(cuda, rng, bits):
 def test_rope_append_and_flash_decode(cuda, rng, hd, Hq, Hkv, splits):
     B, Lmax, past, S = 2, 96, 37, 1
     cos, sin = otp.rope_tables(hd, 128, 10000.0)
-    k_cache = torch.zeros(B, Hkv, Lmax, hd, dtype=torch.float16, device=cuda)
+    k_cache = torch.zeros(B, Hkv, Lmax, hd, dtype=torch.float32, device=cuda)
     v_cache = torch.zeros_like(k_cache)
-    kp = (rng.standard_normal((B, Hkv, past, hd))).astype(np.float16)
-    vp = (rng.standard_normal((B, Hkv, past, hd))).astype(np.float16)
+    kp = (rng.standard_normal((B, Hkv, past, hd))).astype(np.float32)
+    vp = (rng.standard_normal((B, Hkv, past, hd))).astype(np.float32)
     k_cache[:, :, :past] = torch.from_numpy(kp).to(cuda)
     v_cache[:, :, :past] = torch.from_numpy(vp).to(cuda)
     qkv = rng.standard_normal((B * S, (Hq + 2 * Hkv) * hd)).astype(np.float32)
@@ -231,11 +255,11 @@ def test_rope_append_and_flash_decode(cuda, rng, hd, Hq, Hkv, splits):
     qr = otp.apply_rope(q, cos[past:past + S], sin[past:past + S])
     kr = otp.apply_rope(k, cos[past:past + S], sin[past:past + S])
     assert rel_l2(q_out.cpu().numpy().reshape(B, S, Hq, hd).transpose(0, 2, 1, 3), qr) <= 1e-6
-    # fp32 RoPE rounded to fp16 may differ from the float64 oracle by one fp16 ulp
+    # the cache holds the fp32 rotation (fp32 arithmetic against the float64 oracle)
     np.testing.assert_allclose(k_cache[:, :, past:past + S].cpu().numpy().astype(np.float64), kr,
-                               rtol=1e-3, atol=1e-3)
-    kall = np.concatenate([kp.astype(np.float64), kr.astype(np.float16).astype(np.float64)], axis=2)
-    vall = np.concatenate([vp.astype(np.float64), v.astype(np.float16).astype(np.float64)], axis=2)
+                               rtol=1e-5, atol=1e-5)
+    kall = np.concatenate([kp.astype(np.float64), kr], axis=2)
+    vall = np.concatenate([vp.astype(np.float64), v.astype(np.float64)], axis=2)
     rep = Hq // Hkv
     sc = (qr @ np.repeat(kall, rep, axis=1).transpose(0, 1, 3, 2)) / math.sqrt(hd)
     o = otp.softmax(sc) @ np.repeat(vall, rep, axis=1)
@@ -247,10 +271,10 @@ def test_flash_decode_causal_prefill(cuda, rng):
     B, S, Hq, Hkv, hd, Lmax = 1, 5, 4, 2, 64, 32
     past = 3
     cos, sin = otp.rope_tables(hd, 64, 10000.0)
-    k_cache = torch.zeros(B, Hkv, Lmax, hd, dtype=torch.float16, device=cuda)
+    k_cache = torch.zeros(B, Hkv, Lmax, hd, dtype=torch.float32, device=cuda)
     v_cache = torch.zeros_like(k_cache)
-    kp = rng.standard_normal((B, Hkv, past, hd)).astype(np.float16)
-    vp = rng.standard_normal((B, Hkv, past, hd)).astype(np.float16)
+    kp = rng.standard_normal((B, Hkv, past, hd)).astype(np.float32)
+    vp = rng.standard_normal((B, Hkv, past, hd)).astype(np.float32)
     k_cache[:, :, :past] = torch.from_numpy(kp).to(cuda)
     v_cache[:, :, :past] = torch.from_numpy(vp).to(cuda)
     qkv = rng.standard_normal((B * S, (Hq + 2 * Hkv) * hd)).astype(np.float32)
@@ -264,9 +288,9 @@ def test_flash_decode_causal_prefill(cuda, rng):
     k = qkv[:, Hq * hd:(Hq + Hkv) * hd].reshape(B, S, Hkv, hd).transpose(0, 2, 1, 3)
     v = qkv[:, (Hq + Hkv) * hd:].reshape(B, S, Hkv, hd).transpose(0, 2, 1, 3)
     qr = otp.apply_rope(q, cos[past:past + S], sin[past:past + S])
-    kr = otp.apply_rope(k, cos[past:past + S], sin[past:past + S]).astype(np.float16).astype(np.float64)
-    kall = np.concatenate([kp, kr], axis=2)
-    vall = np.concatenate([vp, v.astype(np.float16)], axis=2).astype(np.float64)
+    kr = otp.apply_rope(k, cos[past:past + S], sin[past:past + S])
+    kall = np.concatenate([kp.astype(np.float64), kr], axis=2)
+    vall = np.concatenate([vp, v], axis=2).astype(np.float64)
     Lt = past + S
     sc = (qr @ np.repeat(kall, 2, axis=1).transpose(0, 1, 3, 2)) / math.sqrt(hd)
     sc = sc + np.triu(np.full((S, Lt), -np.inf), k=Lt - S + 1)
@@ -330,8 +354,8 @@ def test_attn_decode_matches_rope_append_plus_flash(cuda, rng, hd, Hq, Hkv, spli
     B, Lmax = 2, 2112
     cos, sin = otp.rope_tables(hd, 4096, 5e5)
     cos_t, sin_t = torch.from_numpy(cos).to(cuda), torch.from_numpy(sin).to(cuda)
-    kc = torch.from_numpy((rng.standard_normal((B, Hkv, Lmax, hd))).astype(np.float16)).to(cuda)
-    vc = torch.from_numpy((rng.standard_normal((B, Hkv, Lmax, hd))).astype(np.float16)).to(cuda)
+    kc = torch.from_numpy((rng.standard_normal((B, Hkv, Lmax, hd))).astype(np.float32)).to(cuda)
+    vc = torch.from_numpy((rng.standard_normal((B, Hkv, Lmax, hd))).astype(np.float32)).to(cuda)
     kc2, vc2 = kc.clone(), vc.clone()
     qkv = torch.from_numpy(rng.standard_normal((B, (Hq + 2 * Hkv) * hd)).astype(np.float32)).to(cuda)
     pos = torch.tensor([past], dtype=torch.int32, device=cuda)
