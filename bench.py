@@ -383,27 +383,39 @@ def main():
            "d2h_bytes_per_step": host_out.numel() * 4,
            "path": "DecodeEngine.decode_host: pinned ids -> device, graph step, sampled ids -> pinned host, sync"}
 
-    # ---- roofline of the dominant kernel (dequant-GEMV): event pairs around every GEMV of a step
-    eng.capture_probe()
-    eng.replay_probe()
-    g_ms, g_bytes, g_n = 0.0, 0, 0
-    for _ in range(args.steps):
-        a, b, n = eng.replay_probe()
-        g_ms += a
-        g_bytes += b
-        g_n += n
     peak, peak_kind = load_peaks()
-    achieved = g_bytes / (g_ms / 1e3) / 1e9
-    gemv_share = g_ms / args.steps / ms_step
-    roofline = {"bound": "hbm", "kernel": "qgemv_tma (fused RMSNorm/dequant-GEMV/epilogue)", "achieved": achieved,
-                "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": NCU_GEMV_TRAFFIC.get((args.model, world, args.batch, args.bits, args.group, args.ctx)),
-                "traffic_unit": "bytes per step (ncu capture, profiles/)", "launches_per_step": g_n // args.steps,
-                "algorithmic_bytes_per_step": g_bytes // args.steps, "ms_per_step": g_ms / args.steps,
-                "share_of_step": gemv_share}
-    step_bytes = g_bytes / args.steps + eng.kv_bytes_per_step()
-    roofline["step_bytes"] = step_bytes
-    roofline["step_frac"] = step_bytes / (ms_step / 1e3) / 1e9 / peak
+    if eng.use_step:
+        # one kernel per step: its algorithmic bytes (weights, scales and biases
+        # of every linear and of the tied head, the KV cache it reads) over the
+        # measured step time, which bounds the kernel's own duration from above
+        step_bytes = eng.weight_bytes_per_step() + eng.kv_bytes_per_step()
+        achieved = step_bytes / (ms_step / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "decode_step_kernel (the whole decode step in one launch)",
+                    "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": None, "traffic_unit": "bytes per step",
+                    "launches_per_step": launches_per_step, "algorithmic_bytes_per_step": step_bytes,
+                    "ms_per_step": ms_step, "share_of_step": 1.0, "step_bytes": step_bytes,
+                    "step_frac": achieved / peak}
+    else:
+        # per-kernel step: event pairs around every dequant-GEMV of a step
+        eng.capture_probe()
+        eng.replay_probe()
+        g_ms, g_bytes, g_n = 0.0, 0, 0
+        for _ in range(args.steps):
+            a, b, n = eng.replay_probe()
+            g_ms += a
+            g_bytes += b
+            g_n += n
+        achieved = g_bytes / (g_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "qgemv_fx (fused RMSNorm/dequant-GEMV/epilogue)", "achieved": achieved,
+                    "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": NCU_GEMV_TRAFFIC.get((args.model, world, args.batch, args.bits, args.group, args.ctx)),
+                    "traffic_unit": "bytes per step", "launches_per_step": g_n // args.steps,
+                    "algorithmic_bytes_per_step": g_bytes // args.steps, "ms_per_step": g_ms / args.steps,
+                    "share_of_step": g_ms / args.steps / ms_step}
+        step_bytes = g_bytes / args.steps + eng.kv_bytes_per_step()
+        roofline["step_bytes"] = step_bytes
+        roofline["step_frac"] = step_bytes / (ms_step / 1e3) / 1e9 / peak
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

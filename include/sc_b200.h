@@ -298,6 +298,61 @@ int sc_p2p_allreduce(const void* send, void* recv, size_t count, int dtype, void
 int sc_p2p_allgather(const void* send, void* recv, size_t count_per_rank, int dtype, void* p2p,
                      cudaStream_t stream);
 
+/* ----------------------------------------------------- persistent decode step --
+ * One launch per greedy decode token of the tensor-parallel quantized Llama at
+ * batch 1 (4-bit, group 64): the embedding gather, every layer's RMSNorm ->
+ * q|k|v -> RoPE + KV append + attention -> o_proj + residual -> RMSNorm ->
+ * gate|up + SiLU*mul -> down_proj + residual, the final RMSNorm, the tied LM
+ * head and the greedy argmax.  Replaces, as one kernel, the per-token call
+ * chain of ParallelTransformer.forward (parallel/transformer.py:516-577)
+ * driven by ParallelExecutor.generate's greedy loop
+ * (worker/executor.py:267-325); its collectives (the row-parallel all-reduces,
+ * parallel/quantized_linear.py:446-447, parallel/mlp.py:252; the embedding
+ * all-reduce, parallel/embedding.py:358; the logits all-gather before the
+ * argmax, parallel/transformer.py:570-573) run inside the kernel over NVLink
+ * peer memory.
+ *
+ * Setup (not on the hot path): sc_step_create; sc_step_set_layer for every
+ * layer (wq / scales / biases: the 7 linears q, k, v, o, gate, up, down in the
+ * MLX layout, 16-byte aligned; caches fp32 [Hkv, max_seq, head_dim]);
+ * sc_step_set_head (the vocab-split embedding, whose weights are the tied LM
+ * head, and the final norm); sc_step_set_io (tok: int32 [1], the token to
+ * embed, overwritten with the sampled one; pos: int32 [1], the cache length,
+ * advanced by one; cos/sin fp32 [max_pos, head_dim/2]; trace: fp32
+ * [layers+1, hidden] or NULL, receives the hidden state after the embedding
+ * and every layer; logits: fp32 [vocab_local] or NULL); with world > 1,
+ * sc_step_set_peers (every rank's exchange arena as mapped here, at least
+ * sc_step_arena_bytes each, zero on creation); then sc_step_finalize with a
+ * caller workspace of sc_step_workspace_bytes (256-byte aligned; the plan,
+ * tensor maps and counters live there and must stay untouched).
+ * sc_step_run enqueues one step (one kernel, one CTA per SM, every CTA
+ * resident; capturable in a CUDA graph).  A wait that runs out (2 s) raises
+ * the error word, read by sc_step_error (reset != 0 restarts the counters).
+ * No reference counterpart as one call (the reference runs the same math as
+ * per-layer MLX ops and TCP collectives). */
+int sc_step_create(int hidden, int heads, int kv_heads, int head_dim, int ffn, int vocab_local, int vocab_start,
+                   int layers, int bits, int group, float eps, int max_seq, int world, int rank, void** step);
+int sc_step_set_layer(void* step, int layer, const uint16_t* ln1, const uint16_t* ln2,
+                      const uint32_t* const* wq, const uint16_t* const* scales, const uint16_t* const* biases,
+                      float* k_cache, float* v_cache);
+int sc_step_set_head(void* step, const uint32_t* embed_wq, const uint16_t* embed_scales,
+                     const uint16_t* embed_biases, const uint16_t* final_norm);
+int sc_step_set_io(void* step, int32_t* tok, int32_t* pos, const float* cos_tab, const float* sin_tab,
+                   int max_pos, float* trace, float* logits);
+size_t sc_step_arena_bytes(int hidden, int world);
+int sc_step_set_peers(void* step, void* const* arenas, size_t arena_bytes);
+size_t sc_step_workspace_bytes(void* step);
+int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+int sc_step_run(void* step, cudaStream_t stream);
+int sc_step_error(void* step, int reset);
+int sc_step_destroy(void* step);
+
+/* Every rank's arena of a peer-memory transport as mapped in this process
+ * (bases[world]) and the arena size, for a kernel that lays out its own lines
+ * in a transport it owns (the persistent decode step).  No reference
+ * counterpart. */
+int sc_p2p_arenas(void* p2p, void** bases, size_t* arena_bytes);
+
 #ifdef __cplusplus
 }
 #endif

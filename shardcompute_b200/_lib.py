@@ -76,6 +76,18 @@ SIGNATURES = {
     "sc_p2p_destroy": (_i, [_vp]),
     "sc_p2p_allreduce": (_i, [_vp, _vp, _sz, _i, _vp, _vp]),
     "sc_p2p_allgather": (_i, [_vp, _vp, _sz, _i, _vp, _vp]),
+    "sc_p2p_arenas": (_i, [_vp, _pp, C.POINTER(_sz)]),
+    "sc_step_create": (_i, [_i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _i, _i, _i, _pp]),
+    "sc_step_set_layer": (_i, [_vp, _i, _vp, _vp, _pp, _pp, _pp, _vp, _vp]),
+    "sc_step_set_head": (_i, [_vp, _vp, _vp, _vp, _vp]),
+    "sc_step_set_io": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
+    "sc_step_arena_bytes": (_sz, [_i, _i]),
+    "sc_step_set_peers": (_i, [_vp, _pp, _sz]),
+    "sc_step_workspace_bytes": (_sz, [_vp]),
+    "sc_step_finalize": (_i, [_vp, _vp, _sz, _vp]),
+    "sc_step_run": (_i, [_vp, _vp]),
+    "sc_step_error": (_i, [_vp, _i]),
+    "sc_step_destroy": (_i, [_vp]),
 }
 
 _lib = None

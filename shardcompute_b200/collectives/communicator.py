@@ -96,6 +96,7 @@ class Communicator:
         self._comm_stream: Optional[torch.cuda.Stream] = None
         self._p2p = None  # sc_p2p handle: NVLink one-shot collectives for small messages
         self._p2p_max = 0
+        self._extra_arenas: List[tuple] = []  # (handle, store prefix) of arenas lent to kernels
 
     # ------------------------------------------------------------ setup
 
@@ -162,17 +163,25 @@ class Communicator:
         gen = next(_P2P_GENERATION)
         if self.world_size < 2 or self.world_size > 8 or os.environ.get("SC_P2P", "1") == "0":
             return
+        max_bytes = int(os.environ.get("SC_P2P_MAX_BYTES", 1 << 20))
+        handle = self._open_arena(f"shardcompute_b200/p2p/{gen}", max_bytes, timeout)
+        if handle is not None:
+            self._p2p, self._p2p_max = handle, max_bytes
+            self._p2p_gen = gen
+
+    def _open_arena(self, pre: str, max_bytes: int, timeout: float):
+        """Collective: create this rank's peer-memory arena, exchange IPC
+        handles through the store, map every peer's.  Returns the transport
+        handle when every rank succeeded, else None on every rank."""
         from .. import _lib as L
 
         lib = L.load()
         hb = int(lib.sc_p2p_handle_bytes())
-        max_bytes = int(os.environ.get("SC_P2P_MAX_BYTES", 1 << 20))
         handle = C.c_void_p()
         buf = (C.c_char * hb)()
         ok = lib.sc_p2p_create(self.world_size, self.rank, max_bytes, C.byref(handle), buf, hb) == L.SC_OK
         if not ok:
             logger.warning("p2p transport unavailable on rank %d: %s", self.rank, L.last_error())
-        pre = f"shardcompute_b200/p2p/{gen}"
         wait = datetime.timedelta(seconds=timeout)
         self._store.set(f"{pre}/h/{self.rank}", bytes(buf) if ok else b"-")
         keys = [f"{pre}/h/{q}" for q in range(self.world_size)]
@@ -191,10 +200,33 @@ class Communicator:
         keys = [f"{pre}/ok/{q}" for q in range(self.world_size)]
         self._store.wait(keys, wait)
         if all(self._store.get(k) == b"1" for k in keys):
-            self._p2p, self._p2p_max = handle, max_bytes
-            self._p2p_gen = gen
-        elif handle.value:
+            return handle
+        if handle.value:
             lib.sc_p2p_destroy(handle)
+        return None
+
+    def step_arena(self, nbytes: int, timeout: float = 60.0):
+        """Collective: a dedicated peer-memory arena of at least ``nbytes``
+        per rank for a kernel that lays out its own lines (the persistent
+        decode step), returned as (every rank's arena base as mapped here,
+        arena bytes).  Freed at shutdown.  Raises if any rank failed."""
+        from .. import _lib as L
+
+        self._require()
+        gen = next(_P2P_GENERATION)
+        pre = f"shardcompute_b200/step_arena/{gen}"
+        # an arena is a 4 KB header + 2 x world regions of 16-byte lines per 8 payload bytes
+        max_bytes = max(8, -(-max(0, nbytes - 4096) // (4 * self.world_size)) + 16)
+        handle = self._open_arena(pre, max_bytes, timeout)
+        if handle is None:
+            raise RuntimeError(f"rank {self.rank}: the decode step's peer-memory arena could not be set up")
+        bases = (C.c_void_p * self.world_size)()
+        size = C.c_size_t()
+        L.check(L.load().sc_p2p_arenas(handle, C.cast(bases, L._pp), C.byref(size)), "sc_p2p_arenas")
+        if size.value < nbytes:
+            raise RuntimeError(f"step arena of {size.value} bytes < {nbytes}")
+        self._extra_arenas.append((handle, pre))
+        return [bases[q] for q in range(self.world_size)], size.value
 
     @property
     def p2p_enabled(self) -> bool:
@@ -464,20 +496,25 @@ class Communicator:
             raise RuntimeError(f"rank {self.rank}: NCCL asynchronous error {code}")
 
     def _close_p2p(self, wait_for_peers: bool):
-        """Free the peer-memory transport; first (unless aborting) wait until
-        every rank got here, so no peer still sends into this rank's arena."""
-        if self._p2p is None:
-            return
+        """Free the peer-memory transports; first (unless aborting) wait until
+        every rank got here, so no peer still sends into this rank's arenas."""
         from .. import _lib as L
 
+        arenas = list(self._extra_arenas)
+        if self._p2p is not None:
+            arenas.append((self._p2p, f"shardcompute_b200/p2p/{self._p2p_gen}"))
+        if not arenas:
+            return
         if wait_for_peers:
-            pre = f"shardcompute_b200/p2p/{self._p2p_gen}"
+            pre = arenas[-1][1]
             self._store.set(f"{pre}/bye/{self.rank}", b"1")
             try:
                 self._store.wait([f"{pre}/bye/{q}" for q in range(self.world_size)], datetime.timedelta(seconds=60))
             except Exception:  # noqa: BLE001 - a dead peer sends nothing more
                 logger.warning("rank %d: peers missing at p2p shutdown", self.rank)
-        L.load().sc_p2p_destroy(self._p2p)
+        for handle, _ in arenas:
+            L.load().sc_p2p_destroy(handle)
+        self._extra_arenas = []
         self._p2p = None
 
     def abort(self):

@@ -321,6 +321,20 @@ int sc_p2p_create(int world, int rank, size_t max_bytes, void** p2p_out, void* h
   return SC_OK;
 }
 
+// Every rank's arena as mapped in this process (bases[world]) and the arena
+// size, for a kernel that lays out its own lines in a transport it owns.
+int sc_p2p_arenas(void* p2p, void** bases, size_t* arena_bytes) {
+  using namespace sc;
+  SC_REQUIRE(p2p && bases && arena_bytes, SC_ERR_ARG, "p2p_arenas: null pointer");
+  P2P* h = static_cast<P2P*>(p2p);
+  for (int q = 0; q < h->world; ++q) {
+    SC_REQUIRE(h->peer[q], SC_ERR_ARG, "p2p_arenas: rank %d's arena is not mapped (call sc_p2p_open first)", q);
+    bases[q] = h->peer[q];
+  }
+  *arena_bytes = P2P_HDR + 2 * (size_t)h->world * h->region_bytes;
+  return SC_OK;
+}
+
 int sc_p2p_open(void* p2p, const void* handles, size_t handle_bytes) {
   using namespace sc;
   SC_REQUIRE(p2p && handles, SC_ERR_ARG, "p2p_open: null pointer");

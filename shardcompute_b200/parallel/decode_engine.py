@@ -19,7 +19,14 @@ worker/executor.py:229-325), re-laid for B200:
   ``[L, 2, B, Hkv/TP, Lmax, hd]`` (as the reference's: RoPE's fp32 tables promote k), preallocated;
 * positions and token ids live in device buffers, so one decode step is
   captured once in a CUDA graph and replayed; each replay reads the token the
-  previous replay wrote and advances the position counter on the device.
+  previous replay wrote and advances the position counter on the device;
+* at batch 1 with 4-bit group-64 weights the whole decode step is ONE
+  persistent kernel (``sc_step_run``, ``csrc/sc_step.cu``): the weights of
+  every GEMV and the cached keys / values stream through one shared-memory
+  ring per SM without stopping at op boundaries, the row-parallel
+  all-reduces run inside it over NVLink, and the last CTA writes the sampled
+  token.  ``SC_STEP=0`` (or any other batch / format) keeps the per-kernel
+  step above.
 """
 
 from __future__ import annotations
@@ -101,6 +108,16 @@ class DecodeEngine:
         # decode scratch: fixed for the engine's lifetime (a captured graph keeps its address)
         self.workspace = torch.empty(self._workspace_bytes(self.B, 1), dtype=torch.uint8, device=dev)
         self._ws = self.workspace
+        # the persistent one-kernel decode step (built at the first decode step)
+        self.use_step = (self.B == 1 and self.bits == 4 and self.group == 64 and cfg.hidden_size % 512 == 0
+                         and (self.Hq * self.hd) % 512 == 0 and self.F % 256 == 0 and self.F >= 512
+                         and self.hd in (64, 128) and (self.Hq // self.Hkv) in (1, 2, 4, 8)
+                         and os.environ.get("SC_STEP", "1") != "0")
+        self._step = None
+        self._step_ws: Optional[torch.Tensor] = None
+        self.step_trace: Optional[torch.Tensor] = None   # [L+1, H] hidden states of the last step (debug)
+        self.step_logits: Optional[torch.Tensor] = None  # [V/TP] logits of the last step (debug)
+        self._step_debug = False
 
     # ------------------------------------------------------------ buffers
 
@@ -292,6 +309,15 @@ class DecodeEngine:
             raise ValueError(f"KV cache full: position {self.host_pos} + {n} exceeds max_seq {self.Lmax}")
         self.host_pos += n
 
+    def weight_bytes_per_step(self) -> int:
+        """Bytes of this rank's weights one decode step streams: every
+        linear's packed words, scales and biases, and the tied head's."""
+        n = sum(t.numel() * t.element_size() for t in self.w.embed)
+        for lw in self.w.layers:
+            for tri in (lw.q, lw.k, lw.v, lw.o, lw.gate, lw.up, lw.down):
+                n += sum(t.numel() * t.element_size() for t in tri)
+        return n
+
     def kv_bytes_per_step(self) -> int:
         """KV-cache bytes one decode step reads at the current length (all layers)."""
         return self.cfg.num_layers * 2 * self.B * self.Hkv * self.host_pos * self.hd * self.kv.element_size()
@@ -311,9 +337,80 @@ class DecodeEngine:
         bf["hlast"][:B].copy_(hl)
         self._sample(bf, bf["hlast"][:B], B, S)
 
+    # ------------------------------------------------------------ the one-kernel step
+
+    def enable_step_debug(self):
+        """Have the one-kernel step also write the hidden state after the
+        embedding and every layer (``step_trace``) and its logits
+        (``step_logits``); call before the first decode step."""
+        if self._step is not None:
+            raise RuntimeError("enable_step_debug must come before the first decode step")
+        self._step_debug = True
+
+    def _build_step(self):
+        lib = L.load()
+        cfg, dev = self.cfg, self.device
+        h = C.c_void_p()
+        L.check(lib.sc_step_create(self.H, self.Hq, self.Hkv, self.hd, self.F, self.Vl, self.w.vocab_start,
+                                   cfg.num_layers, self.bits, self.group, float(self.eps), self.Lmax, self.world,
+                                   self.rank, C.byref(h)), "sc_step_create")
+        try:
+            for i, lw in enumerate(self.w.layers):
+                tris = [lw.q, lw.k, lw.v, lw.o, lw.gate, lw.up, lw.down]
+                arr = [(C.c_void_p * 7)(*[t[j].data_ptr() for t in tris]) for j in range(3)]
+                L.check(lib.sc_step_set_layer(h, i, lw.ln1.data_ptr(), lw.ln2.data_ptr(), C.cast(arr[0], L._pp),
+                                              C.cast(arr[1], L._pp), C.cast(arr[2], L._pp),
+                                              self.kv[i, 0].data_ptr(), self.kv[i, 1].data_ptr()), "sc_step_set_layer")
+            L.check(lib.sc_step_set_head(h, *[t.data_ptr() for t in self.w.embed], self.w.norm.data_ptr()),
+                    "sc_step_set_head")
+            if self._step_debug:
+                self.step_trace = torch.zeros(cfg.num_layers + 1, self.H, dtype=torch.float32, device=dev)
+                self.step_logits = torch.zeros(self.Vl, dtype=torch.float32, device=dev)
+            L.check(lib.sc_step_set_io(h, self.tok.data_ptr(), self.pos.data_ptr(), self.cos.data_ptr(),
+                                       self.sin.data_ptr(), self.cos.shape[0],
+                                       None if self.step_trace is None else self.step_trace.data_ptr(),
+                                       None if self.step_logits is None else self.step_logits.data_ptr()),
+                    "sc_step_set_io")
+            if self.world > 1:
+                bases, size = self.comm.step_arena(int(lib.sc_step_arena_bytes(self.H, self.world)))
+                arr = (C.c_void_p * self.world)(*bases)
+                L.check(lib.sc_step_set_peers(h, C.cast(arr, L._pp), size), "sc_step_set_peers")
+            nbytes = int(lib.sc_step_workspace_bytes(h))
+            self._step_ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            L.check(lib.sc_step_finalize(h, self._step_ws.data_ptr(), nbytes, ops.stream_handle(dev)),
+                    "sc_step_finalize")
+        except BaseException:
+            lib.sc_step_destroy(h)
+            raise
+        self._step = h
+
+    def step_error(self, reset: bool = False) -> int:
+        """The one-kernel step's device error word (0: fine); synchronises."""
+        if self._step is None:
+            return 0
+        return int(L.load().sc_step_error(self._step, 1 if reset else 0))
+
+    def check_step(self):
+        code = self.step_error()
+        if code:
+            raise TimeoutError(f"rank {self.rank}: the decode step kernel gave up on a wait (error {code})")
+
+    def __del__(self):
+        try:
+            if self._step is not None:
+                L.load().sc_step_destroy(self._step)
+                self._step = None
+        except Exception:  # noqa: BLE001 - interpreter teardown
+            pass
+
     def decode_step(self):
         """One greedy step for the engine's full batch (eager)."""
         self._advance(1)
+        if self.use_step:
+            if self._step is None:
+                self._build_step()
+            L.call("sc_step_run", self._step, ops.stream_handle(self.device))
+            return
         B = self.B
         bf = self._buffers(B, 1)
         self._ws = self.workspace
@@ -407,6 +504,7 @@ class DecodeEngine:
                 self.decode_step()
         if self.world > 1:
             self.comm.check_health()  # a timed-out peer-memory collective leaves undefined tokens
+        self.check_step()
         return torch.stack(out, dim=1)
 
     def forward_logits(self, input_ids: torch.Tensor, return_hidden: bool = False):
