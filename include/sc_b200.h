@@ -76,7 +76,10 @@ unsigned long long sc_launch_count(void);
  * and the tied LM head matmul of parallel/transformer.py:565-569.
  *   x: fp16 or fp32 [M, ldx]; bias: fp16 [N] or NULL; y: fp16 or fp32 [M, ldy].
  *   bits in {4, 8}; group_size in {32, 64, 128}; K % group_size == 0.
- *   Any M >= 1; M <= 16 runs as one weight pass per 16 rows of x.
+ *   Any M >= 1.  Up to 4 rows (2 at 4-bit group 64) run the decode GEMV
+ *   (exact weights); more rows run the tcgen05 tensor-core GEMM (sc_qgemm)
+ *   when K % 64 == 0 and the workspace holds its scratch, else batched
+ *   GEMV passes.  sc_qlinear_workspace_bytes covers every case.
  */
 size_t sc_qlinear_workspace_bytes(int M, int K, int N, int bits);
 int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx,
@@ -84,6 +87,24 @@ int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx,
                int N, int group_size, int bits, const uint16_t* bias,
                void* y, int y_dtype, int ldy,
                void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* K2: the tensor-core dequant-GEMM behind sc_qlinear for more rows of x
+ * (prefill, batched decode): tcgen05.mma kind::f16 with fp32 accumulators in
+ * TMEM; weights carried exactly as fp16 high + low parts, x likewise.  Same
+ * arguments and epilogues as sc_qlinear_fused.  Replaces the prefill-shaped
+ * mx.quantized_matmul calls (parallel/quantized_linear.py:168-176, 206-214,
+ * parallel/transformer.py:639).  K % 64 == 0; stacked weight segments a
+ * multiple of 128 rows (the last excepted).  Scratch: x's two fp16 parts and,
+ * for SwiGLU, the [M, 2N] gate|up product. */
+size_t sc_qgemm_workspace_bytes(int M, int K, int N, int epilogue);
+int sc_qgemm(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_weight, float norm_eps,
+             int nseg, const uint32_t* const* wq, const uint16_t* const* scales, const uint16_t* const* biases,
+             const int* seg_rows, int group_size, int bits, const uint16_t* bias, int epilogue, void* y,
+             int y_dtype, int ldy, const float* residual, int ldr, void* workspace, size_t workspace_bytes,
+             cudaStream_t stream);
+/* Device error word of the tensor-core GEMM: nonzero after a bounded wait
+ * gave up (the output is then undefined).  reset != 0 clears it. */
+int sc_qgemm_device_error(int reset);
 
 /* sc_qlinear without a caller workspace: its split-K scratch is a fixed
  * 4 MiB array the library allocates statically on each device.  No
@@ -345,6 +366,9 @@ size_t sc_step_workspace_bytes(void* step);
 int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 int sc_step_run(void* step, cudaStream_t stream);
 int sc_step_error(void* step, int reset);
+/* After finalize: {SMs, CTAs per SM, static shared bytes, dynamic shared
+ * bytes, registers per thread, max threads per block} of the step kernel. */
+int sc_step_fit(void* step, int* out6);
 int sc_step_destroy(void* step);
 
 /* Every rank's arena of a peer-memory transport as mapped in this process

@@ -87,6 +87,11 @@ SIGNATURES = {
     "sc_step_finalize": (_i, [_vp, _vp, _sz, _vp]),
     "sc_step_run": (_i, [_vp, _vp]),
     "sc_step_error": (_i, [_vp, _i]),
+    "sc_step_fit": (_i, [_vp, C.POINTER(_i)]),
+    "sc_qgemm_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "sc_qgemm": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp, _i, _vp, _i, _i,
+                      _vp, _i, _vp, _sz, _vp]),
+    "sc_qgemm_device_error": (_i, [_i]),
     "sc_step_destroy": (_i, [_vp]),
 }
 

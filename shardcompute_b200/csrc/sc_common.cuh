@@ -40,6 +40,13 @@ bool pdl_enabled();
 // Split-K scratch of sc_qlinear for this exact shape and group (one weight
 // set, store epilogue); tma_ok: the weight pointers are 16-byte aligned.
 size_t qlinear_workspace_need(int M, int K, int N, int group, int bits, bool tma_ok);
+// The tensor-core dequant-GEMM (sc_qgemm.cu): eligibility, scratch, launch.
+bool qgemm_eligible(int M, int K, int nseg, const int* seg_rows, int epi, int bits, int group);
+size_t qgemm_workspace_bytes(int M, int K, int N, int epi);
+int run_qgemm(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_w, float eps, int nseg,
+              const uint32_t* const* wq, const uint16_t* const* scales, const uint16_t* const* biases,
+              const int* seg_rows, int group, int bits, const uint16_t* bias, int epi, void* y, int y_dtype,
+              int ldy, const float* residual, int ldr, void* ws, size_t ws_bytes, cudaStream_t stream);
 // Records a failed launch for the next check_launch() on this thread.
 void note_launch_status(cudaError_t e);
 

@@ -1556,11 +1556,13 @@ static int tma_unit(int bits, int group) { return std::max(2, 8 * group / kpc_of
 // Tuning knobs read once from the environment (0 / unset = built-in choice):
 // SC_QGEMV_CPS chunks per stage, SC_QGEMV_NST ring depth, SC_QGEMV_PATH=ldg
 // forces the direct-load kernel, SC_QGEMV_FX=0 the batched kernel for decode,
+// SC_QGEMM=0 keeps passes of more rows off the tensor-core GEMM,
 // SC_QGEMV_WMODE=0/1 the packed-word tensor-map layout (block-major /
 // row-swizzled; default: row-swizzled when the driver accepts it).
 struct Knobs {
-  int cps = 0, nst = 0, ldg = 0, nofx = 0, wmode = -1, pre = -1, pf_after = 1;
+  int cps = 0, nst = 0, ldg = 0, nofx = 0, wmode = -1, pre = -1, pf_after = 1, nok2 = 0;
   Knobs() {
+    if (const char* e = getenv("SC_QGEMM")) nok2 = e[0] == '0';
     if (const char* e = getenv("SC_PF_AFTER")) pf_after = atoi(e);
     if (const char* e = getenv("SC_QGEMV_PRE")) pre = atoi(e);
     if (const char* e = getenv("SC_QGEMV_WMODE")) wmode = atoi(e);
@@ -1962,6 +1964,13 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
   const bool atomic_ok = epi == SC_EPI_RESIDUAL && y_dtype == SC_F32 && (const void*)residual == (const void*)y &&
                          ldr == ldy;
 
+  // More rows than the decode GEMV serves: the tensor-core GEMM (exact
+  // weights, x to ~22 bits) when the shape and the workspace allow it.
+  if (!fx_eligible(M, bits, group) && !knobs().nok2 && tma_ok &&
+      qgemm_eligible(M, K, nseg, seg_rows, epi, bits, group) && ws &&
+      ws_bytes >= qgemm_workspace_bytes(M, K, N, epi))
+    return run_qgemm(x, x_dtype, M, K, ldx, norm_w, eps, nseg, wq, scales, biases, seg_rows, group, bits, bias, epi,
+                     y, y_dtype, ldy, residual, ldr, ws, ws_bytes, stream);
   for (int m0 = 0; m0 < M;) {
     const RowPass rp = plan_rows(M - m0, K, N, bits, group, nacc, tma_ok, atomic_ok);
     const int mb = rp.mb;
@@ -2052,6 +2061,8 @@ size_t sc_qlinear_workspace_bytes(int M, int K, int N, int bits) {
   if (M < 1 || K < 1 || N < 1 || (bits != 4 && bits != 8)) return 0;
   const int mb = M < 16 ? M : 16;
   size_t best = 0;
+  // the tensor-core GEMM (more rows than the decode GEMV serves), SwiGLU worst case
+  if (M > 1) best = sc::qgemm_workspace_bytes(M, K, N, SC_EPI_SWIGLU);
   // the widest plan over every pass size, kernel choice and group size
   for (int mm = 1; mm <= mb; ++mm)
     for (int group : {32, 64, 128})

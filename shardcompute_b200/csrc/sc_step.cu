@@ -1247,6 +1247,8 @@ struct StepPlan {
   StepParams P{};
   size_t smem = 0;
   int G = 1;
+  int grid = 0;      // CTAs per step: every SM, as far as one CTA fits on each
+  int fit[6] = {};   // SMs, CTAs per SM, static smem, dynamic smem, registers, max threads per block
 };
 
 static PFN_cuTensorMapEncodeTiled_v12000 step_encode_fn() {
@@ -1390,7 +1392,7 @@ static cudaError_t launch_step(const StepPlan* p, cudaStream_t stream) {
   }
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p->nsm);
+  cfg.gridDim = dim3(p->grid);
   cfg.blockDim = dim3(SP_THREADS);
   cfg.dynamicSmemBytes = p->smem;
   cfg.stream = stream;
@@ -1413,6 +1415,22 @@ static size_t step_static_smem() {
   cudaFuncAttributes fa{};
   cudaFuncGetAttributes(&fa, decode_step_kernel<G>);
   return fa.sharedSizeBytes;
+}
+
+template <int G>
+static void step_fit(size_t dyn, int* blocks, cudaFuncAttributes* fa) {
+  cudaFuncSetAttribute(decode_step_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, decode_step_kernel<G>, SP_THREADS, dyn);
+  cudaFuncGetAttributes(fa, decode_step_kernel<G>);
+}
+
+static void fit_of(int G, size_t dyn, int* blocks, cudaFuncAttributes* fa) {
+  switch (G) {
+    case 1: step_fit<1>(dyn, blocks, fa); break;
+    case 2: step_fit<2>(dyn, blocks, fa); break;
+    case 4: step_fit<4>(dyn, blocks, fa); break;
+    default: step_fit<8>(dyn, blocks, fa); break;
+  }
 }
 
 static size_t static_smem_of(int G) {
@@ -1743,6 +1761,22 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
   const size_t budget = (size_t)optin - static_smem - 1024;
   const int nst = (int)std::min<size_t>(SP_MAX_NST, (budget - xs_alloc) / SP_STAGE_BYTES);
   p->smem = xs_alloc + (size_t)nst * SP_STAGE_BYTES + 1024;
+  {
+    int nb = 0;
+    cudaFuncAttributes fa{};
+    fit_of(G, p->smem, &nb, &fa);
+    p->fit[0] = p->nsm;
+    p->fit[1] = nb;
+    p->fit[2] = (int)fa.sharedSizeBytes;
+    p->fit[3] = (int)p->smem;
+    p->fit[4] = fa.numRegs;
+    p->fit[5] = fa.maxThreadsPerBlock;
+    SC_REQUIRE(nb >= 1 && fa.maxThreadsPerBlock >= SP_THREADS, SC_ERR_UNSUPPORTED,
+               "step_finalize: the step kernel does not fit an SM (%d CTAs per SM, %d registers x %d threads, "
+               "%zu + %zu bytes of shared memory, at most %d threads per block)",
+               nb, fa.numRegs, SP_THREADS, (size_t)fa.sharedSizeBytes, p->smem, fa.maxThreadsPerBlock);
+    p->grid = p->nsm;
+  }
   // ---- upload
   e = cudaMemcpyAsync(ws + L.ops, ops.data(), sizeof(StepOp) * ops.size(), cudaMemcpyHostToDevice, stream);
   if (e == cudaSuccess)
@@ -1804,6 +1838,13 @@ int sc_step_run(void* step, cudaStream_t stream) {
     case 4: e = launch_step<4>(p, stream); break;
     default: e = launch_step<8>(p, stream); break;
   }
+  if (e == cudaErrorCooperativeLaunchTooLarge) {
+    cudaGetLastError();
+    set_error("step_run: cooperative launch of %d CTAs refused (%d SMs, %d CTAs per SM, %d registers, %d + %d bytes "
+              "of shared memory)",
+              p->grid, p->fit[0], p->fit[1], p->fit[4], p->fit[2], p->fit[3]);
+    return SC_ERR_CUDA;
+  }
   note_launch_status(e);
   return check_launch("decode_step");
 }
@@ -1821,6 +1862,14 @@ int sc_step_error(void* step, int reset) {
     cudaMemset(p->P.ctr, 0, sizeof(int) * L.nctr);
   }
   return v;
+}
+
+int sc_step_fit(void* step, int* out6) {
+  using namespace sc;
+  SC_REQUIRE(step && out6, SC_ERR_ARG, "step_fit: null pointer");
+  const StepPlan* p = static_cast<const StepPlan*>(step);
+  for (int i = 0; i < 6; ++i) out6[i] = p->fit[i];
+  return SC_OK;
 }
 
 int sc_step_destroy(void* step) {
