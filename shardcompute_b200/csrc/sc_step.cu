@@ -49,7 +49,7 @@
 namespace sc {
 
 // ---------------------------------------------------------------- geometry
-constexpr int SP_NCW = 16;                     // consumer warps
+constexpr int SP_NCW = 12;                     // consumer warps (13 warps x 128 registers fill the register file)
 constexpr int SP_NC = SP_NCW * 32;             // consumer threads
 constexpr int SP_THREADS = SP_NC + 32;         // + the producer warp
 constexpr int SP_KPC = 128;                    // k values per chunk (16 words of 4-bit codes)
@@ -57,8 +57,8 @@ constexpr int SP_BOX_CH = 4;                   // chunks per TMA box (two 32-wor
 constexpr int SP_BOX_K = SP_BOX_CH * SP_KPC;   // 512 k values per box
 constexpr int SP_WBOX = 16 * SP_BOX_CH * 64;   // packed-word bytes of a box: 16 rows x 4 chunks (4 KB)
 constexpr int SP_SBOX = 16 * 8 * 2;            // scale (or bias) bytes of a box: 16 rows x 8 groups
-constexpr int SP_STAGE_BOXES = 8;              // 32 chunks of one set, or 16 chunk pairs of gate|up
-constexpr int SP_STAGE_BYTES = SP_STAGE_BOXES * (SP_WBOX + 2 * SP_SBOX);  // 36 KB
+constexpr int SP_STAGE_BOXES = 6;              // 24 chunks of one set, or 12 chunk pairs of gate|up
+constexpr int SP_STAGE_BYTES = SP_STAGE_BOXES * (SP_WBOX + 2 * SP_SBOX);  // 27 KB
 constexpr int SP_STAGE_S = SP_STAGE_BOXES * SP_WBOX;                      // scales start
 constexpr int SP_STAGE_B = SP_STAGE_S + SP_STAGE_BOXES * SP_SBOX;         // biases start
 constexpr int SP_MAX_NST = 8;
@@ -484,7 +484,7 @@ struct StepShared {
 // ---------------------------------------------------------------- the kernel
 
 template <int G>
-__global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
+__global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepParams P) {
   extern __shared__ __align__(1024) unsigned char sp_smem[];
   __shared__ StepShared S;
   __shared__ __align__(16) uint4 s_zero[16];
@@ -519,7 +519,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
   const int L = pos_ok ? pos + 1 : 0;         // keys this step attends to
   const long long TA = (long long)P.Hkv * L;  // attention units (head, key)
   const int na = (int)std::min<long long>(n, std::max<long long>(1, (TA + 63) / 64));  // attention CTAs
-  const int AK = SP_STAGE_BYTES / (2 * HD * 4) / 16 * 16;                             // keys per stage
+  const int AK = SP_STAGE_BYTES / (2 * HD * 4);                                       // keys per stage
   if (!pos_ok && tid == 0) raise_err(P, 1);
 
   if (warp == SP_NCW) {
@@ -623,6 +623,8 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
   if (!pos_ok) *abort = 1;
 
   auto cbar = [&]() { named_bar_sync(1, SP_NC); };
+  // the CTA's abort flag as one decision for the whole warp (before shuffles / votes)
+  auto wabort = [&]() -> bool { return __any_sync(0xffffffffu, *abort != 0); };
 
   for (int oi = 0; oi < P.nops; ++oi) {
     const StepOp& op = P.ops[oi];
@@ -630,7 +632,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
     if (op.kind == SOP_EMBED) {
       const int ng = P.H / 64;
       for (int gg = c + n * warp; gg < ng; gg += n * SP_NCW) {
-        if (*abort) break;
+        if (wabort()) break;
         const int tok = *reinterpret_cast<volatile int*>(P.tok);
         const int lt = tok - P.vocab_start;
         const bool own = lt >= 0 && lt < P.vocab_local;
@@ -718,7 +720,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
           const int s = (int)(it % (uint32_t)P.nst);
           const uint32_t ph = (it / (uint32_t)P.nst) & 1u;
           ++it;
-          if (*abort || !mbar_wait_all(P, &S.full[s], ph, abort)) {
+          if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort)) {
             *abort = 1;
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s]);
@@ -835,7 +837,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
         __threadfence();
         cbar();
         // the last segment of head h merges the head and stages o_proj's input
-        if (warp == 0 && !*abort) {
+        if (warp == 0 && !wabort()) {
           int last = 0;
           if (lane == 0) last = atomicAdd(hctr + h, 1) + 1 == nsh;
           last = __shfl_sync(0xffffffffu, last, 0);
@@ -888,7 +890,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
         S.ndefer = 0;
       }
       cbar();
-      if (!*abort) {
+      if (!wabort()) {
         for (int i = tid; i < op.xs_bytes / 16; i += SP_NC)
           reinterpret_cast<uint4*>(xs)[i] = ldcg_v4(op.xs + (size_t)i * 16);
         if (warp == 0) {
@@ -912,9 +914,9 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
         const int tt = t_first + j;
         const long long a = (std::max(lo, (long long)tt * op.kq) - lo) * SP_BOX_CH;
         const long long b = (std::min(hi, (long long)(tt + 1) * op.kq) - lo) * SP_BOX_CH;
-        if (b - a >= 16) return 0xffffu;
+        if (b - a >= SP_NCW) return (1u << SP_NCW) - 1u;
         uint32_t msk = 0;
-        for (long long p = a; p < b; ++p) msk |= 1u << (p % 16);
+        for (long long p = a; p < b; ++p) msk |= 1u << (p % SP_NCW);
         return msk;
       };
 
@@ -1006,16 +1008,19 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
       int cur = -1;  // this warp's current segment (tile - t_first)
       auto flush = [&](int j, int nset) {
         const int slot = j % SP_WIN;
-        // the slot must have been released by segment j - SP_WIN's epilogue
-        if (*reinterpret_cast<volatile int*>(&S.free_at[slot]) != j) {
+        // the slot must have been released by segment j - SP_WIN's epilogue (lane 0 waits)
+        int freed = 1;
+        if (lane == 0 && *reinterpret_cast<volatile int*>(&S.free_at[slot]) != j) {
           const uint64_t t0 = globaltimer_ns();
           for (uint32_t i = 1; *reinterpret_cast<volatile int*>(&S.free_at[slot]) != j; ++i)
             if ((i & 63) == 0 && (*abort || err_set(P) || globaltimer_ns() - t0 > SP_WAIT_NS)) {
               if (!*abort && !err_set(P)) raise_err(P, SPE_SLOT);
               *abort = 1;
-              return;
+              freed = 0;
+              break;
             }
         }
+        if (!__shfl_sync(0xffffffffu, freed, 0)) return;
 #pragma unroll
         for (int a = 0; a < 2; ++a) {
           if (a >= nset) break;
@@ -1047,9 +1052,9 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
       };
       auto sofs = [&](int b, int cc) -> uint32_t { return (uint32_t)(b * SP_SBOX + pr0 * 16 + cc * 4); };
 
-      // The stream: NS weight sets; a warp takes chunk slots w (+ 16 for one
-      // set) of every stage, loads everything it needs into registers,
-      // releases the slot, then computes.
+      // The stream: NS weight sets; a warp takes chunk slots w (+ SP_NCW for
+      // one set) of every stage, loads the ring's part of them into
+      // registers, releases the slot, then computes.
       auto run = [&](auto nset_tag) {
         constexpr int NS = decltype(nset_tag)::value;
         constexpr int NK = NS == 1 ? 2 : 1;              // chunk slots per warp per stage
@@ -1062,7 +1067,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
           const int s = (int)(it % (uint32_t)P.nst);
           const uint32_t ph = (it / (uint32_t)P.nst) & 1u;
           ++it;
-          if (*abort || !mbar_wait_all(P, &S.full[s], ph, abort)) {
+          if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort)) {
             *abort = 1;
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s]);
@@ -1074,7 +1079,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
           uint32_t SB[NK][NS][4];        // scales g, g + 8, biases g, g + 8 (two groups each)
 #pragma unroll
           for (int k = 0; k < NK; ++k) {
-            const int slotc = warp + 16 * k;
+            const int slotc = warp + SP_NCW * k;
             if (sidx * CPS + slotc < nchi) {
               const int bq = slotc / SP_BOX_CH, cc = slotc % SP_BOX_CH;
 #pragma unroll
@@ -1095,7 +1100,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
           if (lane == 0) mbar_arrive(&S.empty[s]);
 #pragma unroll
           for (int k = 0; k < NK; ++k) {
-            const int slotc = warp + 16 * k;
+            const int slotc = warp + SP_NCW * k;
             const int pc = sidx * CPS + slotc;  // chunk position within this CTA's range
             if (pc >= nchi) break;
             const int ub = lo_r + pc / SP_BOX_CH;      // unit index from the first tile's start
@@ -1143,7 +1148,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
             }
           }
         }
-        if (cur >= 0 && !*abort) flush(cur, NS);
+        if (cur >= 0 && !wabort()) flush(cur, NS);
       };
       if (op.nset == 2)
         run(std::integral_constant<int, 2>{});
@@ -1152,7 +1157,7 @@ __global__ void __maxnreg__(120) decode_step_kernel(const StepParams P) {
       cbar();  // every warp is done with xs and the slots
       // row-op groups completed here: the peers' partials, then the residual and the next input
       const int nd = std::min(S.ndefer, 64);
-      for (int i = warp; i < nd && !*abort; i += SP_NCW) {
+      for (int i = warp; i < nd && !wabort(); i += SP_NCW) {
         const int grp = S.defer[i];
         float v[2];
         sum_rows(op, 0, grp * 64 + 2 * lane, n, v[0], v[1]);
@@ -1385,11 +1390,7 @@ static StepLayout step_layout(const StepPlan& p) {
 template <int G>
 static cudaError_t launch_step(const StepPlan* p, cudaStream_t stream) {
   auto kern = decode_step_kernel<G>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
-  }
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p->grid);
@@ -1419,6 +1420,8 @@ static size_t step_static_smem() {
 
 template <int G>
 static void step_fit(size_t dyn, int* blocks, cudaFuncAttributes* fa) {
+  cudaFuncSetAttribute(decode_step_kernel<G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       cudaSharedmemCarveoutMaxShared);
   cudaFuncSetAttribute(decode_step_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, decode_step_kernel<G>, SP_THREADS, dyn);
   cudaFuncGetAttributes(fa, decode_step_kernel<G>);
