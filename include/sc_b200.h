@@ -319,6 +319,33 @@ int sc_p2p_allreduce(const void* send, void* recv, size_t count, int dtype, void
 int sc_p2p_allgather(const void* send, void* recv, size_t count_per_rank, int dtype, void* p2p,
                      cudaStream_t stream);
 
+/* ------------------------------------------------------------------ K7b --
+ * Temperature + top-p sampling over vocab-split logits (worker/executor.py:
+ * 270-306): logits / T, softmax, keep a token while the probability mass
+ * above it is <= top_p, renormalise, draw with a uniform u per row (inverse
+ * CDF over the kept tokens in vocabulary order).  A threshold found by a
+ * 4-level radix select on the probabilities' bits replaces the sort, so
+ * tensor-parallel ranks never gather the logits.
+ *   sc_sample_topp: one rank holding the whole vocabulary (one launch).
+ *   sc_sample_phase / sc_sample_combine: the same on each rank's vocab slice;
+ *     between phases the caller exchanges the fields of the field-major state
+ *     [8][B] at the start of the workspace (phase 0 -> all-gather field 0 and
+ *     combine what=0; 1 -> all-reduce-sum field 1; every phase 2 (levels
+ *     0..3) -> all-reduce-sum the [B][256] histograms that follow the state,
+ *     then phase 3 of that level; 4 -> all-gather field 4 and combine what=1;
+ *     5 -> all-reduce-sum field 7 and combine what=2, which writes tok).
+ *   sc_sample_uniforms: B uniforms from (seed, a device counter advanced by
+ *     one per call), the same on every rank. */
+size_t sc_sample_workspace_bytes(int B);
+int sc_sample_topp(const float* logits, int B, int V, int ld, float temperature, float top_p, const float* u,
+                   int vocab_start, int32_t* tok, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+int sc_sample_phase(const float* logits, int B, int V, int ld, float temperature, float top_p, const float* u,
+                    int vocab_start, int phase, int level, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream);
+int sc_sample_combine(void* workspace, const float* gathered, int B, int world, int rank, int what, int32_t* tok,
+                      cudaStream_t stream);
+int sc_sample_uniforms(uint64_t seed, unsigned long long* counter, int B, float* u, cudaStream_t stream);
+
 /* ----------------------------------------------------- persistent decode step --
  * One launch per greedy decode token of the tensor-parallel quantized Llama at
  * batch 1 (4-bit, group 64): the embedding gather, every layer's RMSNorm ->
@@ -366,6 +393,17 @@ size_t sc_step_workspace_bytes(void* step);
 int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 int sc_step_run(void* step, cudaStream_t stream);
 int sc_step_error(void* step, int reset);
+/* Where the first error was raised: out[0] op index, out[1] CTA, out[2] warp,
+ * out[3] the counter value seen, out[4] the target, then (n > 8) the op each
+ * CTA's consumers last started (the op count: step finished), one int per SM,
+ * then the step's dependency counters (input counts per op first). */
+int sc_step_error_info(void* step, int* out, int n);
+/* Optional per-op timing of later launches: stamps holds
+ * sc_step_timing_count(step) = SMs x ops x 4 uint64 %globaltimer values (ns)
+ * per CTA and op: op start, input ready, weight stream done, op done (0:
+ * not reached).  nullptr turns it off. */
+int sc_step_set_timing(void* step, unsigned long long* stamps);
+size_t sc_step_timing_count(void* step);
 /* After finalize: {SMs, CTAs per SM, static shared bytes, dynamic shared
  * bytes, registers per thread, max threads per block} of the step kernel. */
 int sc_step_fit(void* step, int* out6);

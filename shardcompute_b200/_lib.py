@@ -87,11 +87,19 @@ SIGNATURES = {
     "sc_step_finalize": (_i, [_vp, _vp, _sz, _vp]),
     "sc_step_run": (_i, [_vp, _vp]),
     "sc_step_error": (_i, [_vp, _i]),
+    "sc_step_error_info": (_i, [_vp, C.POINTER(_i), _i]),
+    "sc_step_set_timing": (_i, [_vp, _vp]),
+    "sc_step_timing_count": (C.c_size_t, [_vp]),
     "sc_step_fit": (_i, [_vp, C.POINTER(_i)]),
     "sc_qgemm_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "sc_qgemm": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp, _i, _vp, _i, _i,
                       _vp, _i, _vp, _sz, _vp]),
     "sc_qgemm_device_error": (_i, [_i]),
+    "sc_sample_workspace_bytes": (_sz, [_i]),
+    "sc_sample_topp": (_i, [_vp, _i, _i, _i, _f, _f, _vp, _i, _vp, _vp, _sz, _vp]),
+    "sc_sample_phase": (_i, [_vp, _i, _i, _i, _f, _f, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    "sc_sample_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "sc_sample_uniforms": (_i, [C.c_uint64, _vp, _i, _vp, _vp]),
     "sc_step_destroy": (_i, [_vp]),
 }
 

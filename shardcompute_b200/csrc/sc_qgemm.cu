@@ -49,7 +49,6 @@ constexpr int QM_NST = 3;                  // pipeline stages
 // stage: x_hi, x_lo, w_hi, w_lo tiles
 constexpr int QM_STAGE_BYTES = 4 * QM_TILE_BYTES;
 constexpr int QM_THREADS = 6 * 32;
-constexpr int QM_DQ0 = 2;                  // first dequant / epilogue warp
 constexpr uint64_t QM_WAIT_NS = 2000000000ull;
 
 __device__ int g_qgemm_error = 0;

@@ -113,6 +113,9 @@ struct StepParams {
   int* ctr;                  // counters
   int* gen;                  // completed steps (device)
   int* err;                  // error word
+  int* info;                 // where the first error was raised: op, CTA, warp, value seen, target
+  int* progress;             // [nsm] per CTA: the op its consumers last started (nops: step done)
+  unsigned long long* stamps;  // null, or [nsm][nops][4] %globaltimer: op start, input ready, stream done, op done
   int* head_done;
   int* attn_ctr;             // [2 parities][layers][Hkv] segment counts, reset every other step
   unsigned long long* key;   // [2] argmax keys by step parity
@@ -168,11 +171,22 @@ __device__ __forceinline__ uint4 ld_v4_volatile(const void* p) {
 }
 
 __device__ __forceinline__ void raise_err(const StepParams& P, int code) { atomicCAS(P.err, 0, code); }
+// The first error also records where: op index, CTA, warp, the value seen and the one waited for.
+__device__ __forceinline__ void raise_at(const StepParams& P, int code, int where, int seen, int target) {
+  if (atomicCAS(P.err, 0, code) == 0) {
+    volatile int* f = P.info;
+    f[0] = where;
+    f[1] = (int)blockIdx.x;
+    f[2] = (int)(threadIdx.x >> 5);
+    f[3] = seen;
+    f[4] = target;
+  }
+}
 __device__ __forceinline__ bool err_set(const StepParams& P) { return *reinterpret_cast<volatile int*>(P.err) != 0; }
 
 // Spin until ctr reaches target (wrap-safe), giving up after SP_WAIT_NS or
 // as soon as any CTA has raised the error word.
-__device__ bool wait_ctr(const StepParams& P, const int* ctr, int target, int code) {
+__device__ bool wait_ctr(const StepParams& P, const int* ctr, int target, int code, int where) {
   if ((int)(ld_acquire(ctr) - target) >= 0) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
@@ -180,7 +194,7 @@ __device__ bool wait_ctr(const StepParams& P, const int* ctr, int target, int co
     if ((i & 31) == 0) {
       if (err_set(P)) return false;
       if (globaltimer_ns() - t0 > SP_WAIT_NS) {
-        raise_err(P, code);
+        raise_at(P, code, where, ld_acquire(ctr), target);
         return false;
       }
     }
@@ -190,7 +204,7 @@ __device__ bool wait_ctr(const StepParams& P, const int* ctr, int target, int co
 // One mbarrier wait for a whole warp (the lanes vote), bounded, watching the
 // CTA's abort flag and the global error word.
 __device__ __forceinline__ bool mbar_wait_all(const StepParams& P, uint64_t* bar, uint32_t parity,
-                                              volatile int* abort) {
+                                              volatile int* abort, int where) {
   if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
   bool ok = true;
   if (!mbar_try_wait(bar, parity)) {
@@ -203,7 +217,7 @@ __device__ __forceinline__ bool mbar_wait_all(const StepParams& P, uint64_t* bar
           break;
         }
         if (globaltimer_ns() - t0 > SP_WAIT_NS) {
-          raise_err(P, SPE_RING);
+          raise_at(P, SPE_RING, where, (int)parity, -1);
           ok = false;
           break;
         }
@@ -219,6 +233,11 @@ __device__ __host__ __forceinline__ int owner_of(long long u, long long T, int n
   return (int)(((u + 1) * n - 1) / T);
 }
 __device__ __host__ __forceinline__ long long range_lo(int c, long long T, int n) { return (long long)c * T / n; }
+
+// CTAs a GEMV's T units are split over: every CTA of the split holds at least
+// one unit, so the CTAs between a tile's first and last owner all hold a piece
+// of it (the segment count below relies on that).
+__device__ __host__ __forceinline__ int gemv_ctas(long long T, int n) { return (int)std::min<long long>(T, n); }
 
 // First CTA holding tile t (units [t*kq, (t+1)*kq)) and the tile's segment count.
 __device__ __host__ __forceinline__ int tile_first(int t, int kq, long long T, int n) {
@@ -568,7 +587,8 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           continue;
         }
         // GEMV: this CTA's units, SP_STAGE_BOXES / nset per stage
-        const long long lo = range_lo(c, op.total, n), hi = range_lo(c + 1, op.total, n);
+        const int nC = gemv_ctas(op.total, n);
+        const long long lo = c < nC ? range_lo(c, op.total, nC) : 0, hi = c < nC ? range_lo(c + 1, op.total, nC) : 0;
         const int qps = SP_STAGE_BOXES / op.nset;
         for (long long u0 = lo; u0 < hi && ok; u0 += qps) {
           int s;
@@ -626,8 +646,13 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
   // the CTA's abort flag as one decision for the whole warp (before shuffles / votes)
   auto wabort = [&]() -> bool { return __any_sync(0xffffffffu, *abort != 0); };
 
+  auto stamp = [&](int oi, int k) {
+    if (P.stamps && tid == 0) P.stamps[((size_t)c * P.nops + oi) * 4 + k] = globaltimer_ns();
+  };
   for (int oi = 0; oi < P.nops; ++oi) {
     const StepOp& op = P.ops[oi];
+    if (tid == 0) *reinterpret_cast<volatile int*>(P.progress + c) = oi;
+    stamp(oi, 0);
     // ---------------------------------------------------------------- embedding
     if (op.kind == SOP_EMBED) {
       const int ng = P.H / 64;
@@ -659,6 +684,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
         __threadfence();
         if (lane == 0) atomicAdd(P.ctr + op.out_ctr, 1);
       }
+      stamp(oi, 3);
       continue;
     }
 
@@ -666,8 +692,10 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
     if (op.kind == SOP_ATTN) {
       if (c >= na) continue;
       const StepOp& qop = P.ops[oi - 1];  // this layer's q|k|v GEMV
+      const int nQ = gemv_ctas(qop.total, n);
       const long long lo = range_lo(c, TA, na), hi = range_lo(c + 1, TA, na);
-      if (tid == 0 && !*abort && !wait_ctr(P, P.ctr + qop.grp_ctr, (gen + 1) * qop.seg_need, SPE_QKV)) *abort = 1;
+      if (tid == 0 && !*abort && !wait_ctr(P, P.ctr + qop.grp_ctr, (gen + 1) * qop.seg_need, SPE_QKV, oi)) *abort = 1;
+      stamp(oi, 1);
       cbar();
       const int LPK = HD / 8, KPW = 32 / LPK;  // lanes per key, keys per warp
       const int sub = lane / LPK, dl = lane % LPK;
@@ -683,17 +711,17 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           for (int e = tid; e < G * HD / 2; e += SP_NC) {
             const int gq = e / (HD / 2), d = e % (HD / 2);
             const int r = (h * G + gq) * HD + d;
-            const float x1 = qkv_row(qop, r, n), x2 = qkv_row(qop, r + HD / 2, n);
+            const float x1 = qkv_row(qop, r, nQ), x2 = qkv_row(qop, r + HD / 2, nQ);
             const float cs = P.cos_tab[(size_t)pos * (HD / 2) + d], sn = P.sin_tab[(size_t)pos * (HD / 2) + d];
             s_q[gq][d] = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(-x2, sn));
             s_q[gq][d + HD / 2] = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
           }
           if (has_new) {
             for (int e = tid; e < HD; e += SP_NC) {
-              s_vnew[e] = qkv_row(qop, (P.Hq + P.Hkv + h) * HD + e, n);
+              s_vnew[e] = qkv_row(qop, (P.Hq + P.Hkv + h) * HD + e, nQ);
               if (e < HD / 2) {
                 const int rk = (P.Hq + h) * HD + e;
-                const float x1 = qkv_row(qop, rk, n), x2 = qkv_row(qop, rk + HD / 2, n);
+                const float x1 = qkv_row(qop, rk, nQ), x2 = qkv_row(qop, rk + HD / 2, nQ);
                 const float cs = P.cos_tab[(size_t)pos * (HD / 2) + e], sn = P.sin_tab[(size_t)pos * (HD / 2) + e];
                 s_knew[e] = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(-x2, sn));
                 s_knew[e + HD / 2] = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
@@ -720,7 +748,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           const int s = (int)(it % (uint32_t)P.nst);
           const uint32_t ph = (it / (uint32_t)P.nst) & 1u;
           ++it;
-          if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort)) {
+          if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort, oi)) {
             *abort = 1;
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s]);
@@ -873,16 +901,19 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
         cbar();
         u = seg_end;
       }
+      stamp(oi, 3);
       continue;
     }
 
     // ---------------------------------------------------------------- GEMV
-    const long long lo = range_lo(c, op.total, n), hi = range_lo(c + 1, op.total, n);
+    const int nC = gemv_ctas(op.total, n);
+    const long long lo = c < nC ? range_lo(c, op.total, nC) : 0, hi = c < nC ? range_lo(c + 1, op.total, nC) : 0;
     if (lo < hi) {
       // input complete, then staged into shared memory (plain loads: the
       // finishing CTAs wrote it with plain stores, released by their counters)
       if (tid == 0) {
-        if (!*abort && !wait_ctr(P, P.ctr + op.x_ctr, (gen + 1) * op.x_need, SPE_INPUT)) *abort = 1;
+        if (!*abort && !wait_ctr(P, P.ctr + op.x_ctr, (gen + 1) * op.x_need, SPE_INPUT, oi)) *abort = 1;
+        stamp(oi, 1);
         for (int i = 0; i < SP_WIN; ++i) {
           S.cnt[i] = 0;
           S.free_at[i] = i;
@@ -939,7 +970,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           __threadfence_block();
           *reinterpret_cast<volatile int*>(&S.free_at[slot]) = j + SP_WIN;
         }
-        const int nseg_t = tile_nseg(tile, op.kq, op.total, n);
+        const int nseg_t = tile_nseg(tile, op.kq, op.total, nC);
         if (op.kind == SOP_HEAD && nseg_t == 1) {
           // the whole tile is here: logits straight into this CTA's argmax candidate
           unsigned long long k = 0ull;
@@ -952,7 +983,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           if (lane == 0) atomicMax(&S.key, k);
           return;
         }
-        const int segslot = c - tile_first(tile, op.kq, op.total, n);
+        const int segslot = c - tile_first(tile, op.kq, op.total, nC);
         if (a < op.nset) op.part[(((size_t)tile * SP_MAXT + segslot) * op.nset + a) * 16 + row] = v;
         __syncwarp();
         __threadfence();
@@ -983,7 +1014,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
         // O / DOWN / GATEUP: the group of four tiles
         const int grp = tile >> 2;
         int need = 0;
-        for (int tt = grp * 4; tt < grp * 4 + 4; ++tt) need += tile_nseg(tt, op.kq, op.total, n);
+        for (int tt = grp * 4; tt < grp * 4 + 4; ++tt) need += tile_nseg(tt, op.kq, op.total, nC);
         int last = 0;
         if (lane == 0) last = atomicAdd(P.ctr + op.grp_ctr + grp, 1) + 1 - (gen + 1) * need == 0;
         last = __shfl_sync(0xffffffffu, last, 0);
@@ -992,7 +1023,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
         if (P.world > 1 && op.kind != SOP_GATEUP) {
           // push this rank's sums now; receive after the stream (see push_group)
           float v0, v1;
-          sum_rows(op, 0, grp * 64 + 2 * lane, n, v0, v1);
+          sum_rows(op, 0, grp * 64 + 2 * lane, nC, v0, v1);
           push_group(P, op.xchg, grp, v0, v1, lane, gen);
           if (lane == 0) {
             const int i = atomicAdd(&S.ndefer, 1);
@@ -1001,7 +1032,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           }
           return;
         }
-        finish_group(P, op, grp, lane, n, gen);
+        finish_group(P, op, grp, lane, nC, gen);
       };
 
       float acc[2][4];
@@ -1067,7 +1098,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           const int s = (int)(it % (uint32_t)P.nst);
           const uint32_t ph = (it / (uint32_t)P.nst) & 1u;
           ++it;
-          if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort)) {
+          if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort, oi)) {
             *abort = 1;
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s]);
@@ -1155,17 +1186,18 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
       else
         run(std::integral_constant<int, 1>{});
       cbar();  // every warp is done with xs and the slots
+      stamp(oi, 2);
       // row-op groups completed here: the peers' partials, then the residual and the next input
       const int nd = std::min(S.ndefer, 64);
       for (int i = warp; i < nd && !wabort(); i += SP_NCW) {
         const int grp = S.defer[i];
         float v[2];
-        sum_rows(op, 0, grp * 64 + 2 * lane, n, v[0], v[1]);
+        sum_rows(op, 0, grp * 64 + 2 * lane, nC, v[0], v[1]);
         if (!recv_group(P, op.xchg, grp, v[0], v[1], lane, gen)) {
           *abort = 1;
           break;
         }
-        finish_group(P, op, grp, lane, n, gen, v);
+        finish_group(P, op, grp, lane, nC, gen, v);
       }
     }
     if (op.kind == SOP_HEAD && tid == 0) {
@@ -1216,7 +1248,10 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
         atomicAdd(P.gen, 1);
       }
     }
+    stamp(oi, 3);
   }
+  // (after an error the record keeps the op each CTA gave up in)
+  if (tid == 0 && !err_set(P)) *reinterpret_cast<volatile int*>(P.progress + c) = P.nops;
 }
 
 // ---------------------------------------------------------------- host side
@@ -1246,6 +1281,7 @@ struct StepPlan {
   int max_pos = 0;
   float* trace = nullptr;
   float* logits = nullptr;
+  unsigned long long* stamps = nullptr;
   char* arena[SP_MAX_WORLD] = {};
   size_t arena_bytes = 0;
   bool ready = false;
@@ -1318,6 +1354,7 @@ struct StepLayout {
   size_t ops, maps, ctr, part_qkv, part_o, part_gu, part_down, part_head, attn_part, xs_h, xss_h, xs_o, xs_gu,
       xss_gu, xs_down, h, pad, total;
   size_t pad_layer;  // padded scale + bias bytes per layer
+  size_t progress;
   int nctr, nops, nmaps, max_groups;
   int ctr_x, ctr_grp, ctr_head_tile, ctr_attn, ctr_misc;
   int xs_bytes_h, xs_bytes_o, xs_bytes_down;
@@ -1339,7 +1376,7 @@ static StepLayout step_layout(const StepPlan& p) {
   L.ctr_head_tile = L.ctr_grp + L.nops * L.max_groups;
   L.ctr_attn = L.ctr_head_tile + (p.Vl + 15) / 16;
   L.ctr_misc = (L.ctr_attn + 2 * nl * p.Hkv + 1) / 2 * 2;  // even: the 8-byte keys follow
-  L.nctr = L.ctr_misc + 8;
+  L.nctr = L.ctr_misc + 16;  // gen, err, head_done, -, keys[2], -, -, info[8]
   size_t o = 0;
   L.ops = o;
   o = align_up(o + sizeof(StepOp) * L.nops, 128);
@@ -1347,6 +1384,8 @@ static StepLayout step_layout(const StepPlan& p) {
   o = align_up(o + sizeof(CUtensorMap) * L.nmaps, 128);
   L.ctr = o;
   o = align_up(o + sizeof(int) * L.nctr, 128);
+  L.progress = o;
+  o = align_up(o + sizeof(int) * p.nsm, 128);
   auto part = [&](int rows, int nset) {
     return align_up(sizeof(float) * (size_t)((rows + 15) / 16) * SP_MAXT * nset * 16, 128);
   };
@@ -1544,6 +1583,21 @@ int sc_step_set_io(void* step, int32_t* tok, int32_t* pos, const float* cos_tab,
   return SC_OK;
 }
 
+int sc_step_set_timing(void* step, unsigned long long* stamps) {
+  using namespace sc;
+  SC_REQUIRE(step, SC_ERR_ARG, "step_set_timing: null handle");
+  StepPlan* p = static_cast<StepPlan*>(step);
+  p->stamps = stamps;
+  p->P.stamps = stamps;  // launches after this call (a captured graph keeps what it captured)
+  return SC_OK;
+}
+
+size_t sc_step_timing_count(void* step) {
+  if (!step) return 0;
+  const sc::StepPlan* p = static_cast<const sc::StepPlan*>(step);
+  return (size_t)p->nsm * (2 + 5 * (size_t)p->nl) * 4;
+}
+
 size_t sc_step_arena_bytes(int hidden, int world) {
   return sc::SP_ARENA_HDR + 2 * (size_t)world * (size_t)hidden / 2 * 16 + 2 * (size_t)world * 16;
 }
@@ -1676,7 +1730,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
     q.x_need = H / 64;
     q.part = reinterpret_cast<float*>(ws + L.part_qkv);
     q.grp_ctr = L.ctr_grp + oq * L.max_groups;
-    for (int tt = 0; tt < q.tiles; ++tt) q.seg_need += tile_nseg(tt, q.kq, q.total, n);
+    for (int tt = 0; tt < q.tiles; ++tt) q.seg_need += tile_nseg(tt, q.kq, q.total, gemv_ctas(q.total, n));
     ops.push_back(q);
     StepOp a{};
     a.kind = SOP_ATTN;
@@ -1748,7 +1802,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
   for (const auto& o : ops) {
     if (o.kind == SOP_EMBED || o.kind == SOP_ATTN) continue;
     for (int tt = 0; tt < o.tiles; ++tt)
-      SC_REQUIRE(tile_nseg(tt, o.kq, o.total, n) <= SP_MAXT, SC_ERR_UNSUPPORTED,
+      SC_REQUIRE(tile_nseg(tt, o.kq, o.total, gemv_ctas(o.total, n)) <= SP_MAXT, SC_ERR_UNSUPPORTED,
                  "step_finalize: a tile of op kind %d spans more than %d CTAs", o.kind, SP_MAXT);
   }
   // ---- shared memory: staged x (or an attention merge), then as many ring stages as fit
@@ -1796,6 +1850,9 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
   P.attn_ctr = ctr + L.ctr_attn;
   P.gen = ctr + L.ctr_misc + 0;
   P.err = ctr + L.ctr_misc + 1;
+  P.info = ctr + L.ctr_misc + 8;
+  P.progress = reinterpret_cast<int*>(ws + L.progress);
+  P.stamps = p->stamps;
   P.head_done = ctr + L.ctr_misc + 2;
   P.key = reinterpret_cast<unsigned long long*>(ctr + L.ctr_misc + 4);
   P.tok = p->tok;
@@ -1865,6 +1922,20 @@ int sc_step_error(void* step, int reset) {
     cudaMemset(p->P.ctr, 0, sizeof(int) * L.nctr);
   }
   return v;
+}
+
+int sc_step_error_info(void* step, int* out, int n) {
+  using namespace sc;
+  SC_REQUIRE(step && out && n >= 8, SC_ERR_ARG, "step_error_info: null pointer or fewer than 8 ints");
+  StepPlan* p = static_cast<StepPlan*>(step);
+  SC_REQUIRE(p->ready, SC_ERR_ARG, "step_error_info: call sc_step_finalize first");
+  cudaError_t e = cudaMemcpy(out, p->P.info, 8 * sizeof(int), cudaMemcpyDeviceToHost);
+  const int np = std::min(n - 8, p->nsm);
+  if (e == cudaSuccess && np > 0) e = cudaMemcpy(out + 8, p->P.progress, np * sizeof(int), cudaMemcpyDeviceToHost);
+  const int nc = std::min(n - 8 - p->nsm, step_layout(*p).nctr);
+  if (e == cudaSuccess && nc > 0) e = cudaMemcpy(out + 8 + p->nsm, p->P.ctr, nc * sizeof(int), cudaMemcpyDeviceToHost);
+  SC_REQUIRE(e == cudaSuccess, SC_ERR_CUDA, "step_error_info: copy failed (%s)", cudaGetErrorString(e));
+  return SC_OK;
 }
 
 int sc_step_fit(void* step, int* out6) {

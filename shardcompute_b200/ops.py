@@ -310,3 +310,77 @@ def argmax_merge(vals: torch.Tensor, idxs: torch.Tensor, world: int, token_out: 
     L.call("sc_argmax_merge", _p(vals), _p(idxs), M, world, _p(token_out), _p(pos), pos_advance,
            stream_handle(vals.device))
     return token_out
+
+
+# ---------------------------------------------------------------- K7b: temperature + top-p sampling
+
+_ST_N, _ST_MAX, _ST_Z, _ST_KEPT, _ST_TOKEN = 8, 0, 1, 4, 7
+
+
+def sample_workspace_bytes(B: int) -> int:
+    return int(L.load().sc_sample_workspace_bytes(B))
+
+
+def sample_uniforms(seed: int, counter: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """Fill ``u`` (float32 [B]) with uniforms from (seed, the int64 device
+    ``counter``), advancing the counter on the device (capturable)."""
+    _cuda(counter, u)
+    if counter.dtype != torch.int64 or u.dtype != torch.float32:
+        raise ValueError("counter must be int64 and u float32")
+    L.call("sc_sample_uniforms", C.c_uint64(seed & 0xFFFFFFFFFFFFFFFF), _p(counter), u.numel(), _p(u),
+           stream_handle(u.device))
+    return u
+
+
+def sample_topp(logits: torch.Tensor, temperature: float, top_p: float, u: torch.Tensor, tok: torch.Tensor,
+                comm=None, vocab_start: int = 0, workspace: Optional[torch.Tensor] = None,
+                gather: Optional[torch.Tensor] = None):
+    """Temperature + top-p draw from ``logits`` (float32 [B, V_local]) into
+    ``tok`` (int32 [B]) -- the sampled branch of the reference's generate
+    (worker/executor.py:270-306).  ``comm`` (tensor parallel): each rank
+    passes its vocab slice and the ranks exchange only per-row scalars and
+    256-bin histograms (all-gather / all-reduce on the current stream), never
+    the logits; every rank ends with the same token in ``tok`` (global ids).
+    ``tok`` keeps its value for a row whose draw found no token."""
+    _cuda(logits, u, tok, workspace, gather)
+    if logits.dtype != torch.float32 or logits.dim() != 2 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous float32 [B, V] tensor")
+    if temperature <= 0.0 or top_p <= 0.0:
+        raise ValueError("temperature and top_p must be positive (temperature 0 is the greedy argmax)")
+    B, V = logits.shape
+    nbytes = sample_workspace_bytes(B)
+    if workspace is None:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=logits.device)
+    stream = stream_handle(logits.device)
+    ws = workspace.data_ptr()
+    world = 1 if comm is None else comm.world_size
+    if world == 1:
+        L.call("sc_sample_topp", _p(logits), B, V, V, float(temperature), float(top_p), _p(u), int(vocab_start),
+               _p(tok), ws, nbytes, stream)
+        return tok
+    rank = comm.rank
+    st = workspace[: _ST_N * B * 4].view(torch.float32).view(_ST_N, B)
+    hist = workspace[_ST_N * B * 4: nbytes].view(torch.float32)
+    if gather is None:
+        gather = torch.empty(world, B, dtype=torch.float32, device=logits.device)
+
+    def phase(ph, level=0):
+        L.call("sc_sample_phase", _p(logits), B, V, V, float(temperature), float(top_p), _p(u), int(vocab_start), ph,
+               level, ws, nbytes, stream)
+
+    phase(0)
+    comm.allgather_into(st[_ST_MAX], gather)
+    L.call("sc_sample_combine", ws, _p(gather), B, world, rank, 0, None, stream)
+    phase(1)
+    comm.allreduce_into(st[_ST_Z], st[_ST_Z], "sum")
+    for level in range(4):
+        phase(2, level)
+        comm.allreduce_into(hist, hist, "sum")
+        phase(3, level)
+    phase(4)
+    comm.allgather_into(st[_ST_KEPT], gather)
+    L.call("sc_sample_combine", ws, _p(gather), B, world, rank, 1, None, stream)
+    phase(5)
+    comm.allreduce_into(st[_ST_TOKEN], st[_ST_TOKEN], "sum")
+    L.call("sc_sample_combine", ws, None, B, world, rank, 2, _p(tok), stream)
+    return tok

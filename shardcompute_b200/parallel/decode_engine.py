@@ -116,8 +116,15 @@ class DecodeEngine:
         self._step = None
         self._step_ws: Optional[torch.Tensor] = None
         self.step_trace: Optional[torch.Tensor] = None   # [L+1, H] hidden states of the last step (debug)
-        self.step_logits: Optional[torch.Tensor] = None  # [V/TP] logits of the last step (debug)
+        # [V/TP] logits of the last one-kernel step (the sampler's input)
+        self.step_logits = torch.zeros(self.Vl, dtype=torch.float32, device=dev)
         self._step_debug = False
+        # sampling (temperature 0: greedy argmax); uniforms from a device counter
+        self.temperature, self.top_p, self.seed = 0.0, 1.0, 0
+        self._u = torch.zeros(self.B, dtype=torch.float32, device=dev)
+        self._rng_counter = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._sample_ws = torch.empty(ops.sample_workspace_bytes(self.B), dtype=torch.uint8, device=dev)
+        self._sample_gather = torch.zeros(self.world, self.B, dtype=torch.float32, device=dev)
 
     # ------------------------------------------------------------ buffers
 
@@ -297,6 +304,7 @@ class DecodeEngine:
             ops.argmax_merge(bf["gval"], bf["gidx"], self.world, self.tok[:B], self.pos, advance)
         else:
             ops.argmax_merge(bf["val"].view(1, B), bf["idx"].view(1, B), 1, self.tok[:B], self.pos, advance)
+        self._draw(bf["logits"][:B], B)
 
     # ------------------------------------------------------------ public steps
 
@@ -365,11 +373,10 @@ class DecodeEngine:
                     "sc_step_set_head")
             if self._step_debug:
                 self.step_trace = torch.zeros(cfg.num_layers + 1, self.H, dtype=torch.float32, device=dev)
-                self.step_logits = torch.zeros(self.Vl, dtype=torch.float32, device=dev)
             L.check(lib.sc_step_set_io(h, self.tok.data_ptr(), self.pos.data_ptr(), self.cos.data_ptr(),
                                        self.sin.data_ptr(), self.cos.shape[0],
                                        None if self.step_trace is None else self.step_trace.data_ptr(),
-                                       None if self.step_logits is None else self.step_logits.data_ptr()),
+                                       self.step_logits.data_ptr()),
                     "sc_step_set_io")
             if self.world > 1:
                 bases, size = self.comm.step_arena(int(lib.sc_step_arena_bytes(self.H, self.world)))
@@ -384,16 +391,113 @@ class DecodeEngine:
             raise
         self._step = h
 
+    # ------------------------------------------------------------ sampling
+
+    def set_sampling(self, temperature: float = 0.0, top_p: float = 1.0, seed: int = 0):
+        """Sampled decoding (the reference's generate with temperature > 0,
+        worker/executor.py:270-306): every token is drawn from the
+        temperature + top-p distribution on the GPU, inside the captured
+        step; temperature 0 is greedy.  Restarts the uniform stream."""
+        if temperature < 0.0 or not (0.0 < top_p <= 1.0):
+            raise ValueError("temperature must be >= 0 and top_p in (0, 1]")
+        if (temperature, top_p, seed) != (self.temperature, self.top_p, self.seed):
+            self.graph = None  # the captured step changes
+        self.temperature, self.top_p, self.seed = float(temperature), float(top_p), int(seed)
+        self._rng_counter.zero_()
+
+    def _draw(self, logits: torch.Tensor, B: int):
+        """Overwrite the greedy token with a temperature + top-p draw from
+        this rank's vocab-split ``logits`` [B, V/TP] (a no-op when greedy)."""
+        if self.temperature <= 0.0:
+            return
+        ops.sample_uniforms(self.seed, self._rng_counter, self._u[:B])
+        gather = self._sample_gather if B == self.B else self._sample_gather[:, :B].contiguous()
+        ops.sample_topp(logits, self.temperature, self.top_p, self._u[:B], self.tok[:B],
+                        comm=self.comm if self.world > 1 else None, vocab_start=self.w.vocab_start,
+                        workspace=self._sample_ws, gather=gather)
+
     def step_error(self, reset: bool = False) -> int:
         """The one-kernel step's device error word (0: fine); synchronises."""
         if self._step is None:
             return 0
         return int(L.load().sc_step_error(self._step, 1 if reset else 0))
 
+    STEP_ERRORS = {1: "position outside the cache", 2: "weight ring", 3: "peer exchange", 4: "q|k|v not complete",
+                   5: "GEMV input not complete", 6: "output slot", 7: "argmax exchange"}
+
+    def step_profile(self, steps: int = 4) -> dict:
+        """Time the one-kernel step's ops from inside the kernel (per-CTA
+        %globaltimer stamps) over `steps` eager steps; returns, per op kind,
+        the step time spent on the critical path (the latest CTA's finish of
+        that op minus the latest finish of the op before it), summed over the
+        layers, plus per-op medians (input wait, weight stream) of the last
+        step.  Advances the decode position by `steps`."""
+        if not self.use_step:
+            raise RuntimeError("step_profile: this engine does not run the one-kernel step")
+        if self._step is None:
+            self._build_step()
+        lib = L.load()
+        nsm = torch.cuda.get_device_properties(self.device).multi_processor_count
+        nops = 2 + 5 * self.cfg.num_layers
+        stamps = torch.zeros(int(lib.sc_step_timing_count(self._step)), dtype=torch.int64, device=self.device)
+        L.check(lib.sc_step_set_timing(self._step, stamps.data_ptr()), "sc_step_set_timing")
+        try:
+            for _ in range(steps):
+                self.decode_step()
+            torch.cuda.synchronize(self.device)
+        finally:
+            L.check(lib.sc_step_set_timing(self._step, None), "sc_step_set_timing")
+        self.check_step()
+        t = stamps.view(nsm, nops, 4).cpu().numpy().astype(np.float64)
+        kinds = ["embed"] + ["qkv", "attn", "o", "gateup", "down"] * self.cfg.num_layers + ["head"]
+        valid = t > 0
+        done = np.where(valid[:, :, 3], t[:, :, 3], -np.inf).max(axis=0)
+        start0 = np.where(valid[:, 0, 0], t[:, 0, 0], np.inf).min()
+        crit, prev = {}, start0
+        per_op = []
+        for i, k in enumerate(kinds):
+            d = max(done[i], prev)
+            crit[k] = crit.get(k, 0.0) + (d - prev) / 1e3
+            prev = d
+            w = t[:, i, 1] - t[:, i, 0]
+            sdur = t[:, i, 2] - t[:, i, 1]
+            ok1 = valid[:, i, 1] & valid[:, i, 0]
+            ok2 = valid[:, i, 2] & valid[:, i, 1]
+            per_op.append({"op": i, "kind": k, "ctas": int(valid[:, i, 3].sum()),
+                           "wait_us_med": float(np.median(w[ok1])) / 1e3 if ok1.any() else None,
+                           "stream_us_med": float(np.median(sdur[ok2])) / 1e3 if ok2.any() else None,
+                           "stream_us_max": float(np.max(sdur[ok2])) / 1e3 if ok2.any() else None,
+                           "finish_us": (done[i] - start0) / 1e3})
+        return {"step_us": (prev - start0) / 1e3, "critical_us_by_kind": crit, "ops": per_op}
+
+    def step_error_info(self) -> dict:
+        """Where the step kernel's first error was raised (op index and kind,
+        CTA, warp, counter seen / target) and the op each CTA last started."""
+        if self._step is None:
+            return {}
+        nsm = torch.cuda.get_device_properties(self.device).multi_processor_count
+        nops = 2 + 5 * self.cfg.num_layers
+        n = 8 + nsm + nops
+        buf = (C.c_int * n)()
+        L.check(L.load().sc_step_error_info(self._step, buf, n), "sc_step_error_info")
+        kinds = ["embed"] + ["qkv", "attn", "o", "gateup", "down"] * self.cfg.num_layers + ["head"]
+        op = buf[0]
+        prog = list(buf[8:8 + nsm])
+        where = {}
+        for c, v in enumerate(prog):
+            if v != nops:
+                where.setdefault(v, []).append(c)
+        return {"op": op, "kind": kinds[op] if 0 <= op < nops else "?", "layer": (op - 1) // 5 if 0 < op < nops - 1
+                else -1, "cta": buf[1], "warp": buf[2], "seen": buf[3], "target": buf[4],
+                "ctas_by_op": {f"{k}:{kinds[k] if 0 <= k < nops else '?'}": (len(v), v[:6]) for k, v in
+                               sorted(where.items())},
+                "input_counts": list(buf[8 + nsm:8 + nsm + nops])}
+
     def check_step(self):
         code = self.step_error()
         if code:
-            raise TimeoutError(f"rank {self.rank}: the decode step kernel gave up on a wait (error {code})")
+            raise TimeoutError(f"rank {self.rank}: the decode step kernel gave up on a wait (error {code}: "
+                               f"{self.STEP_ERRORS.get(code, '?')}; {self.step_error_info()})")
 
     def __del__(self):
         try:
@@ -410,6 +514,7 @@ class DecodeEngine:
             if self._step is None:
                 self._build_step()
             L.call("sc_step_run", self._step, ops.stream_handle(self.device))
+            self._draw(self.step_logits.view(1, self.Vl), 1)
             return
         B = self.B
         bf = self._buffers(B, 1)
@@ -424,6 +529,7 @@ class DecodeEngine:
         self._graph_stream.wait_stream(torch.cuda.current_stream(self.device))
         pos0 = self.pos.clone()
         tok0 = self.tok.clone()
+        rng0 = self._rng_counter.clone()
         hp0 = self.host_pos
         with torch.cuda.stream(self._graph_stream):
             self.decode_step()  # warm-up: plans, tensor maps, lazy module loads
@@ -434,10 +540,12 @@ class DecodeEngine:
             self.decode_step()
         torch.cuda.synchronize(self.device)
         self.host_pos = hp0
-        # the eager warm-up advanced the position and wrote one cache slot that
-        # the next real step overwrites; put the position and token back
+        # the eager warm-up advanced the position, wrote one cache slot that
+        # the next real step overwrites and drew one uniform (sampled decoding);
+        # put the position, token and uniform stream back
         self.pos.copy_(pos0)
         self.tok.copy_(tok0)
+        self._rng_counter.copy_(rng0)
         return self.graph
 
     def capture_probe(self):

@@ -20,6 +20,7 @@ from typing import Any, Awaitable, Callable, Dict, List, Optional
 
 import torch
 
+from .. import ops
 from ..parallel.decode_engine import DecodeEngine
 from ..parallel.transformer import ParallelTransformer
 
@@ -76,6 +77,7 @@ class ParallelExecutor:
         self.engine = engine
         self.last_metrics: Optional[ExecutionMetrics] = None
         self._past_key_values = None
+        self.seed = 0  # seed of the sampled branch's uniform stream
 
     async def forward(self, input_ids: torch.Tensor, attention_mask=None, use_cache: bool = False) -> torch.Tensor:
         if self.model is None:
@@ -140,26 +142,35 @@ class ParallelExecutor:
         return out
 
     async def _generate_sampled(self, input_ids, max_new_tokens, temperature, top_p, stop_tokens, token_callback):
+        """The sampled branch (worker/executor.py:270-306): with the decode
+        engine every draw runs on the GPU inside the captured step (tensor
+        parallel: a distributed top-p over the vocab-split logits); without
+        it, the layer model's gathered logits go through the same sampling
+        kernel."""
+        if self.engine is not None:
+            self.engine.set_sampling(temperature, top_p, seed=self.seed)
+            try:
+                return await self._generate_greedy(input_ids, max_new_tokens, stop_tokens, token_callback)
+            finally:
+                self.engine.set_sampling(0.0)
         if self.model is None:
-            raise RuntimeError("sampling needs the layer model")
+            raise RuntimeError("sampling needs the decode engine or the layer model")
         self._past_key_values = None
         logits = await self.forward(input_ids, use_cache=True)
         out = []
-        gen = torch.Generator(device=logits.device)
-        gen.manual_seed(0)
+        B = logits.shape[0]
+        dev = logits.device
+        counter = torch.zeros(1, dtype=torch.int64, device=dev)
+        u = torch.empty(B, dtype=torch.float32, device=dev)
+        tok = torch.empty(B, dtype=torch.int32, device=dev)
         for i in range(max_new_tokens):
-            nl = logits[:, -1, :].float()
+            nl = logits[:, -1, :].float().contiguous()
             if temperature == 0:
-                nxt = torch.argmax(nl, dim=-1)
+                tok.copy_(torch.argmax(nl, dim=-1))
             else:
-                probs = torch.softmax(nl / temperature, dim=-1)
-                sp, si = torch.sort(probs, dim=-1, descending=True)
-                keep = torch.cumsum(sp, dim=-1) <= top_p
-                keep = torch.cat([torch.ones_like(keep[:, :1]), keep[:, :-1]], dim=-1)
-                sp = torch.where(keep, sp, torch.zeros_like(sp))
-                sp = sp / sp.sum(-1, keepdim=True)
-                pick = torch.multinomial(sp, 1, generator=gen)
-                nxt = torch.gather(si, -1, pick)[:, 0]
+                ops.sample_uniforms(self.seed, counter, u)
+                ops.sample_topp(nl, temperature, top_p, u, tok)
+            nxt = tok.clone()
             out.append(nxt)
             tid = int(nxt[0])
             is_stop = tid in stop_tokens
@@ -168,7 +179,7 @@ class ParallelExecutor:
                 await token_callback(tid, i, is_last)
             if is_last:
                 break
-            logits = await self.forward(nxt[:, None].to(torch.int32), use_cache=True)
+            logits = await self.forward(nxt[:, None], use_cache=True)
         return out
 
     def reset_cache(self):

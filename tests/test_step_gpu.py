@@ -60,7 +60,7 @@ def test_step_kernel_hidden_states_and_logits(cuda, name):
     for step in range(3):
         eng.decode_step()  # one launch: embedding of tok ... argmax
         torch.cuda.synchronize()
-        assert eng.step_error() == 0
+        assert eng.step_error() == 0, eng.step_error_info()
         rl, rh = ref.forward(np.array([[tok]]), return_hidden=True)
         trace = eng.step_trace.double().cpu().numpy()
         for i, r in enumerate(rh):
@@ -86,7 +86,7 @@ def test_step_kernel_greedy_128_graph(cuda):
     ref_tok = ref.generate(prompt, steps)[0]
     out = eng.generate(torch.from_numpy(prompt).to(cuda), steps).cpu().numpy()[0]  # CUDA-graph replays
     assert float(np.mean(out == ref_tok)) >= 0.99, f"{out[:20]} vs {ref_tok[:20]}"
-    assert eng.step_error() == 0
+    assert eng.step_error() == 0, eng.step_error_info()
 
 
 def test_step_kernel_stops_cleanly_past_the_cache(cuda):
@@ -100,7 +100,7 @@ def test_step_kernel_stops_cleanly_past_the_cache(cuda):
     eng.prefill(torch.zeros(1, 8, dtype=torch.int64, device=cuda))
     eng.decode_step()
     torch.cuda.synchronize()
-    assert eng.step_error() == 0
+    assert eng.step_error() == 0, eng.step_error_info()
     tok0 = int(eng.tok[0])
     eng.pos.fill_(32)  # == max_seq: outside the cache
     eng.host_pos = 0
