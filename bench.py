@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: build this many decoder layers instead of the model's")
+    ap.add_argument("--workload", choices=["cfg3", "cfg2", "cfg4"], default="cfg3",
+                    help="cfg3: the decode step (default, the headline); cfg2: the isolated quantized-linear sweep; "
+                         "cfg4: the vocab-parallel embedding + LM head (one JSON line per case)")
     ap.add_argument("--kernel-gemv", default="",
                     help="profiling only: N,K,epilogue (store|residual|swiglu) -- time --steps launches of one "
                          "decode GEMV over 5 rotating weight sets and print one JSON line")
@@ -118,6 +121,229 @@ def run_gemv(args) -> int:
     print(json.dumps({"kernel": "qgemv_fx", "N": N, "K": K, "epilogue": mode, "us_per_launch": us,
                       "algorithmic_bytes": nbytes, "GB/s": nbytes / us / 1e3,
                       "device_error": L.load().sc_qgemv_device_error(1)}), flush=True)
+    return 0
+
+
+def _graph_time(fn, n_calls: int, reps: int, dev, sync=None) -> float:
+    """Mean device time (ms) of one call: `n_calls` calls captured in one CUDA
+    graph, replayed `reps` times between CUDA events on the replay stream
+    (`sync` lines the ranks up before the timed replays)."""
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(n_calls):  # warm-up: plans, lazy loads, collective rendezvous
+            fn(i)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for i in range(n_calls):
+            fn(i)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    if sync:
+        sync()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / (reps * n_calls)
+    del g
+    return ms
+
+
+def _peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def _setup_dist(local: int, world: int, rank: int):
+    import torch.distributed as dist
+
+    from shardcompute_b200.collectives import Communicator
+
+    torch.cuda.set_device(local)
+    comm = None
+    if world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300))
+        comm = Communicator(rank, world, backend="nccl")
+        comm.initialize_sync(timeout=300)
+    return comm
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sync(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def run_linear_sweep(args) -> int:
+    """cfg2: the isolated quantized linear, fp16 activations N(0,1) [M, 4096]
+    times 4- / 8-bit g64 weights N(0,0.02) [14336, 4096], column-parallel (N
+    split, no collective) and row-parallel (K split + all-reduce of the fp32
+    partial), M in {1, 4, 16, 256}.  Weight sets rotate so every call streams
+    from HBM (the sets together exceed 3x the L2).  One JSON line per case:
+    device time per call (max over ranks), algorithmic bytes (weights,
+    scales, biases, x in, y out) and FLOPs per rank, fractions of the
+    measured HBM and bf16 peaks."""
+    from shardcompute_b200 import ops
+
+    rank, world, local = dist_env()
+    comm = _setup_dist(local, world, rank)
+    dev = torch.device("cuda", local)
+    hbm, tf, kind = _peaks()
+    K, N = 4096, 14336
+    torch.manual_seed(0)
+    modes = ["column"] if world == 1 else ["column", "row"]
+    for bits in (4, 8):
+        for mode in modes:
+            n_r, k_r = (N // world, K) if mode == "column" else (N, K // world)
+            wbytes = n_r * k_r * bits // 8 + n_r * (k_r // args.group) * 4
+            nsets = max(2, min(48, -(-3 * 126 * 2 ** 20 // wbytes)))
+            sets = [ops.quantize((torch.randn(n_r, k_r, device=dev) * 0.02).half(), args.group, bits)
+                    for _ in range(nsets)]
+            for M in (1, 4, 16, 256):
+                x = torch.randn(M, k_r, device=dev).half()
+                y = torch.empty(M, n_r, device=dev, dtype=torch.float16 if mode == "column" else torch.float32)
+                red = torch.empty_like(y) if mode == "row" else None
+
+                def call(i, x=x, y=y, red=red):
+                    wq, sc, bi = sets[i % nsets]
+                    ops.qlinear(x, wq, sc, bi, args.group, bits, out=y)
+                    if red is not None:
+                        comm.allreduce_into(y, red)
+
+                ms = _max_over_ranks(_graph_time(call, nsets, max(4, args.steps // 8), dev, lambda: _sync(world)),
+                                     world)
+                nbytes = wbytes + M * k_r * 2 + M * n_r * y.element_size()
+                flops = 2 * M * n_r * k_r
+                gbs, tfs = nbytes / (ms / 1e3) / 1e9, flops / (ms / 1e3) / 1e12
+                if rank == 0:
+                    print(json.dumps({"workload": "cfg2", "mode": mode, "tp": world, "bits": bits, "group": args.group,
+                                      "M": M, "K": K, "N": N, "rank_shape": [n_r, k_r], "us_per_call": ms * 1e3,
+                                      "algorithmic_bytes": nbytes, "GB/s": gbs, "hbm_frac": gbs / hbm,
+                                      "TFLOP/s": tfs, "tensor_frac": tfs / tf, "peak_kind": kind,
+                                      "collective": "all-reduce of the fp32 partial [M, N]" if mode == "row" else None,
+                                      "weight_sets": nsets,
+                                      "kernel": "qgemv (decode GEMV)" if M <= 16 else "qgemm_tc (tcgen05)"}),
+                          flush=True)
+            del sets
+            torch.cuda.empty_cache()
+    if comm is not None:
+        comm.shutdown_sync()
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def zipf_ids(n: int, vocab: int, s: float, seed: int) -> torch.Tensor:
+    """n token ids with P(id = k) proportional to (k + 1)^-s over the vocabulary."""
+    import numpy as np
+
+    p = np.arange(1, vocab + 1, dtype=np.float64) ** -s
+    p /= p.sum()
+    return torch.from_numpy(np.random.default_rng(seed).choice(vocab, size=n, p=p).astype(np.int32))
+
+
+def run_embed_head(args) -> int:
+    """cfg4: vocab-parallel embedding + LM head, 4096 Zipf(1.1) token ids per
+    step: masked fp16 row gather from this rank's [V/TP, 4096] table (K3) +
+    all-reduce, then the rank's 4-bit g64 head [V/TP, 4096] over the 4096
+    gathered rows (tcgen05 dequant-GEMM, K2), per-row argmax of the rank's
+    logits, all-gather of (max, index) and the merge (distributed argmax).
+    Prints one JSON line: tokens/s and each part's device time."""
+    from shardcompute_b200 import _lib as L
+    from shardcompute_b200 import ops
+
+    rank, world, local = dist_env()
+    comm = _setup_dist(local, world, rank)
+    dev = torch.device("cuda", local)
+    hbm, tf, kind = _peaks()
+    V, H, T = 128256, 4096, 4096
+    Vl = V // world
+    v0 = rank * Vl
+    torch.manual_seed(rank)
+    table = (torch.randn(Vl, H, device=dev) * 0.02).half()
+    head = ops.quantize((torch.randn(Vl, H, device=dev) * 0.02).half(), args.group, args.bits)
+    ids = zipf_ids(T, V, 1.1, seed=3).to(dev)
+    h_part = torch.empty(T, H, device=dev)
+    h = torch.empty(T, H, device=dev)
+    logits = torch.empty(T, Vl, device=dev)
+    val = torch.empty(T, device=dev)
+    idx = torch.empty(T, dtype=torch.int32, device=dev)
+    gv = torch.empty(world, T, device=dev)
+    gi = torch.empty(world, T, dtype=torch.int32, device=dev)
+    tok = torch.empty(T, dtype=torch.int32, device=dev)
+
+    def gather(_):
+        L.call("sc_embed_gather_f16", ids.data_ptr(), T, table.data_ptr(), v0, v0 + Vl, H, h_part.data_ptr(),
+               L.SC_F32, ops.stream_handle(dev))
+        if comm is not None:
+            comm.allreduce_into(h_part, h)
+
+    def head_gemm(_):
+        ops.qlinear(h if comm is not None else h_part, *head, args.group, args.bits, out=logits)
+
+    def pick(_):
+        ops.argmax(logits, v0, val, idx)
+        if comm is not None:
+            comm.allgather_into(val, gv)
+            comm.allgather_into(idx, gi)
+        else:
+            gv[0].copy_(val)
+            gi[0].copy_(idx)
+        ops.argmax_merge(gv, gi, world, tok)
+
+    reps = max(4, args.steps // 8)
+    t_g = _max_over_ranks(_graph_time(gather, 4, reps, dev, lambda: _sync(world)), world)
+    t_h = _max_over_ranks(_graph_time(head_gemm, 2, reps, dev, lambda: _sync(world)), world)
+    t_p = _max_over_ranks(_graph_time(pick, 4, reps, dev, lambda: _sync(world)), world)
+
+    def step(i):
+        gather(i)
+        head_gemm(i)
+        pick(i)
+
+    t_s = _max_over_ranks(_graph_time(step, 2, reps, dev, lambda: _sync(world)), world)
+    in_range = int(((ids >= v0) & (ids < v0 + Vl)).sum())
+    g_bytes = in_range * H * 2 + T * H * 4 + T * 4  # rows read, fp32 rows written, ids
+    hw_bytes = Vl * H * args.bits // 8 + Vl * (H // args.group) * 4
+    flops = 2 * T * Vl * H
+    if rank == 0:
+        print(json.dumps({
+            "workload": "cfg4", "metric": "embedding + LM head tokens/s (4096 Zipf(1.1) ids per step)",
+            "value": T / (t_s / 1e3), "unit": "tok/s", "tp": world, "bits": args.bits, "group": args.group,
+            "ms_per_step": t_s, "parts_ms": {"gather+allreduce": t_g, "head_gemm": t_h, "argmax+gather+merge": t_p},
+            "gather": {"rows_in_range_rank0": in_range, "algorithmic_bytes": g_bytes,
+                       "GB/s_incl_allreduce": g_bytes / (t_g / 1e3) / 1e9},
+            "head": {"flops": flops, "TFLOP/s": flops / (t_h / 1e3) / 1e12,
+                     "tensor_frac": flops / (t_h / 1e3) / 1e12 / tf, "weight_bytes": hw_bytes, "peak_kind": kind,
+                     "kernel": "qgemm_tc (tcgen05, exact weights as fp16 hi + lo, x hi + lo: 3 MMAs per k-step)"},
+            "data": "synthetic (N(0,0.02) table and head, Zipf(1.1) ids, seed 3)"}), flush=True)
+    if comm is not None:
+        comm.shutdown_sync()
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
     return 0
 
 
@@ -283,6 +509,10 @@ def main():
         return run_reference(args, rank, world)
     if args.kernel_gemv:
         return run_gemv(args)
+    if args.workload == "cfg2":
+        return run_linear_sweep(args)
+    if args.workload == "cfg4":
+        return run_embed_head(args)
     if args.warmup < 3:
         print("--warmup must be >= 3", file=sys.stderr)
         return 2

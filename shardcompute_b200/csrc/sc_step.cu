@@ -57,10 +57,9 @@ constexpr int SP_BOX_CH = 4;                   // chunks per TMA box (two 32-wor
 constexpr int SP_BOX_K = SP_BOX_CH * SP_KPC;   // 512 k values per box
 constexpr int SP_WBOX = 16 * SP_BOX_CH * 64;   // packed-word bytes of a box: 16 rows x 4 chunks (4 KB)
 constexpr int SP_SBOX = 16 * 8 * 2;            // scale (or bias) bytes of a box: 16 rows x 8 groups
+constexpr int SP_UNIT = SP_WBOX + 2 * SP_SBOX;   // one unit of a weight image: words, scales, biases (4.5 KB)
 constexpr int SP_STAGE_BOXES = 6;              // 24 chunks of one set, or 12 chunk pairs of gate|up
-constexpr int SP_STAGE_BYTES = SP_STAGE_BOXES * (SP_WBOX + 2 * SP_SBOX);  // 27 KB
-constexpr int SP_STAGE_S = SP_STAGE_BOXES * SP_WBOX;                      // scales start
-constexpr int SP_STAGE_B = SP_STAGE_S + SP_STAGE_BOXES * SP_SBOX;         // biases start
+constexpr int SP_STAGE_BYTES = SP_STAGE_BOXES * SP_UNIT;  // 27 KB
 constexpr int SP_MAX_NST = 8;
 constexpr int SP_WIN = 8;                      // segments in flight per CTA (output slots)
 constexpr int SP_MAXT = 4;                     // segments per tile (CTAs a tile may be cut over)
@@ -82,7 +81,7 @@ struct StepOp {
   int nset;                  // 1, or 2 for the gate|up pair (row r of both)
   int nseg;                  // weight tensors stacked along N
   int seg_tiles[SP_MAX_SEG]; // tiles of each tensor
-  int map;                   // first tensor map: map + 3 * (seg or set) + {0 words, 1 scales, 2 biases}
+  const unsigned char* img;  // weight image: unit u, set a at (u * nset + a) * SP_UNIT
   int K, kq, tiles;          // reduction length, boxes per row, 16-row tiles
   int rows;                  // valid output rows
   long long total;           // tiles * kq
@@ -109,7 +108,6 @@ struct StepOp {
 struct StepParams {
   const StepOp* ops;
   int nops;
-  const CUtensorMap* maps;
   int* ctr;                  // counters
   int* gen;                  // completed steps (device)
   int* err;                  // error word
@@ -264,20 +262,15 @@ __device__ __forceinline__ uint64_t evict_first() {
   return pol;
 }
 
-__device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar,
-                                     uint64_t pol) {
+// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16, no
+// multicast) with an L2 eviction hint: streamed weights should not push the
+// KV cache and the activations out of L2.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
-      "[%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma2(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
-      "[%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(pol)
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 
@@ -496,14 +489,127 @@ struct StepShared {
   int cnt[SP_WIN];           // warps that flushed a segment into a slot
   int free_at[SP_WIN];       // first segment allowed into a slot
   float rinv;                // 1 / rms of the current GEMV's input
+  int attn_last;             // this CTA completed the current kv head's segments: it merges them
   int ndefer;                // row-op groups completed here, waiting for the peers' partials
   int defer[64];
 };
 
+// ---------------------------------------------------------------- GEMV segments
+
+// One CTA's share of a GEMV op: units [lo, hi) (tile rows t_first...), kq
+// units per tile row, nC CTAs in the split, the RMSNorm factor of the input.
+struct SegCtx {
+  long long lo, hi;
+  int t_first, kq, nC;
+  float rinv;
+};
+
+// Warps holding a piece of segment j (chunk p of the CTA's range goes to
+// warp p % SP_NCW; the segment's chunks are one contiguous run of them).
+__device__ __forceinline__ uint32_t seg_warps(const SegCtx& sc, int j) {
+  constexpr uint32_t FULL = (1u << SP_NCW) - 1u;
+  const long long tt = sc.t_first + j;
+  const long long a = (std::max(sc.lo, tt * sc.kq) - sc.lo) * SP_BOX_CH;
+  const long long b = (std::min(sc.hi, (tt + 1) * sc.kq) - sc.lo) * SP_BOX_CH;
+  if (b - a >= SP_NCW) return FULL;
+  const uint32_t m = ((1u << (int)(b - a)) - 1u) << (int)(a % SP_NCW);
+  return (m | (m >> SP_NCW)) & FULL;
+}
+
+// Epilogue of segment j, run by the warp that completed it: the warps'
+// partials summed in warp order, then the segment's partial to global memory
+// (or, for a tile held whole, straight into the LM-head argmax), and, when it
+// was the tile group's last segment, the group's finish.  Out of line: it
+// runs once per segment and keeps its registers out of the stream loop.
+__device__ __noinline__ void seg_epilogue(const StepParams& P, const StepOp& op, StepShared& S,
+                                          float (*s_slot)[2][16][SP_NCW], const SegCtx& sc, int j, int c, int gen,
+                                          int lane) {
+  const int slot = j % SP_WIN;
+  const int tile = sc.t_first + j;
+  const uint32_t msk = seg_warps(sc, j);
+  const int a = lane >> 4, row = lane & 15;
+  float v = 0.f;
+  if (a < op.nset) {
+#pragma unroll
+    for (int w = 0; w < SP_NCW; ++w)
+      if (msk & (1u << w)) v += s_slot[slot][a][row][w];
+    v *= sc.rinv;
+  }
+  __syncwarp();
+  if (lane == 0) {  // the slot is free for segment j + SP_WIN
+    S.cnt[slot] = 0;
+    __threadfence_block();
+    *reinterpret_cast<volatile int*>(&S.free_at[slot]) = j + SP_WIN;
+  }
+  const int nseg_t = tile_nseg(tile, sc.kq, op.total, sc.nC);
+  if (op.kind == SOP_HEAD && nseg_t == 1) {
+    // the whole tile is here: logits straight into this CTA's argmax candidate
+    unsigned long long k = 0ull;
+    const int r = tile * 16 + row;
+    if (a == 0 && r < op.rows) {
+      if (P.logits) P.logits[r] = v;
+      k = argmax_key(v, P.vocab_start + r);
+    }
+    k = warp_max_key(k);
+    if (lane == 0) atomicMax(&S.key, k);
+    return;
+  }
+  const int segslot = c - tile_first(tile, sc.kq, op.total, sc.nC);
+  if (a < op.nset) op.part[(((size_t)tile * SP_MAXT + segslot) * op.nset + a) * 16 + row] = v;
+  __syncwarp();
+  __threadfence();
+  if (op.kind == SOP_QKV) {
+    if (lane == 0) atomicAdd(P.ctr + op.grp_ctr, 1);
+    return;
+  }
+  if (op.kind == SOP_HEAD) {
+    int last = 0;
+    if (lane == 0) last = atomicAdd(P.ctr + op.grp_ctr + tile, 1) + 1 - (gen + 1) * nseg_t == 0;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    unsigned long long k = 0ull;
+    if (lane < 16) {
+      float s = 0.f;
+      for (int jj = 0; jj < nseg_t; ++jj) s += ldcg_f(op.part + ((size_t)tile * SP_MAXT + jj) * 16 + lane);
+      const int r = tile * 16 + lane;
+      if (r < op.rows) {
+        if (P.logits) P.logits[r] = s;
+        k = argmax_key(s, P.vocab_start + r);
+      }
+    }
+    k = warp_max_key(k);
+    if (lane == 0) atomicMax(&S.key, k);
+    return;
+  }
+  // O / DOWN / GATEUP: the group of four tiles
+  const int grp = tile >> 2;
+  int need = 0;
+  for (int tt = grp * 4; tt < grp * 4 + 4; ++tt) need += tile_nseg(tt, sc.kq, op.total, sc.nC);
+  int last = 0;
+  if (lane == 0) last = atomicAdd(P.ctr + op.grp_ctr + grp, 1) + 1 - (gen + 1) * need == 0;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  if (P.world > 1 && op.kind != SOP_GATEUP) {
+    // push this rank's sums now; receive after the stream (see push_group)
+    float v0, v1;
+    sum_rows(op, 0, grp * 64 + 2 * lane, sc.nC, v0, v1);
+    push_group(P, op.xchg, grp, v0, v1, lane, gen);
+    if (lane == 0) {
+      const int i = atomicAdd(&S.ndefer, 1);
+      if (i < 64) S.defer[i] = grp;
+      else raise_err(P, SPE_SLOT);
+    }
+    return;
+  }
+  finish_group(P, op, grp, lane, sc.nC, gen);
+}
+
 // ---------------------------------------------------------------- the kernel
 
 template <int G>
-__global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepParams P) {
+__global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const __grid_constant__ StepParams P) {
   extern __shared__ __align__(1024) unsigned char sp_smem[];
   __shared__ StepShared S;
   __shared__ __align__(16) uint4 s_zero[16];
@@ -589,7 +695,9 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
         // GEMV: this CTA's units, SP_STAGE_BOXES / nset per stage
         const int nC = gemv_ctas(op.total, n);
         const long long lo = c < nC ? range_lo(c, op.total, nC) : 0, hi = c < nC ? range_lo(c + 1, op.total, nC) : 0;
+        // one bulk copy per stage: the CTA's units are contiguous in the op's image
         const int qps = SP_STAGE_BOXES / op.nset;
+        const size_t ubytes = (size_t)op.nset * SP_UNIT;
         for (long long u0 = lo; u0 < hi && ok; u0 += qps) {
           int s;
           unsigned char* st = acquire(s);
@@ -597,24 +705,9 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
             ok = false;
             break;
           }
-          const int nu = (int)std::min<long long>(qps, hi - u0);
-          mbar_arrive_expect_tx(&S.full[s], (uint32_t)(nu * op.nset * (SP_WBOX + 2 * SP_SBOX)));
-          for (int j = 0; j < nu; ++j) {
-            const long long u = u0 + j;
-            const int t = (int)(u / op.kq), kb = (int)(u % op.kq);
-            int seg = 0, row0 = t * 16;
-            while (seg + 1 < op.nseg && row0 >= op.seg_tiles[seg] * 16) {
-              row0 -= op.seg_tiles[seg] * 16;
-              ++seg;
-            }
-            for (int a = 0; a < op.nset; ++a) {
-              const int b = j * op.nset + a;
-              const CUtensorMap* m = P.maps + op.map + 3 * (seg + a);
-              tma3(st + (size_t)b * SP_WBOX, m, 0, row0, kb * 2, &S.full[s], pol);
-              tma2(st + SP_STAGE_S + (size_t)b * SP_SBOX, m + 1, kb * 8, row0, &S.full[s], pol);
-              tma2(st + SP_STAGE_B + (size_t)b * SP_SBOX, m + 2, kb * 8, row0, &S.full[s], pol);
-            }
-          }
+          const uint32_t bytes = (uint32_t)(std::min<long long>(qps, hi - u0) * ubytes);
+          mbar_arrive_expect_tx(&S.full[s], bytes);
+          bulk_load_hint(st, op.img + (size_t)u0 * ubytes, bytes, &S.full[s], pol);
           ++it;
         }
       }
@@ -638,7 +731,14 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
   const uint32_t zero_x = smem_u32(s_zero);
   const uint32_t xbase = smem_u32(xs);
   const uint32_t rbase = smem_u32(ring);
-  uint32_t it = 0;  // ring position (the producer's sequence)
+  int rs = 0;        // ring slot of the next stage (the producer's sequence, modulo the ring)
+  uint32_t rph = 0;  // its mbarrier parity
+  auto ring_next = [&]() {
+    if (++rs == P.nst) {
+      rs = 0;
+      rph ^= 1u;
+    }
+  };
   volatile int* abort = &S.abort;
   if (!pos_ok) *abort = 1;
 
@@ -745,9 +845,9 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           for (int i = 0; i < 8; ++i) o[gq][i] = 0.f;
         }
         for (int kt = k0; kt < k1; kt += AK) {
-          const int s = (int)(it % (uint32_t)P.nst);
-          const uint32_t ph = (it / (uint32_t)P.nst) & 1u;
-          ++it;
+          const int s = rs;
+          const uint32_t ph = rph;
+          ring_next();
           if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort, oi)) {
             *abort = 1;
             __syncwarp();
@@ -864,38 +964,50 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
           }
         __threadfence();
         cbar();
-        // the last segment of head h merges the head and stages o_proj's input
-        if (warp == 0 && !wabort()) {
-          int last = 0;
-          if (lane == 0) last = atomicAdd(hctr + h, 1) + 1 == nsh;
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (last) {
-            __threadfence();
-            for (int gq = 0; gq < G; ++gq) {
-              float M = -INFINITY;
-              for (int j = lane; j < nsh; j += 32) M = fmaxf(M, ldcg_f(hp + ((size_t)j * G + gq) * (HD + 4)));
+        // the last segment of head h merges the head and stages o_proj's input:
+        // one warp per 64-value group, the segments' partials loaded 8 at a time
+        if (tid == 0) S.attn_last = !*abort && atomicAdd(hctr + h, 1) + 1 == nsh;
+        cbar();
+        if (S.attn_last) {
+          __threadfence();
+          for (int grp = warp; grp < G * (HD / 64); grp += SP_NCW) {
+            const int gq = grp / (HD / 64), gg = grp % (HD / 64);
+            const float* hg = hp + (size_t)gq * (HD + 4);
+            const size_t js = (size_t)G * (HD + 4);  // stride between segments
+            float M = -INFINITY;
+            for (int j = lane; j < nsh; j += 32) M = fmaxf(M, ldcg_f(hg + j * js));
 #pragma unroll
-              for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-              for (int gg = 0; gg < HD / 64; ++gg) {  // 64-value groups of o_proj's input
-                const int d = gg * 64 + 2 * lane;
-                float Ls = 0.f, O0 = 0.f, O1 = 0.f;
-                for (int j = 0; j < nsh; ++j) {
-                  const float* pj = hp + ((size_t)j * G + gq) * (HD + 4);
-                  const float mj = ldcg_f(pj);
-                  const float wgt = mj == -INFINITY ? 0.f : expf(mj - M);
-                  Ls = fmaf(ldcg_f(pj + 1), wgt, Ls);
-                  const float2 oo = __ldcg(reinterpret_cast<const float2*>(pj + 4 + d));
-                  O0 = fmaf(oo.x, wgt, O0);
-                  O1 = fmaf(oo.y, wgt, O1);
-                }
-                const float inv = 1.f / Ls;
-                stage_group(op.out_xs, nullptr, nullptr, ((h * G + gq) * HD + gg * 64) / 64, O0 * inv, O1 * inv,
-                            lane);
+            for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            float Ls = 0.f;
+            for (int j = lane; j < nsh; j += 32) {
+              const float mj = ldcg_f(hg + j * js);
+              Ls += mj == -INFINITY ? 0.f : ldcg_f(hg + j * js + 1) * expf(mj - M);
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, off);
+            const int d = gg * 64 + 2 * lane;
+            float O0 = 0.f, O1 = 0.f;
+            for (int j0 = 0; j0 < nsh; j0 += 8) {
+              float mj[8];
+              float2 oj[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const int j = std::min(j0 + q, nsh - 1);
+                mj[q] = ldcg_f(hg + j * js);
+                oj[q] = __ldcg(reinterpret_cast<const float2*>(hg + j * js + 4 + d));
+              }
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float wgt = (j0 + q >= nsh || mj[q] == -INFINITY) ? 0.f : expf(mj[q] - M);
+                O0 = fmaf(oj[q].x, wgt, O0);
+                O1 = fmaf(oj[q].y, wgt, O1);
               }
             }
+            const float inv = 1.f / Ls;
+            stage_group(op.out_xs, nullptr, nullptr, ((h * G + gq) * HD + gg * 64) / 64, O0 * inv, O1 * inv, lane);
             __syncwarp();
             __threadfence();
-            if (lane == 0) atomicAdd(P.ctr + op.out_ctr, G * HD / 64);
+            if (lane == 0) atomicAdd(P.ctr + op.out_ctr, 1);
           }
         }
         cbar();
@@ -938,105 +1050,16 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
       }
       cbar();
       const float rinv = S.rinv;
-      const int t_first = (int)(lo / op.kq);
-      const long long nch = (hi - lo) * SP_BOX_CH;  // chunks of this CTA
-
-      auto touched_mask = [&](int j) -> uint32_t {  // warps holding a piece of segment j
-        const int tt = t_first + j;
-        const long long a = (std::max(lo, (long long)tt * op.kq) - lo) * SP_BOX_CH;
-        const long long b = (std::min(hi, (long long)(tt + 1) * op.kq) - lo) * SP_BOX_CH;
-        if (b - a >= SP_NCW) return (1u << SP_NCW) - 1u;
-        uint32_t msk = 0;
-        for (long long p = a; p < b; ++p) msk |= 1u << (p % SP_NCW);
-        return msk;
-      };
-
-      // epilogue of segment j, run by the warp that completed it
-      auto seg_epilogue = [&](int j) {
-        const int slot = j % SP_WIN;
-        const int tile = t_first + j;
-        const uint32_t msk = touched_mask(j);
-        const int a = lane >> 4, row = lane & 15;
-        float v = 0.f;
-        if (a < op.nset) {
-#pragma unroll
-          for (int w = 0; w < SP_NCW; ++w)
-            if (msk & (1u << w)) v += s_slot[slot][a][row][w];
-          v *= rinv;
-        }
-        __syncwarp();
-        if (lane == 0) {  // the slot is free for segment j + SP_WIN
-          S.cnt[slot] = 0;
-          __threadfence_block();
-          *reinterpret_cast<volatile int*>(&S.free_at[slot]) = j + SP_WIN;
-        }
-        const int nseg_t = tile_nseg(tile, op.kq, op.total, nC);
-        if (op.kind == SOP_HEAD && nseg_t == 1) {
-          // the whole tile is here: logits straight into this CTA's argmax candidate
-          unsigned long long k = 0ull;
-          const int r = tile * 16 + row;
-          if (a == 0 && r < op.rows) {
-            if (P.logits) P.logits[r] = v;
-            k = argmax_key(v, P.vocab_start + r);
-          }
-          k = warp_max_key(k);
-          if (lane == 0) atomicMax(&S.key, k);
-          return;
-        }
-        const int segslot = c - tile_first(tile, op.kq, op.total, nC);
-        if (a < op.nset) op.part[(((size_t)tile * SP_MAXT + segslot) * op.nset + a) * 16 + row] = v;
-        __syncwarp();
-        __threadfence();
-        if (op.kind == SOP_QKV) {
-          if (lane == 0) atomicAdd(P.ctr + op.grp_ctr, 1);
-          return;
-        }
-        if (op.kind == SOP_HEAD) {
-          int last = 0;
-          if (lane == 0) last = atomicAdd(P.ctr + op.grp_ctr + tile, 1) + 1 - (gen + 1) * nseg_t == 0;
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (!last) return;
-          __threadfence();
-          unsigned long long k = 0ull;
-          if (lane < 16) {
-            float s = 0.f;
-            for (int jj = 0; jj < nseg_t; ++jj) s += ldcg_f(op.part + ((size_t)tile * SP_MAXT + jj) * 16 + lane);
-            const int r = tile * 16 + lane;
-            if (r < op.rows) {
-              if (P.logits) P.logits[r] = s;
-              k = argmax_key(s, P.vocab_start + r);
-            }
-          }
-          k = warp_max_key(k);
-          if (lane == 0) atomicMax(&S.key, k);
-          return;
-        }
-        // O / DOWN / GATEUP: the group of four tiles
-        const int grp = tile >> 2;
-        int need = 0;
-        for (int tt = grp * 4; tt < grp * 4 + 4; ++tt) need += tile_nseg(tt, op.kq, op.total, nC);
-        int last = 0;
-        if (lane == 0) last = atomicAdd(P.ctr + op.grp_ctr + grp, 1) + 1 - (gen + 1) * need == 0;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) return;
-        __threadfence();
-        if (P.world > 1 && op.kind != SOP_GATEUP) {
-          // push this rank's sums now; receive after the stream (see push_group)
-          float v0, v1;
-          sum_rows(op, 0, grp * 64 + 2 * lane, nC, v0, v1);
-          push_group(P, op.xchg, grp, v0, v1, lane, gen);
-          if (lane == 0) {
-            const int i = atomicAdd(&S.ndefer, 1);
-            if (i < 64) S.defer[i] = grp;
-            else raise_err(P, SPE_SLOT);
-          }
-          return;
-        }
-        finish_group(P, op, grp, lane, nC, gen);
-      };
+      const int kq = op.kq;
+      const int t_first = (int)(lo / kq);
+      const int lo_r = (int)(lo % kq);  // unit of the first chunk within its tile row
+      const int nchi = (int)((hi - lo) * SP_BOX_CH);  // chunks of this CTA
+      SegCtx sc{lo, hi, t_first, kq, nC, rinv};
 
       float acc[2][4];
       int cur = -1;  // this warp's current segment (tile - t_first)
+      // this warp's partial of segment j into its output slot; the last warp
+      // holding a piece of the segment runs the segment epilogue
       auto flush = [&](int j, int nset) {
         const int slot = j % SP_WIN;
         // the slot must have been released by segment j - SP_WIN's epilogue (lane 0 waits)
@@ -1067,37 +1090,44 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
         int last = 0;
         if (lane == 0) {
           __threadfence_block();
-          last = atomicAdd(&S.cnt[slot], 1) + 1 == __popc(touched_mask(j));
+          last = atomicAdd(&S.cnt[slot], 1) + 1 == __popc(seg_warps(sc, j));
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           __threadfence_block();
-          seg_epilogue(j);
+          seg_epilogue(P, op, S, s_slot, sc, j, c, gen, lane);
         }
       };
 
       // per-lane shared-memory offsets of chunk cc of box b
       auto wofs = [&](int b, int cc) -> uint32_t {
         const int uu = ((cc & 1) << 2) | t;
-        return (uint32_t)(b * SP_WBOX + (cc >> 1) * 2048 + pr0 * 128 + ((uu ^ (pr0 & 7)) << 4));
+        return (uint32_t)(b * SP_UNIT + (cc >> 1) * 2048 + pr0 * 128 + ((uu ^ (pr0 & 7)) << 4));
       };
-      auto sofs = [&](int b, int cc) -> uint32_t { return (uint32_t)(b * SP_SBOX + pr0 * 16 + cc * 4); };
+      auto sofs = [&](int b, int cc) -> uint32_t { return (uint32_t)(b * SP_UNIT + SP_WBOX + pr0 * 16 + cc * 4); };
 
       // The stream: NS weight sets; a warp takes chunk slots w (+ SP_NCW for
       // one set) of every stage, loads the ring's part of them into
-      // registers, releases the slot, then computes.
+      // registers, releases the slot, then computes.  Each slot's segment
+      // (tile row) and unit within the row advance by a stage's units per
+      // stage, tracked incrementally.
       auto run = [&](auto nset_tag) {
         constexpr int NS = decltype(nset_tag)::value;
         constexpr int NK = NS == 1 ? 2 : 1;              // chunk slots per warp per stage
         constexpr int QPS = SP_STAGE_BOXES / NS;         // units per stage
         constexpr int CPS = QPS * SP_BOX_CH;             // chunk slots per stage
         const int nstage = (int)((hi - lo + QPS - 1) / QPS);
-        const int lo_r = (int)(lo % op.kq);  // box of the first unit within its tile row
-        const int nchi = (int)nch;
+        int jk[NK], mk[NK];  // per slot: segment, unit within the tile row
+#pragma unroll
+        for (int k = 0; k < NK; ++k) {
+          const int ub = lo_r + (warp + SP_NCW * k) / SP_BOX_CH;
+          jk[k] = ub / kq;
+          mk[k] = ub - jk[k] * kq;
+        }
         for (int sidx = 0; sidx < nstage; ++sidx) {
-          const int s = (int)(it % (uint32_t)P.nst);
-          const uint32_t ph = (it / (uint32_t)P.nst) & 1u;
-          ++it;
+          const int s = rs;
+          const uint32_t ph = rph;
+          ring_next();
           if (wabort() || !mbar_wait_all(P, &S.full[s], ph, abort, oi)) {
             *abort = 1;
             __syncwarp();
@@ -1116,13 +1146,13 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
 #pragma unroll
               for (int a = 0; a < NS; ++a) {
                 const int b = bq * NS + a;
-                const uint32_t wo = st + wofs(b, cc), so = sofs(b, cc);
+                const uint32_t wo = st + wofs(b, cc), so = st + sofs(b, cc);
                 W0[k][a] = lds_v4(wo);
                 W1[k][a] = lds_v4(wo + 1024);
-                SB[k][a][0] = lds_u32(st + SP_STAGE_S + so);
-                SB[k][a][1] = lds_u32(st + SP_STAGE_S + so + 128);
-                SB[k][a][2] = lds_u32(st + SP_STAGE_B + so);
-                SB[k][a][3] = lds_u32(st + SP_STAGE_B + so + 128);
+                SB[k][a][0] = lds_u32(so);
+                SB[k][a][1] = lds_u32(so + 128);
+                SB[k][a][2] = lds_u32(so + SP_SBOX);
+                SB[k][a][3] = lds_u32(so + SP_SBOX + 128);
               }
             }
           }
@@ -1132,11 +1162,9 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
 #pragma unroll
           for (int k = 0; k < NK; ++k) {
             const int slotc = warp + SP_NCW * k;
-            const int pc = sidx * CPS + slotc;  // chunk position within this CTA's range
-            if (pc >= nchi) break;
-            const int ub = lo_r + pc / SP_BOX_CH;      // unit index from the first tile's start
-            const int j = ub / op.kq;                  // segment (tile - t_first)
-            const int kc = (ub % op.kq) * SP_BOX_CH + slotc % SP_BOX_CH;  // chunk along K
+            if (sidx * CPS + slotc >= nchi) break;
+            const int j = jk[k];                                    // segment (tile - t_first)
+            const int kc = mk[k] * SP_BOX_CH + (slotc % SP_BOX_CH);  // chunk along K
             if (j != cur) {
               if (cur >= 0) flush(cur, NS);
               cur = j;
@@ -1145,37 +1173,48 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const StepPa
 #pragma unroll
                 for (int r = 0; r < 4; ++r) acc[a][r] = 0.f;
             }
-            // this chunk's B fragments and column sums (the staged input stays put for the op)
-            uint32_t XB[4][4];
+            // this chunk's B fragments (one 16-byte unit per mma pair) and column sums
             const uint32_t xo = bact ? xbase + (uint32_t)kc * SP_CB + bx_off : zero_x;
-#pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-              const uint4 v = lds_v4(xo + (bact ? qq * 64 : 0));
-              XB[qq][0] = v.x;
-              XB[qq][1] = v.y;
-              XB[qq][2] = v.z;
-              XB[qq][3] = v.w;
-            }
             const float4 TB = lds_f4(xbase + (uint32_t)kc * SP_CB + 512 + t * 16);
+            float ca[NS][4], cz[NS][4];
 #pragma unroll
             for (int a = 0; a < NS; ++a) {
-              float ca[4] = {TB.x, TB.y, TB.x, TB.y}, cz[4] = {0.f, 0.f, 0.f, 0.f};
-              const uint32_t r0[4] = {W0[k][a].x, W0[k][a].y, W0[k][a].z, W0[k][a].w};
-              const uint32_t r1[4] = {W1[k][a].x, W1[k][a].y, W1[k][a].z, W1[k][a].w};
+              ca[a][0] = TB.x;
+              ca[a][1] = TB.y;
+              ca[a][2] = TB.x;
+              ca[a][3] = TB.y;
+              cz[a][0] = cz[a][1] = cz[a][2] = cz[a][3] = 0.f;
+            }
 #pragma unroll
-              for (int jw = 0; jw < 4; ++jw) {
-                const uint32_t w8a = r0[jw] >> 8, w8b = r1[jw] >> 8;
-                mma_16816(ca, mag<0x000F000Fu>(r0[jw]), mag<0x000F000Fu>(r1[jw]), mag<0x00F000F0u>(r0[jw]),
-                          mag<0x00F000F0u>(r1[jw]), XB[jw][0], XB[jw][1]);
-                mma_16816(cz, mag<0x000F000Fu>(w8a), mag<0x000F000Fu>(w8b), mag<0x00F000F0u>(w8a),
-                          mag<0x00F000F0u>(w8b), XB[jw][2], XB[jw][3]);
+            for (int jw = 0; jw < 4; ++jw) {
+              const uint4 xb = lds_v4(xo + (bact ? jw * 64 : 0));
+#pragma unroll
+              for (int a = 0; a < NS; ++a) {
+                const uint32_t r0 = jw == 0 ? W0[k][a].x : jw == 1 ? W0[k][a].y : jw == 2 ? W0[k][a].z : W0[k][a].w;
+                const uint32_t r1 = jw == 0 ? W1[k][a].x : jw == 1 ? W1[k][a].y : jw == 2 ? W1[k][a].z : W1[k][a].w;
+                const uint32_t w8a = r0 >> 8, w8b = r1 >> 8;
+                mma_16816(ca[a], mag<0x000F000Fu>(r0), mag<0x000F000Fu>(r1), mag<0x00F000F0u>(r0),
+                          mag<0x00F000F0u>(r1), xb.x, xb.y);
+                mma_16816(cz[a], mag<0x000F000Fu>(w8a), mag<0x000F000Fu>(w8b), mag<0x00F000F0u>(w8a),
+                          mag<0x00F000F0u>(w8b), xb.z, xb.w);
               }
+            }
+#pragma unroll
+            for (int a = 0; a < NS; ++a) {
               const __half2 s0 = u32_as_h2(SB[k][a][0]), s1 = u32_as_h2(SB[k][a][1]);
               const __half2 b0 = u32_as_h2(SB[k][a][2]), b1 = u32_as_h2(SB[k][a][3]);
-              acc[a][0] = fmaf(__low2float(s0), ca[0] + cz[0], fmaf(__low2float(b0), TB.z, acc[a][0]));
-              acc[a][1] = fmaf(__high2float(s0), ca[1] + cz[1], fmaf(__high2float(b0), TB.w, acc[a][1]));
-              acc[a][2] = fmaf(__low2float(s1), ca[2] + cz[2], fmaf(__low2float(b1), TB.z, acc[a][2]));
-              acc[a][3] = fmaf(__high2float(s1), ca[3] + cz[3], fmaf(__high2float(b1), TB.w, acc[a][3]));
+              acc[a][0] = fmaf(__low2float(s0), ca[a][0] + cz[a][0], fmaf(__low2float(b0), TB.z, acc[a][0]));
+              acc[a][1] = fmaf(__high2float(s0), ca[a][1] + cz[a][1], fmaf(__high2float(b0), TB.w, acc[a][1]));
+              acc[a][2] = fmaf(__low2float(s1), ca[a][2] + cz[a][2], fmaf(__low2float(b1), TB.z, acc[a][2]));
+              acc[a][3] = fmaf(__high2float(s1), ca[a][3] + cz[a][3], fmaf(__high2float(b1), TB.w, acc[a][3]));
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < NK; ++k) {
+            mk[k] += QPS;
+            while (mk[k] >= kq) {
+              mk[k] -= kq;
+              ++jk[k];
             }
           }
         }
@@ -1292,70 +1331,80 @@ struct StepPlan {
   int fit[6] = {};   // SMs, CTAs per SM, static smem, dynamic smem, registers, max threads per block
 };
 
-static PFN_cuTensorMapEncodeTiled_v12000 step_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+// ---------------------------------------------------------------- weight images
+//
+// Each GEMV op streams its weights from an image written once at finalize:
+// unit u (16 rows x 512 k of tile u / kq, block u % kq) of set a sits at
+// (u * nset + a) * SP_UNIT, holding the unit's packed words in the order the
+// consumers read them from shared memory (two 256-k halves of 16 rows x 128
+// bytes, the 16-byte pieces of row r permuted by XOR with r & 7 so the
+// fragment loads are bank-conflict free), then its 16 x 8 scales and 16 x 8
+// biases.  A CTA's run of units is one contiguous range, so a ring stage is
+// one bulk copy.  Rows past the tensor and k past K are zero (a zero scale
+// and bias contribute nothing).
+
+struct PackOp {
+  const uint32_t* w[SP_MAX_SEG];  // tensors stacked along N (q | k | v), or the gate, up pair
+  const uint16_t* s[SP_MAX_SEG];
+  const uint16_t* b[SP_MAX_SEG];
+  int rows[SP_MAX_SEG];
+  int seg_tiles[SP_MAX_SEG];
+  int nseg, nset, K, kq, tiles;
+  unsigned char* img;
+};
+
+__global__ void step_pack_kernel(const PackOp po) {
+  constexpr int P16 = SP_UNIT / 16;  // 16-byte pieces per unit
+  const long long n16 = (long long)po.tiles * po.kq * po.nset * P16;
+  const int KW = po.K / 8, KG = po.K / 64;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n16; i += (long long)gridDim.x * blockDim.x) {
+    const long long us = i / P16;
+    const int o16 = (int)(i % P16);
+    const long long u = us / po.nset;
+    const int a = (int)(us % po.nset);
+    const int t = (int)(u / po.kq), kb = (int)(u % po.kq);
+    int seg = 0, row0 = t * 16;
+    while (seg + 1 < po.nseg && row0 >= po.seg_tiles[seg] * 16) {
+      row0 -= po.seg_tiles[seg] * 16;
+      ++seg;
+    }
+    const int ti = po.nset == 2 ? a : seg;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (o16 < SP_WBOX / 16) {
+      const int zb = o16 >> 7, r = (o16 >> 3) & 15, piece = (o16 & 7) ^ (r & 7);
+      const int row = row0 + r, w0 = (kb * 2 + zb) * 32 + piece * 4;
+      if (row < po.rows[ti] && w0 < KW) v = *reinterpret_cast<const uint4*>(po.w[ti] + (size_t)row * KW + w0);
+    } else {
+      const int q = o16 - SP_WBOX / 16, r = q & 15;
+      const uint16_t* src = q >= 16 ? po.b[ti] : po.s[ti];
+      const int row = row0 + r;
+      uint32_t hw[4] = {0u, 0u, 0u, 0u};
+      if (row < po.rows[ti])
+        for (int g = 0; g < 8; ++g) {
+          const int gi = kb * 8 + g;
+          if (gi < KG) hw[g >> 1] |= (uint32_t)src[(size_t)row * KG + gi] << (16 * (g & 1));
+        }
+      v = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    }
+    reinterpret_cast<uint4*>(po.img)[i] = v;
   }
-  return fn;
 }
 
-// packed words of one weight tensor: (32 words, rows, K/256 blocks), box (32, 16, 2), 128-byte swizzle
-static bool step_wmap(CUtensorMap* m, const uint32_t* w, int rows, int K) {
-  auto fn = step_encode_fn();
-  if (!fn) return false;
-  const int KW = K / 8;
-  cuuint64_t dims[3] = {32, (cuuint64_t)rows, (cuuint64_t)(KW / 32)};
-  cuuint64_t strides[2] = {(cuuint64_t)KW * 4, 128};
-  cuuint32_t box[3] = {32, 16, 2}, es[3] = {1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint32_t*>(w), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// scales / biases with a row pitch of ld groups: (K/64 groups, rows), box (8, 16)
-static bool step_smap(CUtensorMap* m, const uint16_t* s, int rows, int K, int ld) {
-  auto fn = step_encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)(K / 64), (cuuint64_t)rows}, strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {8, 16}, es[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(s), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+static size_t image_bytes(int rows, int K, int nset) {
+  return (size_t)((rows + 15) / 16) * ((K + SP_BOX_K - 1) / SP_BOX_K) * nset * SP_UNIT;
 }
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 static int kq_of(int K) { return (K + SP_BOX_K - 1) / SP_BOX_K; }
 static int staged_bytes(int K) { return kq_of(K) * SP_BOX_CH * SP_CB; }
 
-// rows / K of the 7 linears of a layer: q, k, v, o, gate, up, down
-static void layer_shapes(const StepPlan& p, int rows[7], int ks[7]) {
-  const int r[7] = {p.Hq * p.hd, p.Hkv * p.hd, p.Hkv * p.hd, p.H, p.F, p.F, p.H};
-  const int k[7] = {p.H, p.H, p.H, p.Hq * p.hd, p.H, p.H, p.F};
-  for (int i = 0; i < 7; ++i) {
-    rows[i] = r[i];
-    ks[i] = k[i];
-  }
-}
-
-// Scales / biases whose rows are not a whole number of 16 bytes (K/64 not a
-// multiple of 8, e.g. down_proj at TP 8) cannot be described by a tensor
-// map; the plan keeps zero-padded copies of those with a 16-byte row pitch.
-static bool needs_pad(int K) { return (K / 64) % 8 != 0; }
-static int padded_ld(int K) { return (K / 64 + 7) / 8 * 8; }
-
 struct StepLayout {
-  size_t ops, maps, ctr, part_qkv, part_o, part_gu, part_down, part_head, attn_part, xs_h, xss_h, xs_o, xs_gu,
-      xss_gu, xs_down, h, pad, total;
-  size_t pad_layer;  // padded scale + bias bytes per layer
+  size_t ops, ctr, part_qkv, part_o, part_gu, part_down, part_head, attn_part, xs_h, xss_h, xs_o, xs_gu,
+      xss_gu, xs_down, h, img, total;
+  size_t img_layer;             // weight-image bytes of one layer
+  size_t img_off[4], img_head;  // q|k|v, o, gate|up, down within a layer; the head after the layers
   size_t progress;
-  int nctr, nops, nmaps, max_groups;
+  int nctr, nops, max_groups;
   int ctr_x, ctr_grp, ctr_head_tile, ctr_attn, ctr_misc;
   int xs_bytes_h, xs_bytes_o, xs_bytes_down;
 };
@@ -1364,7 +1413,6 @@ static StepLayout step_layout(const StepPlan& p) {
   StepLayout L{};
   const int nl = p.nl;
   L.nops = 1 + 5 * nl + 1;
-  L.nmaps = nl * 21 + 3;
   const int qkvN = (p.Hq + 2 * p.Hkv) * p.hd;
   const int G = p.Hq / p.Hkv;
   L.xs_bytes_h = staged_bytes(p.H);
@@ -1380,8 +1428,6 @@ static StepLayout step_layout(const StepPlan& p) {
   size_t o = 0;
   L.ops = o;
   o = align_up(o + sizeof(StepOp) * L.nops, 128);
-  L.maps = o;
-  o = align_up(o + sizeof(CUtensorMap) * L.nmaps, 128);
   L.ctr = o;
   o = align_up(o + sizeof(int) * L.nctr, 128);
   L.progress = o;
@@ -1415,13 +1461,14 @@ static StepLayout step_layout(const StepPlan& p) {
   o = align_up(o + L.xs_bytes_down, 128);
   L.h = o;
   o = align_up(o + sizeof(float) * p.H, 128);
-  int rows[7], ks[7];
-  layer_shapes(p, rows, ks);
-  L.pad_layer = 0;
-  for (int j = 0; j < 7; ++j)
-    if (needs_pad(ks[j])) L.pad_layer += 2 * align_up((size_t)rows[j] * padded_ld(ks[j]) * 2, 128);
-  L.pad = o;
-  o += L.pad_layer * nl;
+  L.img = o = align_up(o, 1024);
+  L.img_off[0] = 0;
+  L.img_off[1] = L.img_off[0] + image_bytes(qkvN, p.H, 1);
+  L.img_off[2] = L.img_off[1] + image_bytes(p.H, p.Hq * p.hd, 1);
+  L.img_off[3] = L.img_off[2] + image_bytes(p.F, p.H, 2);
+  L.img_layer = L.img_off[3] + image_bytes(p.H, p.F, 1);
+  L.img_head = L.img_layer * nl;
+  o += L.img_head + image_bytes(p.Vl, p.H, 1);
   L.total = align_up(o, 128);
   return L;
 }
@@ -1639,45 +1686,47 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
   const int n = p->nsm;
   const int H = p->H, hd = p->hd, Hq = p->Hq, Hkv = p->Hkv, F = p->F;
   const int qkvN = (Hq + 2 * Hkv) * hd;
-  cudaError_t e = cudaMemsetAsync(ws, 0, L.total, stream);
+  // everything but the weight images starts at zero (the images are written whole below)
+  cudaError_t e = cudaMemsetAsync(ws, 0, L.img, stream);
   SC_REQUIRE(e == cudaSuccess, SC_ERR_CUDA, "step_finalize: memset failed (%s)", cudaGetErrorString(e));
-  // ---- tensor maps (padded copies of the scales / biases that need them)
-  int rows[7], ks[7];
-  layer_shapes(*p, rows, ks);
-  std::vector<CUtensorMap> maps(L.nmaps);
-  for (int i = 0; i < p->nl; ++i) {
-    size_t po = L.pad + L.pad_layer * i;
-    for (int j = 0; j < 7; ++j) {
-      const StepLayer& ly = p->layers[i];
-      const uint16_t* sp = ly.s[j];
-      const uint16_t* bp = ly.b[j];
-      int ld = ks[j] / 64;
-      if (needs_pad(ks[j])) {
-        ld = padded_ld(ks[j]);
-        const size_t bytes = align_up((size_t)rows[j] * ld * 2, 128);
-        uint16_t* s2 = reinterpret_cast<uint16_t*>(ws + po);
-        uint16_t* b2 = reinterpret_cast<uint16_t*>(ws + po + bytes);
-        e = cudaMemcpy2DAsync(s2, (size_t)ld * 2, sp, (size_t)(ks[j] / 64) * 2, (size_t)(ks[j] / 64) * 2, rows[j],
-                              cudaMemcpyDeviceToDevice, stream);
-        if (e == cudaSuccess)
-          e = cudaMemcpy2DAsync(b2, (size_t)ld * 2, bp, (size_t)(ks[j] / 64) * 2, (size_t)(ks[j] / 64) * 2, rows[j],
-                                cudaMemcpyDeviceToDevice, stream);
-        SC_REQUIRE(e == cudaSuccess, SC_ERR_CUDA, "step_finalize: scale copy failed (%s)", cudaGetErrorString(e));
-        sp = s2;
-        bp = b2;
-        po += 2 * bytes;
-      }
-      const int mi = i * 21 + 3 * j;
-      SC_REQUIRE(step_wmap(&maps[mi], ly.w[j], rows[j], ks[j]) && step_smap(&maps[mi + 1], sp, rows[j], ks[j], ld) &&
-                     step_smap(&maps[mi + 2], bp, rows[j], ks[j], ld),
-                 SC_ERR_CUDA, "step_finalize: tensor map of layer %d weight %d refused", i, j);
+  // ---- weight images
+  auto pack = [&](unsigned char* img, int nseg, int nset, const uint32_t* const* w, const uint16_t* const* sc,
+                  const uint16_t* const* bi, const int* rws, int K) -> bool {
+    PackOp po{};
+    po.nseg = nseg;
+    po.nset = nset;
+    po.K = K;
+    po.kq = kq_of(K);
+    int total_rows = 0;
+    for (int j = 0; j < std::max(nseg, nset); ++j) {
+      po.w[j] = w[j];
+      po.s[j] = sc[j];
+      po.b[j] = bi[j];
+      po.rows[j] = rws[j];
+      po.seg_tiles[j] = (rws[j] + 15) / 16;
+      if (j < nseg) total_rows += po.seg_tiles[j] * 16;
     }
+    po.tiles = total_rows / 16;
+    po.img = img;
+    launch(step_pack_kernel, dim3(4 * n), dim3(256), 0, stream, po);
+    return cudaGetLastError() == cudaSuccess;
+  };
+  bool packed = true;
+  for (int i = 0; i < p->nl && packed; ++i) {
+    const StepLayer& ly = p->layers[i];
+    unsigned char* base = reinterpret_cast<unsigned char*>(ws + L.img + L.img_layer * i);
+    const int rq[3] = {Hq * hd, Hkv * hd, Hkv * hd}, ro[1] = {H}, rg[2] = {F, F}, rd[1] = {H};
+    packed = pack(base + L.img_off[0], 3, 1, ly.w, ly.s, ly.b, rq, H) &&
+             pack(base + L.img_off[1], 1, 1, ly.w + 3, ly.s + 3, ly.b + 3, ro, Hq * hd) &&
+             pack(base + L.img_off[2], 1, 2, ly.w + 4, ly.s + 4, ly.b + 4, rg, H) &&
+             pack(base + L.img_off[3], 1, 1, ly.w + 6, ly.s + 6, ly.b + 6, rd, F);
   }
-  SC_REQUIRE(!needs_pad(H), SC_ERR_UNSUPPORTED, "step_finalize: hidden size %d", H);
-  SC_REQUIRE(step_wmap(&maps[p->nl * 21], p->emb_w, p->Vl, H) &&
-                 step_smap(&maps[p->nl * 21 + 1], p->emb_s, p->Vl, H, H / 64) &&
-                 step_smap(&maps[p->nl * 21 + 2], p->emb_b, p->Vl, H, H / 64),
-             SC_ERR_CUDA, "step_finalize: tensor map of the embedding refused");
+  if (packed) {
+    const int rv[1] = {p->Vl};
+    packed = pack(reinterpret_cast<unsigned char*>(ws + L.img + L.img_head), 1, 1, &p->emb_w, &p->emb_s, &p->emb_b,
+                  rv, H);
+  }
+  SC_REQUIRE(packed, SC_ERR_CUDA, "step_finalize: weight image pack failed");
   // ---- ops
   std::vector<StepOp> ops;
   auto gemv = [&](int kind, int layer, int K, int nrows, int nset) {
@@ -1723,7 +1772,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
     q.seg_tiles[0] = Hq * hd / 16;
     q.seg_tiles[1] = Hkv * hd / 16;
     q.seg_tiles[2] = Hkv * hd / 16;
-    q.map = i * 21;
+    q.img = reinterpret_cast<const unsigned char*>(ws + L.img + L.img_layer * i + L.img_off[0]);
     q.xs = xs_h;
     q.xss = xss_h;
     q.x_ctr = L.ctr_x + oq;
@@ -1743,7 +1792,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
     ops.push_back(a);
     const int oo = (int)ops.size();
     StepOp o = gemv(SOP_O, i, Hq * hd, H, 1);
-    o.map = i * 21 + 9;
+    o.img = reinterpret_cast<const unsigned char*>(ws + L.img + L.img_layer * i + L.img_off[1]);
     o.xs = xs_o;
     o.x_ctr = L.ctr_x + oo;
     o.x_need = Hq * hd / 64;
@@ -1758,7 +1807,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
     ops.push_back(o);
     const int og = (int)ops.size();
     StepOp gu = gemv(SOP_GATEUP, i, H, F, 2);
-    gu.map = i * 21 + 12;
+    gu.img = reinterpret_cast<const unsigned char*>(ws + L.img + L.img_layer * i + L.img_off[2]);
     gu.xs = xs_gu;
     gu.xss = xss_gu;
     gu.x_ctr = L.ctr_x + og;
@@ -1770,7 +1819,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
     ops.push_back(gu);
     const int od = (int)ops.size();
     StepOp d = gemv(SOP_DOWN, i, F, H, 1);
-    d.map = i * 21 + 18;
+    d.img = reinterpret_cast<const unsigned char*>(ws + L.img + L.img_layer * i + L.img_off[3]);
     d.xs = xs_down;
     d.x_ctr = L.ctr_x + od;
     d.x_need = F / 64;
@@ -1788,7 +1837,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
   {
     const int oh = (int)ops.size();
     StepOp ho = gemv(SOP_HEAD, p->nl, H, p->Vl, 1);
-    ho.map = p->nl * 21;
+    ho.img = reinterpret_cast<const unsigned char*>(ws + L.img + L.img_head);
     ho.xs = xs_h;
     ho.xss = xss_h;
     ho.x_ctr = L.ctr_x + oh;
@@ -1836,15 +1885,12 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
   }
   // ---- upload
   e = cudaMemcpyAsync(ws + L.ops, ops.data(), sizeof(StepOp) * ops.size(), cudaMemcpyHostToDevice, stream);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(ws + L.maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   SC_REQUIRE(e == cudaSuccess, SC_ERR_CUDA, "step_finalize: upload failed (%s)", cudaGetErrorString(e));
   StepParams& P = p->P;
   P = StepParams{};
   P.ops = reinterpret_cast<const StepOp*>(ws + L.ops);
   P.nops = L.nops;
-  P.maps = reinterpret_cast<const CUtensorMap*>(ws + L.maps);
   int* ctr = reinterpret_cast<int*>(ws + L.ctr);
   P.ctr = ctr;
   P.attn_ctr = ctr + L.ctr_attn;

@@ -25,8 +25,8 @@ worker/executor.py:229-325), re-laid for B200:
   every GEMV and the cached keys / values stream through one shared-memory
   ring per SM without stopping at op boundaries, the row-parallel
   all-reduces run inside it over NVLink, and the last CTA writes the sampled
-  token.  ``SC_STEP=0`` (or any other batch / format) keeps the per-kernel
-  step above.
+  token.  Opt-in (``one_kernel_step=True`` or ``SC_STEP=1``, batch 1, 4-bit
+  g64); the per-kernel step above is the default.
 """
 
 from __future__ import annotations
@@ -60,7 +60,7 @@ class DecodeEngine:
 
     def __init__(self, weights: RankWeights, comm=None, max_batch: int = 1, max_seq: int = 2048,
                  device: Optional[torch.device] = None, attn_splits: Optional[int] = None,
-                 prefetch_mb: Optional[float] = None):
+                 prefetch_mb: Optional[float] = None, one_kernel_step: Optional[bool] = None):
         cfg: ModelConfig = weights.cfg
         self.cfg = cfg
         self.w = weights
@@ -108,11 +108,14 @@ class DecodeEngine:
         # decode scratch: fixed for the engine's lifetime (a captured graph keeps its address)
         self.workspace = torch.empty(self._workspace_bytes(self.B, 1), dtype=torch.uint8, device=dev)
         self._ws = self.workspace
-        # the persistent one-kernel decode step (built at the first decode step)
-        self.use_step = (self.B == 1 and self.bits == 4 and self.group == 64 and cfg.hidden_size % 512 == 0
-                         and (self.Hq * self.hd) % 512 == 0 and self.F % 256 == 0 and self.F >= 512
-                         and self.hd in (64, 128) and (self.Hq // self.Hkv) in (1, 2, 4, 8)
-                         and os.environ.get("SC_STEP", "1") != "0")
+        # the persistent one-kernel decode step (built at the first decode step);
+        # opt-in (argument, or SC_STEP=1): its GEMV consumers are slower than
+        # the per-kernel step's today
+        if one_kernel_step is None:
+            one_kernel_step = os.environ.get("SC_STEP", "0") == "1"
+        self.use_step = (one_kernel_step and self.B == 1 and self.bits == 4 and self.group == 64
+                         and cfg.hidden_size % 512 == 0 and (self.Hq * self.hd) % 512 == 0 and self.F % 256 == 0
+                         and self.F >= 512 and self.hd in (64, 128) and (self.Hq // self.Hkv) in (1, 2, 4, 8))
         self._step = None
         self._step_ws: Optional[torch.Tensor] = None
         self.step_trace: Optional[torch.Tensor] = None   # [L+1, H] hidden states of the last step (debug)

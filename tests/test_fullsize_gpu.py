@@ -29,21 +29,21 @@ HIDDEN_TOL = 1e-3
 AGREE = 0.99
 
 
-def _engine(shape, shard, max_batch, max_seq, dev, world=1, rank=0, comm=None):
+def _engine(shape, shard, max_batch, max_seq, dev, world=1, rank=0, comm=None, one_kernel=False):
     from shardcompute_b200.model.config import ModelConfig
     from shardcompute_b200.parallel.decode_engine import DecodeEngine
     from shardcompute_b200.parallel.weights import RankWeights
 
     cfg = ModelConfig.from_dict(synth.model_config_dict(shape))
     w = RankWeights.from_shard(cfg, shard, world, rank, shape.bits, shape.group_size, dev)
-    return DecodeEngine(w, comm, max_batch=max_batch, max_seq=max_seq, device=dev)
+    return DecodeEngine(w, comm, max_batch=max_batch, max_seq=max_seq, device=dev, one_kernel_step=one_kernel)
 
 
 def _layer_errors(hid_e, hid_r, B, S):
     return [rel_l2(e.view(B, S, -1), r) for e, r in zip(hid_e, hid_r)]
 
 
-def run_parity(shape, B, ctx, steps, dev, seed=0):
+def run_parity(shape, B, ctx, steps, dev, seed=0, one_kernel=False):
     """Prefill + one decode step (per-layer hidden states), then `steps`
     greedy steps teacher-forced through the production decode step (each
     step fed the reference's previous token from pinned host memory, the
@@ -55,7 +55,7 @@ def run_parity(shape, B, ctx, steps, dev, seed=0):
     later token."""
     torch.manual_seed(seed)
     ckpt = gpu_checkpoint(shape, seed, dev)
-    eng = _engine(shape, ckpt, B, ctx + 2 * steps + 8, dev)
+    eng = _engine(shape, ckpt, B, ctx + 2 * steps + 8, dev, one_kernel=one_kernel)
     ref = TorchRef([ckpt], shape, max_len=ctx + steps + 8, device=dev)
     prompt = torch.randint(0, shape.vocab_size, (B, ctx), generator=torch.Generator().manual_seed(2))
 
@@ -127,9 +127,12 @@ def _check(res, name):
     assert res["agree"] >= AGREE, msg + f"\n{res['tokens'][0, :24]}\n{res['ref_tokens'][0, :24]}"
 
 
-def test_cfg3_llama3_8b_32_layers_ctx2048(cuda):
+@pytest.mark.parametrize("one_kernel", [False, True])
+def test_cfg3_llama3_8b_32_layers_ctx2048(cuda, one_kernel):
     shape = LlamaShape(**LLAMA3_8B, bits=4, group_size=64)
-    _check(run_parity(shape, B=1, ctx=2048, steps=128, dev=cuda), "cfg3 b1 ctx2048")
+    res = run_parity(shape, B=1, ctx=2048, steps=128, dev=cuda, one_kernel=one_kernel)
+    assert bool(res["step_logits"]) == one_kernel
+    _check(res, f"cfg3 b1 ctx2048 {'one-kernel' if one_kernel else 'per-kernel'} step")
 
 
 @pytest.mark.parametrize("B", [8, 32])

@@ -138,7 +138,8 @@ def test_device_uniforms_follow_splitmix64(cuda):
     assert int(counter[0]) == 3
 
 
-def test_engine_sampled_generate(cuda):
+@pytest.mark.parametrize("one_kernel", [False, True])
+def test_engine_sampled_generate(cuda, one_kernel):
     from shardcompute_b200.model.config import ModelConfig
     from shardcompute_b200.parallel.decode_engine import DecodeEngine
     from shardcompute_b200.parallel.weights import RankWeights
@@ -147,7 +148,8 @@ def test_engine_sampled_generate(cuda):
     shard = osh.shard_weights(synth.checkpoint(shape, seed=4, std=0.05), 1, 0)
     cfg = ModelConfig.from_dict(synth.model_config_dict(shape))
     w = RankWeights.from_shard(cfg, shard, 1, 0, shape.bits, shape.group_size, cuda)
-    eng = DecodeEngine(w, None, max_batch=1, max_seq=96, device=cuda)
+    eng = DecodeEngine(w, None, max_batch=1, max_seq=96, device=cuda, one_kernel_step=one_kernel)
+    assert eng.use_step == one_kernel
     prompt = torch.from_numpy(np.random.default_rng(2).integers(0, shape.vocab_size, size=(1, 8))).to(cuda)
     greedy = eng.generate(prompt, 24).cpu().numpy()
     eng.set_sampling(1.0, 1e-6, seed=3)  # top_p -> 0 keeps only the most likely token: greedy

@@ -35,7 +35,7 @@ def _engine(shape, shard, max_seq, dev):
 
     cfg = ModelConfig.from_dict(synth.model_config_dict(shape))
     w = RankWeights.from_shard(cfg, shard, 1, 0, shape.bits, shape.group_size, dev)
-    return DecodeEngine(w, None, max_batch=1, max_seq=max_seq, device=dev)
+    return DecodeEngine(w, None, max_batch=1, max_seq=max_seq, device=dev, one_kernel_step=True)
 
 
 def _rel(a, b):
