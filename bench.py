@@ -555,8 +555,18 @@ def main():
     eng = DecodeEngine(weights, comm, max_batch=B, max_seq=args.ctx + n_replays + 16, device=dev)
     gen = torch.Generator().manual_seed(2)
     prompt = torch.randint(0, cfg.vocab_size, (B, args.ctx), generator=gen, dtype=torch.int64).to(torch.int32)
+    prompt_dev = prompt.to(dev)
+    # prefill (untimed for the decode metric): one warm-up, then one timed with CUDA events
     eng.reset()
-    eng.prefill(prompt.to(dev))
+    eng.prefill(prompt_dev)
+    torch.cuda.synchronize(dev)
+    eng.reset()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    eng.prefill(prompt_dev)
+    p1.record()
+    barrier()
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
     # one eager step: count this library's launches per step
     c0 = _lib.load().sc_launch_count()
     eng.decode_step()
@@ -659,7 +669,10 @@ def main():
                 "data": "synthetic (random-init N(0,0.02) weights, uniform random prompt ids)",
                 "config": workload_config(args, world), "clocks": clk, "e2e": e2e,
                 "gpu_launches": launches_per_step * args.steps, "roofline": roofline, "cpu_baseline": cpu,
-                "first_tokens": first}
+                "first_tokens": first,
+                "prefill": {"tokens": B * args.ctx, "ms": prefill_ms, "tok_per_s": B * args.ctx / (prefill_ms / 1e3),
+                            "note": "the prompt through every layer (tensor-core GEMM for more than 16 rows, "
+                                    "flash attention), CUDA events, after one warm-up prefill"}}
         print(json.dumps(line), flush=True)
     eng.graph = None
     eng._probe_graph = None

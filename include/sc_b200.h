@@ -76,10 +76,11 @@ unsigned long long sc_launch_count(void);
  * and the tied LM head matmul of parallel/transformer.py:565-569.
  *   x: fp16 or fp32 [M, ldx]; bias: fp16 [N] or NULL; y: fp16 or fp32 [M, ldy].
  *   bits in {4, 8}; group_size in {32, 64, 128}; K % group_size == 0.
- *   Any M >= 1.  Up to 4 rows (2 at 4-bit group 64) run the decode GEMV
- *   (exact weights); more rows run the tcgen05 tensor-core GEMM (sc_qgemm)
- *   when K % 64 == 0 and the workspace holds its scratch, else batched
- *   GEMV passes.  sc_qlinear_workspace_bytes covers every case.
+ *   Any M >= 1.  Up to 16 rows run passes of the decode GEMV (exact
+ *   weights; 4 rows per pass, 2 at 4-bit group 64, 1 at group 32); more
+ *   rows run the tcgen05 tensor-core GEMM (sc_qgemm) when K % 64 == 0 and
+ *   the workspace holds its scratch, else GEMV passes.
+ *   sc_qlinear_workspace_bytes covers every case.
  */
 size_t sc_qlinear_workspace_bytes(int M, int K, int N, int bits);
 int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx,
@@ -88,8 +89,8 @@ int sc_qlinear(const void* x, int x_dtype, int M, int K, int ldx,
                void* y, int y_dtype, int ldy,
                void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
-/* K2: the tensor-core dequant-GEMM behind sc_qlinear for more rows of x
- * (prefill, batched decode): tcgen05.mma kind::f16 with fp32 accumulators in
+/* K2: the tensor-core dequant-GEMM behind sc_qlinear for more than 16 rows
+ * of x (prefill, batched decode past batch 16): tcgen05.mma kind::f16 with fp32 accumulators in
  * TMEM; weights carried exactly as fp16 high + low parts, x likewise.  Same
  * arguments and epilogues as sc_qlinear_fused.  Replaces the prefill-shaped
  * mx.quantized_matmul calls (parallel/quantized_linear.py:168-176, 206-214,

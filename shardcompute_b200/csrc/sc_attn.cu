@@ -81,12 +81,12 @@ template <int HD, int G, typename OT>
 __global__ void __launch_bounds__(FD_WARPS * 32)
 flash_decode_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                     const int32_t* __restrict__ pos_ptr, int S, int Hq, int Hkv, int Lmax, float scale,
-                    int splits, float* __restrict__ part, OT* __restrict__ out) {
+                    int splits, float* __restrict__ part, OT* __restrict__ out, int tok0) {
   pdl_trigger();
   pdl_wait();
   constexpr int LPK = HD / 8;    // lanes per key
   constexpr int KPS = 32 / LPK;  // keys per warp step
-  const int split = blockIdx.x, kvh = blockIdx.y, tok = blockIdx.z;
+  const int split = blockIdx.x, kvh = blockIdx.y, tok = tok0 + (int)blockIdx.z;
   const int b = tok / S, s = tok % S;
   // keys visible to this query, never past the cache (a position beyond
   // Lmax was not appended by sc_rope_append either)
@@ -327,10 +327,11 @@ __device__ __forceinline__ void merge_partials_1r(const float* pbase, int splits
 }
 
 template <int HD, typename OT>
-__global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq, int splits, OT* __restrict__ out) {
+__global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq, int splits, OT* __restrict__ out,
+                                          int tok0) {
   pdl_trigger();
   pdl_wait();
-  const int qh = blockIdx.x, tok = blockIdx.y;
+  const int qh = blockIdx.x, tok = tok0 + (int)blockIdx.y;
   __shared__ float s_w[FD_MAX_SPLITS][1], s_l[FD_MAX_SPLITS][1], s_inv[1];
   merge_partials<HD, 1, HD, OT>(part + ((size_t)tok * Hq + qh) * splits * (HD + 2), HD + 2, 0, splits,
                                 out + (size_t)tok * Hq * HD + (size_t)qh * HD, s_w, s_l, s_inv);
@@ -339,13 +340,20 @@ __global__ void flash_decode_merge_kernel(const float* __restrict__ part, int Hq
 template <int HD, int G, typename OT>
 static int launch_fd(const float* q, const float* kc, const float* vc, const int32_t* pos, int B, int S, int Hq,
                      int Hkv, int Lmax, float scale, int splits, float* part, OT* out, cudaStream_t stream) {
-  dim3 grid(splits, Hkv, B * S);
-  ::sc::launch(flash_decode_kernel<HD, G, OT>, grid, FD_WARPS * 32, 0, stream, q, kc, vc, pos, S, Hq, Hkv, Lmax, scale, splits,
-                                                                    part, out);
-  int st = check_launch("flash_decode");
-  if (st != SC_OK || splits == 1) return st;
-  ::sc::launch(flash_decode_merge_kernel<HD, OT>, dim3(Hq, B * S), HD, 0, stream, part, Hq, splits, out);
-  return check_launch("flash_decode_merge");
+  // tokens go on the grid's y / z axes (at most 65535 each): launches of up to 32768 tokens
+  const int T = B * S;
+  for (int t0 = 0; t0 < T; t0 += 32768) {
+    const int nt = std::min(32768, T - t0);
+    ::sc::launch(flash_decode_kernel<HD, G, OT>, dim3(splits, Hkv, nt), FD_WARPS * 32, 0, stream, q, kc, vc, pos, S, Hq,
+                 Hkv, Lmax, scale, splits, part, out, t0);
+    int st = check_launch("flash_decode");
+    if (st != SC_OK) return st;
+    if (splits == 1) continue;
+    ::sc::launch(flash_decode_merge_kernel<HD, OT>, dim3(Hq, nt), HD, 0, stream, part, Hq, splits, out, t0);
+    st = check_launch("flash_decode_merge");
+    if (st != SC_OK) return st;
+  }
+  return SC_OK;
 }
 
 template <int HD, typename OT>

