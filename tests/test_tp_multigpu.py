@@ -1,6 +1,7 @@
 """Tensor parallelism across GPUs: TP=2, 4 and 8 decode against the float64
-oracle of the same sharded model, and cfg1 (TinyLlama shapes, 22 layers,
-TP2, a 128-token prompt, 128 greedy steps) against the float64 torch
+oracle of the same sharded model (and the one-kernel step at TP2), and cfg1
+(TinyLlama shapes, 22 layers, TP2, a 128-token prompt, 128 greedy steps
+teacher-forced through the captured step) against the float64 torch
 restatement of the oracle.
 
 One process per GPU, rendezvous on 127.0.0.1; skipped when fewer GPUs are
@@ -31,7 +32,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, one_kernel=False):
     try:
         sys.path.insert(0, ROOT)
         import torch
@@ -46,7 +47,8 @@ def _rank_main(rank, world, port, q):
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         # kv heads must divide by the world size (8 heads of 64 at world 8)
-        shape = (synth.tiny_shape(num_layers=2, num_heads=8, num_kv_heads=4) if world <= 4 else
+        # (the one-kernel step needs 512 q dims per rank: the wider shape at world 2)
+        shape = (synth.tiny_shape(num_layers=2, num_heads=8, num_kv_heads=4) if world <= 4 and not one_kernel else
                  synth.tiny_shape(num_layers=2, hidden_size=1024, num_heads=16, num_kv_heads=8,
                                   intermediate_size=2048))
         full = synth.checkpoint(shape, seed=13)
@@ -55,7 +57,8 @@ def _rank_main(rank, world, port, q):
         comm.initialize_sync(timeout=60)
         cfg = ModelConfig.from_dict(synth.model_config_dict(shape))
         w = RankWeights.from_shard(cfg, shards[rank], world, rank, shape.bits, shape.group_size, dev)
-        eng = DecodeEngine(w, comm, max_batch=1, max_seq=64, device=dev)
+        eng = DecodeEngine(w, comm, max_batch=1, max_seq=64, device=dev, one_kernel_step=one_kernel)
+        assert eng.use_step == one_kernel
         prompt = np.random.default_rng(3).integers(0, shape.vocab_size, size=(1, 7))
         logits = eng.forward_logits(torch.from_numpy(prompt).to(dev)).double().cpu().numpy()
         ref_logits = TPModel(shards, shape, max_len=64).forward(prompt)
@@ -65,12 +68,18 @@ def _rank_main(rank, world, port, q):
         ref_toks = TPModel(shards, shape, max_len=64).generate(prompt, 16)
         agree = float(np.mean(toks == ref_toks))
         assert agree >= 0.99, f"rank {rank}: greedy agreement {agree:.2f}"
+        if one_kernel:
+            assert eng.step_error() == 0, eng.step_error_info()
         eng.graph = None
         torch.cuda.synchronize()
         comm.shutdown_sync()
         q.put((rank, "ok", toks.tolist()))
     except BaseException:  # noqa: BLE001 - report to the parent
         q.put((rank, traceback.format_exc(), None))
+
+
+def _rank_main_one_kernel(rank, world, port, q):
+    _rank_main(rank, world, port, q, one_kernel=True)
 
 
 def _cfg1_rank_main(rank, world, port, q):
@@ -109,9 +118,21 @@ def _cfg1_rank_main(rank, world, port, q):
             toks.append(ref.forward(toks[-1][:, None])[:, -1].argmax(-1))
         ref_tok = torch.stack(toks, dim=1).cpu().numpy()
         del ref
-        out = eng.generate(prompt.to(dev), steps).cpu().numpy()
+        # teacher-forced through the production step (every rank feeds the same
+        # reference token from host memory, replays its graph, reads its argmax)
+        eng.reset()
+        eng.prefill(prompt.to(dev))
+        out = np.zeros_like(ref_tok)
+        out[:, 0] = eng.tok[:1].cpu().numpy()
+        hin = torch.zeros(1, dtype=torch.int32).pin_memory()
+        hout = torch.zeros(1, dtype=torch.int32).pin_memory()
+        for t in range(1, steps):
+            hin[0] = int(ref_tok[0, t - 1])
+            eng.decode_host(hin, hout)
+            out[0, t] = int(hout[0])
+        comm.check_health()
         agree = float(np.mean(out == ref_tok))
-        assert agree >= 0.99, f"rank {rank}: cfg1 greedy agreement {agree:.3f}"
+        assert agree >= 0.99, f"rank {rank}: cfg1 teacher-forced greedy agreement {agree:.3f}"
         eng.graph = None
         torch.cuda.synchronize()
         comm.shutdown_sync()
@@ -147,6 +168,12 @@ def _spawn(target, world):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_decode_matches_oracle(world):
     _spawn(_rank_main, world)
+
+
+def test_tp2_one_kernel_step_matches_oracle():
+    """The persistent one-kernel step with its in-kernel NVLink exchange (row
+    sums and the argmax) at TP2."""
+    _spawn(_rank_main_one_kernel, 2)
 
 
 def test_cfg1_tinyllama_tp2_128_steps():
