@@ -46,7 +46,7 @@ enum sc_status {
   SC_ERR_WORKSPACE = 7    /* ValueError: workspace too small */
 };
 
-enum sc_dtype { SC_F16 = 0, SC_F32 = 1, SC_I32 = 2 };
+enum sc_dtype { SC_F16 = 0, SC_F32 = 1, SC_I32 = 2, SC_U8 = 3 };  /* SC_U8: raw bytes (send / recv / broadcast) */
 
 /* Epilogues of the fused quantized linear. */
 enum sc_epilogue {
@@ -286,6 +286,11 @@ int sc_allgather(const void* send, void* recv, size_t count_per_rank, int dtype,
                  cudaStream_t stream);
 int sc_broadcast(const void* send, void* recv, size_t count, int dtype, int root, void* comm,
                  cudaStream_t stream);
+/* Point-to-point (Communicator.send / recv, collectives/communicator.py:520-561,
+ * and the pipeline stage transfers of worker/executor.py:376-479): a rank's
+ * sc_send to `peer` matches that peer's sc_recv of the same count and dtype. */
+int sc_send(const void* buf, size_t count, int dtype, int peer, void* comm, cudaStream_t stream);
+int sc_recv(void* buf, size_t count, int dtype, int peer, void* comm, cudaStream_t stream);
 
 /* ------------------------------------------------------ NVLink peer memory --
  * One-shot all-reduce / all-gather through peer memory for the small

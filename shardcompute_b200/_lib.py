@@ -19,7 +19,7 @@ import threading
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libsc_b200.so")
 
 SC_OK, SC_ERR_SHAPE, SC_ERR_CUDA, SC_ERR_NCCL, SC_ERR_TIMEOUT, SC_ERR_ARG, SC_ERR_UNSUPPORTED, SC_ERR_WORKSPACE = range(8)
-SC_F16, SC_F32, SC_I32 = 0, 1, 2
+SC_F16, SC_F32, SC_I32, SC_U8 = 0, 1, 2, 3
 SC_EPI_STORE, SC_EPI_RESIDUAL, SC_EPI_SWIGLU = 0, 1, 2
 SC_OP_SUM, SC_OP_MAX, SC_OP_MIN, SC_OP_AVG = 0, 1, 2, 3
 ABI_VERSION = 1
@@ -67,6 +67,8 @@ SIGNATURES = {
     "sc_allreduce": (_i, [_vp, _vp, _sz, _i, _i, _vp, _vp]),
     "sc_allgather": (_i, [_vp, _vp, _sz, _i, _vp, _vp]),
     "sc_broadcast": (_i, [_vp, _vp, _sz, _i, _i, _vp, _vp]),
+    "sc_send": (_i, [_vp, _sz, _i, _i, _vp, _vp]),
+    "sc_recv": (_i, [_vp, _sz, _i, _i, _vp, _vp]),
     "sc_p2p_handle_bytes": (_sz, []),
     "sc_p2p_create": (_i, [_i, _i, _sz, _pp, _vp, _sz]),
     "sc_p2p_open": (_i, [_vp, _vp, _sz]),

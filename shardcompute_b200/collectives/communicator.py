@@ -432,18 +432,62 @@ class Communicator:
         if dev.type == "cuda":
             torch.cuda.current_stream(dev).synchronize()
 
+    def _nccl_p2p(self, tensor: Optional[torch.Tensor] = None) -> bool:
+        return (self.backend != "gloo" and self._comm is not None and
+                (tensor is None or tensor.device.type == "cuda"))
+
+    def send_into(self, tensor: torch.Tensor, dest: int) -> None:
+        """Enqueue a send of ``tensor``'s bytes to ``dest`` on the current
+        stream (NCCL; graph-capturable).  ``dest`` must post a matching
+        ``recv_into`` of the same byte count."""
+        self._require()
+        if dest == self.rank or not 0 <= dest < self.world_size:
+            raise ValueError(f"Invalid destination rank: {dest}")
+        if not self._nccl_p2p(tensor):
+            raise RuntimeError("send_into needs the NCCL backend and a CUDA tensor")
+        from .. import _lib as L
+
+        t = tensor.contiguous()
+        L.call("sc_send", t.data_ptr(), t.numel() * t.element_size(), L.SC_U8, dest, self._comm,
+               torch.cuda.current_stream(t.device).cuda_stream)
+        self.stats.total_bytes_sent += t.numel() * t.element_size()
+
+    def recv_into(self, tensor: torch.Tensor, source: int) -> torch.Tensor:
+        """Enqueue a receive from ``source`` into ``tensor`` (contiguous, the
+        sender's byte count) on the current stream (NCCL; graph-capturable)."""
+        self._require()
+        if source == self.rank or not 0 <= source < self.world_size:
+            raise ValueError(f"Invalid source rank: {source}")
+        if not self._nccl_p2p(tensor) or not tensor.is_contiguous():
+            raise RuntimeError("recv_into needs the NCCL backend and a contiguous CUDA tensor")
+        from .. import _lib as L
+
+        L.call("sc_recv", tensor.data_ptr(), tensor.numel() * tensor.element_size(), L.SC_U8, source, self._comm,
+               torch.cuda.current_stream(tensor.device).cuda_stream)
+        self.stats.total_bytes_received += tensor.numel() * tensor.element_size()
+        return tensor
+
     async def send(self, tensor: torch.Tensor, dest: int):
-        """Point-to-point send of a small tensor through the store (control plane)."""
+        """Point-to-point send (collectives/communicator.py:520-541).  CUDA
+        tensors on the NCCL backend: the shape and dtype go through the store,
+        the bytes through NCCL on the current stream.  Otherwise the whole
+        tensor goes through the store (control plane, CPU tests)."""
         self._require()
         if dest == self.rank or not 0 <= dest < self.world_size:
             raise ValueError(f"Invalid destination rank: {dest}")
         n = self._p2p_counter.get((self.rank, dest), 0) + 1
         self._p2p_counter[(self.rank, dest)] = n
         key = f"shardcompute_b200/p2p/{self.rank}->{dest}/{n}"
+        if self._nccl_p2p(tensor):
+            self._store.set(key, pickle.dumps((tuple(tensor.shape), str(tensor.dtype), None)))
+            self.send_into(tensor, dest)
+            return
         self._store.set(key, pickle.dumps((tuple(tensor.shape), str(tensor.dtype),
                                            tensor.detach().cpu().contiguous().numpy().tobytes())))
 
     async def recv(self, source: int) -> torch.Tensor:
+        """Point-to-point receive of the next tensor ``source`` sent to this
+        rank (collectives/communicator.py:543-561)."""
         self._require()
         if source == self.rank or not 0 <= source < self.world_size:
             raise ValueError(f"Invalid source rank: {source}")
@@ -454,6 +498,9 @@ class Communicator:
         key = f"shardcompute_b200/p2p/{source}->{self.rank}/{n}"
         self._store.wait([key], datetime.timedelta(seconds=60))
         shape, dt, raw = pickle.loads(self._store.get(key))
+        if raw is None:  # the bytes travel through NCCL
+            t = torch.empty(shape, dtype=getattr(torch, dt.split(".")[-1]), device=self._device())
+            return self.recv_into(t, source)
         t = torch.from_numpy(np.frombuffer(bytearray(raw), dtype=_np_dtype(dt)).reshape(shape).copy())
         return t.to(self._device())
 

@@ -25,6 +25,7 @@ static ncclDataType_t nccl_type(int dt, bool* ok) {
     case SC_F16: return ncclFloat16;
     case SC_F32: return ncclFloat32;
     case SC_I32: return ncclInt32;
+    case SC_U8: return ncclUint8;
   }
   *ok = false;
   return ncclFloat32;
@@ -128,6 +129,27 @@ int sc_broadcast(const void* send, void* recv, size_t count, int dtype, int root
   if (count == 0) return SC_OK;
   return sc::nccl_status(ncclBroadcast(send, recv, count, t, root, static_cast<sc::Comm*>(comm)->nccl, stream),
                          "ncclBroadcast");
+}
+
+// Point-to-point: one rank's send matches the peer's recv of the same count
+// and dtype (Communicator.send / recv, collectives/communicator.py:520-561;
+// the pipeline stage transfers of worker/executor.py:376-479).
+int sc_send(const void* buf, size_t count, int dtype, int peer, void* comm, cudaStream_t stream) {
+  SC_REQUIRE(comm && buf, SC_ERR_ARG, "send: null pointer");
+  bool ok;
+  const ncclDataType_t t = sc::nccl_type(dtype, &ok);
+  SC_REQUIRE(ok, SC_ERR_ARG, "send: dtype %d", dtype);
+  if (count == 0) return SC_OK;
+  return sc::nccl_status(ncclSend(buf, count, t, peer, static_cast<sc::Comm*>(comm)->nccl, stream), "ncclSend");
+}
+
+int sc_recv(void* buf, size_t count, int dtype, int peer, void* comm, cudaStream_t stream) {
+  SC_REQUIRE(comm && buf, SC_ERR_ARG, "recv: null pointer");
+  bool ok;
+  const ncclDataType_t t = sc::nccl_type(dtype, &ok);
+  SC_REQUIRE(ok, SC_ERR_ARG, "recv: dtype %d", dtype);
+  if (count == 0) return SC_OK;
+  return sc::nccl_status(ncclRecv(buf, count, t, peer, static_cast<sc::Comm*>(comm)->nccl, stream), "ncclRecv");
 }
 
 }  // extern "C"

@@ -108,10 +108,10 @@ class RankWeights:
             s = shard[f"{prefix}.scales"]
             b = shard[f"{prefix}.biases"]
             if row_parallel:
-                local_groups = np.shape(w)[1] * pf // group
-                if np.shape(s)[1] == local_groups * world and world > 1:
+                local_groups = tuple(w.shape)[1] * pf // group
+                if tuple(s.shape)[1] == local_groups * world and world > 1:
                     sl = slice(rank * local_groups, (rank + 1) * local_groups)
-                    s, b = np.asarray(s)[:, sl], np.asarray(b)[:, sl]
+                    s, b = s[:, sl], b[:, sl]
             return _dev_words(w, device), _dev_f16(s, device), _dev_f16(b, device)
 
         layers = []
@@ -127,6 +127,16 @@ class RankWeights:
         return cls(cfg=cfg, world=world, rank=rank, bits=bits, group=group,
                    embed=tri("model.embed_tokens"), norm=_dev_f16(shard["model.norm.weight"], device),
                    layers=layers)
+
+    @classmethod
+    def from_safetensors(cls, cfg: ModelConfig, shard_dir: str, world: int, rank: int, bits: int, group: int,
+                         device: torch.device) -> "RankWeights":
+        """Load ``shard_dir/rank_{rank}/model.safetensors`` straight into one
+        device allocation (``model.loader.load_rank_shard``) and build the
+        rank's weights from those views (no host copy of any tensor)."""
+        from ..model.loader import load_rank_shard
+
+        return cls.from_shard(cfg, load_rank_shard(shard_dir, rank, device), world, rank, bits, group, device)
 
     @classmethod
     def synthetic(cls, cfg: ModelConfig, world: int, rank: int, bits: int = 4, group: int = 64,

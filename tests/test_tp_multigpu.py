@@ -141,6 +141,88 @@ def _cfg1_rank_main(rank, world, port, q):
         q.put((rank, traceback.format_exc(), None))
 
 
+def _pp_rank_main(rank, world, port, q):
+    """NCCL point-to-point: Communicator.send / recv of CUDA tensors (shape
+    and dtype through the store), then a two-stage pipeline transfer as the
+    reference's PipelineExecutor does it (worker/executor.py:376-479): stage
+    0 computes a hidden state and sends it, stage 1 runs its part and sends
+    the result back to stage 0 -- once eagerly and once as a captured graph
+    of send_into / recv_into, replayed."""
+    try:
+        sys.path.insert(0, ROOT)
+        import asyncio
+
+        import torch
+
+        from oracle import mlx_affine as qa
+        from shardcompute_b200 import ops
+        from shardcompute_b200.collectives import Communicator
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        comm = Communicator(rank, world, host="127.0.0.1", port=port, backend="nccl")
+        comm.initialize_sync(timeout=60)
+        loop = asyncio.new_event_loop()
+        # every rank draws the same inputs
+        g = torch.Generator().manual_seed(5)
+        a = torch.randn(3, 5, generator=g)
+        b = torch.randint(-9, 9, (7,), generator=g, dtype=torch.int64)
+        if rank == 0:
+            loop.run_until_complete(comm.send(a.to(dev), dest=1))
+            loop.run_until_complete(comm.send(b.to(dev), dest=1))
+            back = loop.run_until_complete(comm.recv(source=1))
+            assert torch.equal(back.cpu(), a * 2), "round trip"
+        else:
+            ra = loop.run_until_complete(comm.recv(source=0))
+            rb = loop.run_until_complete(comm.recv(source=0))
+            assert ra.dtype == torch.float32 and ra.shape == (3, 5) and torch.equal(ra.cpu(), a)
+            assert rb.dtype == torch.int64 and torch.equal(rb.cpu(), b)
+            loop.run_until_complete(comm.send(ra * 2, dest=0))
+        torch.cuda.synchronize()
+        # two stages of quantized linears; stage 1 returns its output to stage 0
+        rng = np.random.default_rng(8)
+        K, N1, N2, group = 256, 192, 64, 64
+        w1 = qa.quantize((rng.standard_normal((N1, K)) * 0.05).astype(np.float16), group, 4)
+        w2 = qa.quantize((rng.standard_normal((N2, N1)) * 0.05).astype(np.float16), group, 4)
+        x = torch.from_numpy(rng.standard_normal((2, K)).astype(np.float32)).to(dev)
+        dw = lambda t: [torch.from_numpy(np.ascontiguousarray(v.view(np.int32) if v.dtype == np.uint32 else v)).to(dev)
+                        for v in t]
+        W1, W2 = dw(w1), dw(w2)
+        h = torch.zeros(2, N1, device=dev)
+        y = torch.zeros(2, N2, device=dev)
+
+        def step():
+            if rank == 0:
+                ops.qlinear(x, *W1, group, 4, out=h)
+                comm.send_into(h, 1)
+                comm.recv_into(y, 1)
+            else:
+                comm.recv_into(h, 0)
+                ops.qlinear(h, *W2, group, 4, out=y)
+                comm.send_into(y, 0)
+
+        step()
+        torch.cuda.synchronize()
+        ref = qa.quantized_matmul(qa.quantized_matmul(x.cpu().numpy(), *w1, group, 4).astype(np.float32), *w2,
+                                  group, 4)
+        assert np.linalg.norm(y.cpu().numpy() - ref) / np.linalg.norm(ref) <= 1e-3
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+        y.zero_()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        assert np.linalg.norm(y.cpu().numpy() - ref) / np.linalg.norm(ref) <= 1e-3
+        del graph
+        comm.shutdown_sync()
+        q.put((rank, "ok", y.cpu().numpy().round(4).tolist()))
+    except BaseException:  # noqa: BLE001 - report to the parent
+        q.put((rank, traceback.format_exc(), None))
+
+
 def _spawn(target, world):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -174,6 +256,10 @@ def test_tp2_one_kernel_step_matches_oracle():
     """The persistent one-kernel step with its in-kernel NVLink exchange (row
     sums and the argmax) at TP2."""
     _spawn(_rank_main_one_kernel, 2)
+
+
+def test_nccl_send_recv_and_pipeline_stage_transfer():
+    _spawn(_pp_rank_main, 2)
 
 
 def test_cfg1_tinyllama_tp2_128_steps():
