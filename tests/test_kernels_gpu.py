@@ -123,7 +123,7 @@ def test_qlinear_fused_segments_norm_residual(cuda, rng, bits, rows):
     ref = np.concatenate([ref16(xn64, *sg, group, bits) for sg in segs], axis=1)
     ref_x = np.concatenate([ref_exact(xn64, *sg, group, bits) for sg in segs], axis=1)
     # x is normalised in fp32 and carried as fp16 high + low parts
-    assert_kernel_close(y, [ref, ref_x], 2e-5)
+    assert_kernel_close(y, [ref, ref_x], 5e-5)
     # residual epilogue, in place
     for K2 in (256, 4096):
         wq, s, b = make_q(rng, K, K2, bits, group)
@@ -133,7 +133,7 @@ def test_qlinear_fused_segments_norm_residual(cuda, rng, bits, rows):
         ops.qlinear_fused(to_dev(x, cuda), [(to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda))], group, bits,
                           epilogue=L.SC_EPI_RESIDUAL, residual=r_dev, out=r_dev)
         assert_kernel_close(r_dev.cpu().numpy(), [res + ref16(x, wq, s, b, group, bits),
-                                                  res + ref_exact(x, wq, s, b, group, bits)], 2e-5)
+                                                  res + ref_exact(x, wq, s, b, group, bits)], 5e-5)
 
 
 @pytest.mark.parametrize("M", [1, 4, 12])
@@ -146,17 +146,18 @@ def test_qlinear_swiglu(cuda, rng, M, K, F):
     y = ops.qlinear_fused(to_dev(x, cuda), [tuple(to_dev(a, cuda) for a in g), tuple(to_dev(a, cuda) for a in u)],
                           group, bits, epilogue=L.SC_EPI_SWIGLU, out_dtype=torch.float32).cpu().numpy()
     refs = [otp.silu(f(x, *g, group, bits)) * f(x, *u, group, bits) for f in (ref16, ref_exact)]
-    assert_kernel_close(y, refs, 5e-5)
+    # the product of two GEMV outputs doubles their relative error
+    assert_kernel_close(y, refs, 1e-4)
 
 
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("M", [3, 8, 16, 21])
 def test_batched_kernel_fp32_input_keeps_x(cuda, rng, bits, M):
-    """fp32 activations through the batched kernel (weights rounded once to
-    fp16 as ``mx.dequantize`` does, x carried as fp16 high + low parts): the
-    product matches the float64 one of the fp16-rounded weights to ~1e-5,
-    where rounding x to fp16 alone sits near 3e-4.  Passes the decode kernel
-    takes (8-bit, M <= 4) match the exact-weight product instead."""
+    """fp32 activations in batches: up to 16 rows run decode-GEMV passes
+    (exact weights, x carried as fp16 high + low parts), more run the
+    tensor-core GEMM (the same definition); the product matches the float64
+    exact-weight one to 5e-5, where rounding x to fp16 alone sits near 3e-4
+    and rounding the weights to fp16 near 2e-4."""
     K, N, group = 4096, 512, 64
     wq, s, b = make_q(rng, N, K, bits, group)
     x = rng.standard_normal((M, K)).astype(np.float32)
@@ -172,7 +173,7 @@ def test_batched_kernel_fp32_input_keeps_x(cuda, rng, bits, M):
                               epilogue=L.SC_EPI_RESIDUAL, residual=r_dev, out=r_dev)
             y = r_dev.cpu().numpy()
             refs = [res + ref16(x, wq, s, b, group, bits), res + ref_exact(x, wq, s, b, group, bits)]
-        assert_kernel_close(y, refs, 2e-5)
+        assert_kernel_close(y, refs, 5e-5)
     assert L.load().sc_qgemv_device_error(1) == 0
 
 
