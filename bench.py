@@ -637,17 +637,30 @@ def main():
                     "ms_per_step": ms_step, "share_of_step": 1.0, "step_bytes": step_bytes,
                     "step_frac": achieved / peak}
     else:
-        # per-kernel step: event pairs around every dequant-GEMV of a step
+        # per-kernel step: in-kernel %globaltimer stamps of every dequant-GEMV
+        # of a step (first consumer past the dependency wait .. last CTA's
+        # exit), in a second capture of the same step with PDL left on
         eng.capture_probe()
         eng.replay_probe()
         g_ms, g_bytes, g_n = 0.0, 0, 0
+        kinds = {}  # launch order per step: per layer q|k|v, o, gate|up, down; then the head
         for _ in range(args.steps):
             a, b, n = eng.replay_probe()
             g_ms += a
             g_bytes += b
             g_n += n
+            nl = cfg.num_layers
+            for slot, ns, nb in eng.probe_last:
+                k = ("qkv", "o", "gate_up", "down")[slot % 4] if slot < 4 * nl else "lm_head"
+                e = kinds.setdefault(k, [0, 0, 0])
+                e[0] += ns
+                e[1] += nb
+                e[2] += 1
         achieved = g_bytes / (g_ms / 1e3) / 1e9
         roofline = {"bound": "hbm", "kernel": "qgemv_fx (fused RMSNorm/dequant-GEMV/epilogue)", "achieved": achieved,
+                    "time_source": "in-kernel %globaltimer stamps per GEMV launch inside the graph step (PDL on)",
+                    "by_kind": {k: {"us_per_launch": v[0] / 1e3 / v[2], "GB/s": v[1] / v[0], "frac": v[1] / v[0] / peak}
+                                for k, v in kinds.items() if v[0] > 0},
                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                     "traffic": NCU_GEMV_TRAFFIC.get((args.model, world, args.batch, args.bits, args.group, args.ctx)),
                     "traffic_unit": "bytes per step", "launches_per_step": g_n // args.steps,

@@ -127,6 +127,14 @@ int sc_qlinear_noalloc(const void* x, int x_dtype, int M, int K, int ldx,
  * Synchronises with the device; reset != 0 clears it.  No reference
  * counterpart (the reference has no device code). */
 int sc_qgemv_device_error(int reset);
+/* In-step timing of the decode GEMV: the sc_qlinear* launches this host
+ * thread makes after this call carry `pair` (two uint64 in device memory,
+ * preset to {UINT64_MAX, 0}); the decode kernel atomically lowers pair[0] to
+ * the %globaltimer (ns) at which its first consumer passed the dependency
+ * wait and raises pair[1] to its last CTA's exit (or its split-K reduce's).
+ * No event is recorded, so programmatic dependent launch stays on.  NULL
+ * stops it. */
+int sc_qgemv_probe_stamps(unsigned long long* pair);
 
 /* Fused form used by the decode engine (no reference counterpart as one
  * call; it fuses the reference's RMSNorm -> q/k/v or gate/up linears ->

@@ -36,6 +36,7 @@ SIGNATURES = {
     "sc_qlinear_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "sc_qlinear_noalloc": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp]),
     "sc_qgemv_device_error": (_i, [_i]),
+    "sc_qgemv_probe_stamps": (_i, [_vp]),
     "sc_l2_prefetch": (_i, [_pp, C.POINTER(_sz), _i, _sz, _vp]),
     "sc_qlinear": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "sc_qlinear_fused": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp, _i,

@@ -76,7 +76,12 @@ struct QGemvParams {
   int lg_group;          // log2(group)
   int x_vec;             // x rows start on 16 bytes: 8 values load as one or two 16-byte vectors
   PrefetchList pf;       // the next kernel's weights, pulled into L2 by the decode kernel's producer
+  unsigned long long* stamp;  // null, or {first consumer start after the dependency wait, last exit} (%globaltimer)
 };
+
+// The stamp pointer the next sc_qlinear* launches of this host thread carry
+// (sc_qgemv_probe_stamps).
+static thread_local unsigned long long* t_next_stamp = nullptr;
 
 template <int BITS>
 struct QTraits;
@@ -1182,6 +1187,7 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   // ============================ consumers ============================
   const int g = lane >> 2, t = lane & 3;
   pdl_wait();
+  if (p.stamp && tid == 0) atomicMin(p.stamp, (unsigned long long)globaltimer_ns());
   // The epilogue's global reads (residual, bias) do not depend on this
   // kernel's results: when every consumer thread owns at most one output of
   // the CTA, issue them now, beside the x loads, so the kernel ends in writes.
@@ -1469,6 +1475,10 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
     else
       epilogue<EPI, YT>(p, split, geo.atomic_out != 0, row, mm, v);
   }
+  if (p.stamp) {  // the CTA's last output is written
+    named_bar_sync(1, NC);
+    if (tid == 0) atomicMax(p.stamp + 1, (unsigned long long)globaltimer_ns());
+  }
 }
 
 template <int EPI, typename YT>
@@ -1495,6 +1505,10 @@ __global__ void qgemv_splitk_reduce(const QGemvParams p) {
       if (EPI == SC_EPI_RESIDUAL) out += p.residual[(size_t)col * p.ldr + row];
     }
     reinterpret_cast<YT*>(p.y)[(size_t)col * p.ldy + row] = from_f32<YT>(out);
+  }
+  if (p.stamp) {
+    __syncthreads();
+    if (threadIdx.x == 0) atomicMax(p.stamp + 1, (unsigned long long)globaltimer_ns());
   }
 }
 
@@ -1937,6 +1951,7 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
   SC_REQUIRE(epi != SC_EPI_SWIGLU || !bias, SC_ERR_UNSUPPORTED, "qlinear: bias with SwiGLU epilogue");
 
   QGemvParams p{};
+  p.stamp = t_next_stamp;
   p.K = K;
   p.ldx = ldx;
   p.norm_w = norm_w;
@@ -2080,6 +2095,11 @@ size_t sc_qlinear_workspace_bytes(int M, int K, int N, int bits) {
                                                  N, 2));
       }
   return best;
+}
+
+int sc_qgemv_probe_stamps(unsigned long long* pair) {
+  sc::t_next_stamp = pair;
+  return SC_OK;
 }
 
 int sc_qgemv_device_error(int reset) {

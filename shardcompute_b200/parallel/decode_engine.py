@@ -198,9 +198,8 @@ class DecodeEngine:
         Bp = (C.c_void_p * n)(*[s[2].data_ptr() for s in segs])
         R = (C.c_int * n)(*rows)
         if self._probe is not None:
-            ev0 = torch.cuda.Event(enable_timing=True, external=True)
-            ev1 = torch.cuda.Event(enable_timing=True, external=True)
-            ev0.record()
+            slot = len(self._probe)
+            L.call("sc_qgemv_probe_stamps", self._stamps[slot].data_ptr())
         args = (x.data_ptr(), ops._dt(x), M, K, K, None if norm is None else norm.data_ptr(), float(self.eps), n,
                 C.cast(W, L._pp), C.cast(Sp, L._pp), C.cast(Bp, L._pp), R, self.group, self.bits, None, epilogue,
                 out.data_ptr(), ops._dt(out), N, None if residual is None else residual.data_ptr(),
@@ -212,13 +211,13 @@ class DecodeEngine:
             L.call("sc_qlinear_fused_prefetch", *args, C.cast(pf[0], L._pp), pf[1], pf[2], 0,
                    ops.stream_handle(self.device))
         if self._probe is not None:
-            ev1.record()
+            L.call("sc_qgemv_probe_stamps", None)
             # algorithmic bytes: packed words + fp16 scale/bias of every segment,
             # the activations in, the norm weight, the outputs (and residual) once
             nbytes = (sum(r * K * self.bits // 8 + r * (K // self.group) * 4 for r in rows) +
                       M * K * x.element_size() + (0 if norm is None else K * 2) +
                       M * N * out.element_size() + (M * N * residual.element_size() if residual is not None else 0))
-            self._probe.append((ev0, ev1, nbytes))
+            self._probe.append((slot, nbytes))
 
     def _pf_list(self, segs):
         """(ptrs, sizes, n) for an L2 prefetch of a budget's share of ``segs``:
@@ -552,31 +551,52 @@ class DecodeEngine:
         return self.graph
 
     def capture_probe(self):
-        """Capture a second copy of the decode step with a CUDA event pair
-        around every dequant-GEMV launch; ``replay_probe`` then returns the
-        summed GEMV device time and algorithmic bytes of one step."""
+        """Capture a second copy of the decode step whose dequant-GEMV
+        launches carry in-kernel time stamps (``sc_qgemv_probe_stamps``: the
+        first consumer past the dependency wait, the last CTA's exit), so
+        programmatic dependent launch stays on and the GEMVs run as they do
+        in the step; ``replay_probe`` then returns their summed in-step time
+        and algorithmic bytes."""
         stream = torch.cuda.Stream(device=self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
+        nmax = 4 * self.cfg.num_layers + 8
+        init = torch.zeros(nmax, 2, dtype=torch.int64, device=self.device)
+        init[:, 0] = -1  # UINT64_MAX: the stamps lower it
+        self._stamps_init = init
+        self._stamps = init.clone()
         self._probe = []
         g = torch.cuda.CUDAGraph()
         hp0 = self.host_pos
         try:
             with torch.cuda.graph(g, stream=stream):
+                self._stamps.copy_(self._stamps_init)
                 self.decode_step()
         finally:
             probe, self._probe = self._probe, None
             self.host_pos = hp0
+            L.call("sc_qgemv_probe_stamps", None)
         torch.cuda.synchronize(self.device)
-        self._probe_graph, self._probe_events = g, probe
+        self._probe_graph, self._probe_slots = g, probe
         return g
 
     def replay_probe(self):
-        """Replay the instrumented step; returns (gemv_ms, gemv_bytes, launches)."""
+        """Replay the instrumented step; returns (gemv_ms, gemv_bytes,
+        launches): the sum over the step's GEMVs of (last exit - first
+        consumer start), all on the device clock."""
         self._advance(1)
         self._probe_graph.replay()
         torch.cuda.synchronize(self.device)
-        ms = sum(a.elapsed_time(b) for a, b, _ in self._probe_events)
-        return ms, sum(n for _, _, n in self._probe_events), len(self._probe_events)
+        st = self._stamps.cpu().numpy().view(np.uint64)
+        ns, nbytes, n = 0, 0, 0
+        self.probe_last = []  # (slot, ns, bytes) of the last replay, in launch order
+        for slot, b in self._probe_slots:
+            t0, t1 = int(st[slot, 0]), int(st[slot, 1])
+            if t0 != 0xFFFFFFFFFFFFFFFF and t1 >= t0:
+                ns += t1 - t0
+                nbytes += b
+                n += 1
+                self.probe_last.append((slot, t1 - t0, b))
+        return ns / 1e6, nbytes, n
 
     def decode_host(self, tokens: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """One greedy step driven from host memory: copy ``tokens`` (pinned
