@@ -656,9 +656,15 @@ def main():
                 e[0] += ns
                 e[1] += nb
                 e[2] += 1
+        if g_n == 0:  # no decode-GEMV launch in the step (more than 16 rows: the tensor-core GEMM)
+            g_ms, g_bytes, g_n = ms_step * args.steps, int(eng.weight_bytes_per_step()) * args.steps, args.steps
+            kinds = {}
         achieved = g_bytes / (g_ms / 1e3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "qgemv_fx (fused RMSNorm/dequant-GEMV/epilogue)", "achieved": achieved,
-                    "time_source": "in-kernel %globaltimer stamps per GEMV launch inside the graph step (PDL on)",
+        roofline = {"bound": "hbm", "kernel": "qgemv_fx (fused RMSNorm/dequant-GEMV/epilogue)" if kinds else
+                    "whole decode step (more than 16 rows per linear: the tensor-core GEMM; weights over the step time)",
+                    "achieved": achieved,
+                    "time_source": "in-kernel %globaltimer stamps per GEMV launch inside the graph step (PDL on)"
+                    if kinds else "step time (CUDA events)",
                     "by_kind": {k: {"us_per_launch": v[0] / 1e3 / v[2], "GB/s": v[1] / v[0], "frac": v[1] / v[0] / peak}
                                 for k, v in kinds.items() if v[0] > 0},
                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,

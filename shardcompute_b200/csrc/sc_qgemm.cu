@@ -73,7 +73,8 @@ struct QgemmParams {
   int ldy;
   const float* residual;
   int ldr;
-  int row_tiles, tok_tiles, tok_groups, kblocks;  // tok_groups: work items per weight tile
+  int row_tiles, tok_tiles, tok_groups, kblocks;  // tok_groups: token groups per weight tile
+  int ksplit;                // 1, or 2: each work item takes half of the k blocks and adds its result atomically
 };
 
 struct QgemmMaps {
@@ -190,7 +191,12 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
 
   unsigned char* base = qm_smem + ((1024 - (smem_u32(qm_smem) & 1023)) & 1023);
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0), lane = threadIdx.x & 31;
-  const int ntiles = p.row_tiles * p.tok_groups;
+  const int ntiles = p.row_tiles * p.tok_groups * p.ksplit;
+  // work item `tile`: weight tile rt, token group tg, k half ks (fastest, so both halves run together)
+  auto tg_of = [&](int tile) { return (tile / p.ksplit) % p.tok_groups; };
+  auto rt_of = [&](int tile) { return tile / (p.ksplit * p.tok_groups); };
+  auto kb_lo = [&](int tile) { return (tile % p.ksplit) * (p.kblocks / 2); };
+  auto kb_hi = [&](int tile) { return p.ksplit == 1 || (tile % p.ksplit) == 1 ? p.kblocks : p.kblocks / 2; };
   if (threadIdx.x == 0) {
     for (int s = 0; s < QM_NST; ++s) {
       mbar_init(&full_x[s], 1);
@@ -210,16 +216,15 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
   pdl_wait();
   volatile int* abort = &s_abort;
   const uint32_t tmem = s_tmem;
-  const int kb_n = p.kblocks;
 
   if (warp == 0) {
     // ================================ x tiles ================================
     if (lane == 0) {
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
-        const int tt0 = (tile % p.tok_groups) * QM_TT;
+        const int tt0 = tg_of(tile) * QM_TT;
         const int nsub = min(QM_TT, p.tok_tiles - tt0);
-        for (int kb = 0; kb < kb_n; ++kb, ++it) {
+        for (int kb = kb_lo(tile); kb < kb_hi(tile); ++kb, ++it) {
           const int s = it % QM_NST;
           const uint32_t ph = (it / QM_NST) & 1u;
           if (!qm_wait(&empty[s], ph ^ 1u, abort)) break;
@@ -242,8 +247,9 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
     if (lane == 0) {
       uint32_t it = 0, tl = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x, ++tl) {
-        const int tt0 = (tile % p.tok_groups) * QM_TT;
+        const int tt0 = tg_of(tile) * QM_TT;
         const int nsub = min(QM_TT, p.tok_tiles - tt0);
+        const int k_first = kb_lo(tile);
         uint32_t idesc[QM_TT];
         for (int j = 0; j < QM_TT; ++j) {
           const int nt = j < nsub ? min(QM_TN, p.M - (tt0 + j) * QM_TN) : 16;
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
         if (tl > 0 && !qm_wait(&acc_empty, (tl - 1) & 1u, abort)) break;
         tc_fence_after();
         bool ok = true;
-        for (int kb = 0; kb < kb_n; ++kb, ++it) {
+        for (int kb = k_first; kb < kb_hi(tile); ++kb, ++it) {
           const int s = it % QM_NST;
           const uint32_t ph = (it / QM_NST) & 1u;
           if (!qm_wait(&full_x[s], ph, abort) || !qm_wait(&full_w[s], ph, abort)) {
@@ -266,7 +272,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
 #pragma unroll
           for (int kk = 0; kk < QM_KB / 16; ++kk) {
             const uint32_t off = kk * 32;  // 16 fp16 of k inside the 128-byte swizzle atom
-            const uint32_t acc = (kb | kk) != 0;
+            const uint32_t acc = (kb != k_first || kk != 0) ? 1u : 0u;
             for (int j = 0; j < nsub; ++j) {
               const uint32_t xh = st + 2 * j * QM_TILE_BYTES, xl = xh + QM_TILE_BYTES;
               const uint32_t td = tmem + (uint32_t)(j * QM_TN);
@@ -301,7 +307,8 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
     uint32_t it = 0, tl = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tl) {
-      const int rt = tile / p.tok_groups, tt0 = (tile % p.tok_groups) * QM_TT;
+      const int rt = rt_of(tile), tt0 = tg_of(tile) * QM_TT;
+      const int k_end = kb_hi(tile);
       // this thread's weight row
       int rr = rt * QM_TM + r, sg = 0;
       const bool inN = rr < p.N;
@@ -325,7 +332,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
         for (int i = 0; i < NV; ++i) {
           const int j = (4 * i) / WPH, wi = (4 * i) % WPH;
           const int kb = kb0 + j;
-          dw[i] = (rvalid && kb < kb_n) ? ldg_stream_v4(wrow_p + (size_t)kb * (2 * WPH) + wi)
+          dw[i] = (rvalid && kb < k_end) ? ldg_stream_v4(wrow_p + (size_t)kb * (2 * WPH) + wi)
                                         : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
@@ -333,18 +340,18 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
           const int kb = kb0 + j;
           const int k0 = kb * QM_KB + half * (QM_KB / 2);
           const int g0 = k0 >> p.lg_group, g1 = (k0 + QM_KB / 2 - 1) >> p.lg_group;
-          const bool v = rvalid && kb < kb_n;
+          const bool v = rvalid && kb < k_end;
           dsb[j][0] = v ? (uint32_t)ldg_u16(srow_p + g0) | ((uint32_t)ldg_u16(brow_p + g0) << 16) : 0u;
           dsb[j][1] = v ? (uint32_t)ldg_u16(srow_p + g1) | ((uint32_t)ldg_u16(brow_p + g1) << 16) : 0u;
         }
       };
-      load_group(0, cw, csb);
-      for (int kb0 = 0; kb0 < kb_n && ok; kb0 += PD) {
-        if (kb0 + PD < kb_n) load_group(kb0 + PD, nw, nsb);
+      load_group(kb_lo(tile), cw, csb);
+      for (int kb0 = kb_lo(tile); kb0 < k_end && ok; kb0 += PD) {
+        if (kb0 + PD < k_end) load_group(kb0 + PD, nw, nsb);
 #pragma unroll
         for (int jb = 0; jb < PD; ++jb) {
           const int kb = kb0 + jb;
-          if (kb >= kb_n) break;
+          if (kb >= k_end) break;
           const int s = it % QM_NST;
           const uint32_t ph = (it / QM_NST) & 1u;
           ++it;
@@ -425,6 +432,10 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
           for (int i = 0; i < 32; ++i) {
             if (c0 + i >= nt) break;
             const int m = tt * QM_TN + c0 + i;
+            if (p.ksplit > 1) {  // fp32 scratch, zeroed: two halves add in either order to the same bits
+              atomicAdd(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + col, v[i]);
+              continue;
+            }
             float o = v[i] + bb;
             if (p.epi == SC_EPI_RESIDUAL) o += p.residual[(size_t)m * p.ldr + col];
             if (p.y_f16)
@@ -542,8 +553,25 @@ __global__ void qgemm_swiglu_rows_kernel(const float* __restrict__ t, int M, int
 
 size_t qgemm_workspace_bytes(int M, int K, int N, int epi) {
   size_t b = 2 * (size_t)M * K * sizeof(__half) + 512;
-  if (epi == SC_EPI_SWIGLU) b += (size_t)M * 2 * N * sizeof(float) + 256;
+  // fp32 scratch: the [gate | up] product (SwiGLU), or the split-k sum
+  b += (size_t)M * (epi == SC_EPI_SWIGLU ? 2 * N : N) * sizeof(float) + 256;
   return b;
+}
+
+// Split-k finish: y = acc (+ bias) (+ residual), in y's dtype.
+template <typename YT>
+__global__ void qgemm_finish_kernel(const float* __restrict__ acc, int M, int N, const uint16_t* __restrict__ bias,
+                                    const float* residual, int ldr, YT* y, int ldy) {
+  pdl_trigger();
+  pdl_wait();
+  const size_t total = (size_t)M * N;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(e / N), n = (int)(e % N);
+    float o = acc[e];
+    if (bias) o += __half2float(__ushort_as_half(bias[n]));
+    if (residual) o += residual[(size_t)m * ldr + n];
+    y[(size_t)m * ldy + n] = from_f32<YT>(o);
+  }
 }
 
 int run_qgemm(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_w, float eps, int nseg,
@@ -592,16 +620,23 @@ int run_qgemm(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t*
   p.bits = bits;
   p.bias = epi == SC_EPI_SWIGLU ? nullptr : bias;
   p.epi = epi == SC_EPI_SWIGLU ? SC_EPI_STORE : epi;
-  p.y = epi == SC_EPI_SWIGLU ? static_cast<void*>(tmp) : y;
-  p.y_f16 = epi == SC_EPI_SWIGLU ? 0 : y_dtype == SC_F16;
-  p.ldy = epi == SC_EPI_SWIGLU ? N : ldy;
-  p.residual = residual;
-  p.ldr = ldr;
   p.row_tiles = (N + QM_TM - 1) / QM_TM;
   p.tok_tiles = (M + QM_TN - 1) / QM_TN;
   p.tok_groups = (p.tok_tiles + QM_TT - 1) / QM_TT;
   p.kblocks = K / QM_KB;
-  const int ntiles = p.row_tiles * p.tok_groups;
+  // halves of k as separate work items when twice the tiles still fit one wave of SMs
+  p.ksplit = (2 * p.row_tiles * p.tok_groups <= sm_count() && p.kblocks >= 8) ? 2 : 1;
+  const bool scratch = epi == SC_EPI_SWIGLU || p.ksplit > 1;
+  p.y = scratch ? static_cast<void*>(tmp) : y;
+  p.y_f16 = scratch ? 0 : y_dtype == SC_F16;
+  p.ldy = scratch ? N : ldy;
+  if (p.ksplit > 1) {
+    cudaError_t e = cudaMemsetAsync(tmp, 0, (size_t)M * N * sizeof(float), stream);
+    SC_REQUIRE(e == cudaSuccess, SC_ERR_CUDA, "qgemm: scratch memset failed (%s)", cudaGetErrorString(e));
+  }
+  p.residual = residual;
+  p.ldr = ldr;
+  const int ntiles = p.row_tiles * p.tok_groups * p.ksplit;
   const int grid = std::min(ntiles, sm_count());
   const size_t smem = (size_t)QM_NST * QM_STAGE_BYTES + 1024;
   if (bits == 4) {
@@ -620,7 +655,19 @@ int run_qgemm(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t*
     launch(qgemm_tc_kernel<8>, dim3(grid), dim3(QM_THREADS), smem, stream, p, maps);
   }
   st = check_launch("qgemm_tc");
-  if (st != SC_OK || epi != SC_EPI_SWIGLU) return st;
+  if (st != SC_OK) return st;
+  if (epi != SC_EPI_SWIGLU) {
+    if (p.ksplit == 1) return SC_OK;
+    const int blocks = (int)std::min<size_t>(((size_t)M * N + 255) / 256, (size_t)8 * sm_count());
+    const float* res = epi == SC_EPI_RESIDUAL ? residual : nullptr;
+    if (y_dtype == SC_F16)
+      launch(qgemm_finish_kernel<__half>, dim3(blocks), dim3(256), 0, stream, tmp, M, N, bias, res, ldr,
+             static_cast<__half*>(y), ldy);
+    else
+      launch(qgemm_finish_kernel<float>, dim3(blocks), dim3(256), 0, stream, tmp, M, N, bias, res, ldr,
+             static_cast<float*>(y), ldy);
+    return check_launch("qgemm_finish");
+  }
   const int F = seg_rows[0];
   const int blocks = (int)std::min<size_t>(((size_t)M * F + 255) / 256, (size_t)8 * sm_count());
   if (y_dtype == SC_F16)
