@@ -181,7 +181,9 @@ __device__ __forceinline__ bool qm_wait(uint64_t* bar, uint32_t parity, volatile
 // Byte offset of 16-byte chunk c of row r in a SW128 K-major tile.
 __device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-template <int BITS>
+// KS: 1, or 2 (each work item takes half of the k blocks; the split is a
+// template parameter so the unsplit kernel keeps its constant-folded loops)
+template <int BITS, int KS>
 __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmParams p,
                                                                  const __grid_constant__ QgemmMaps maps) {
   extern __shared__ __align__(1024) unsigned char qm_smem[];
@@ -191,12 +193,12 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
 
   unsigned char* base = qm_smem + ((1024 - (smem_u32(qm_smem) & 1023)) & 1023);
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0), lane = threadIdx.x & 31;
-  const int ntiles = p.row_tiles * p.tok_groups * p.ksplit;
+  const int ntiles = p.row_tiles * p.tok_groups * KS;
   // work item `tile`: weight tile rt, token group tg, k half ks (fastest, so both halves run together)
-  auto tg_of = [&](int tile) { return (tile / p.ksplit) % p.tok_groups; };
-  auto rt_of = [&](int tile) { return tile / (p.ksplit * p.tok_groups); };
-  auto kb_lo = [&](int tile) { return (tile % p.ksplit) * (p.kblocks / 2); };
-  auto kb_hi = [&](int tile) { return p.ksplit == 1 || (tile % p.ksplit) == 1 ? p.kblocks : p.kblocks / 2; };
+  auto tg_of = [&](int tile) { return (tile / KS) % p.tok_groups; };
+  auto rt_of = [&](int tile) { return tile / (KS * p.tok_groups); };
+  auto kb_lo = [&](int tile) { return KS == 1 ? 0 : (tile % KS) * (p.kblocks / 2); };
+  auto kb_hi = [&](int tile) { return KS == 1 || (tile % KS) == 1 ? p.kblocks : p.kblocks / 2; };
   if (threadIdx.x == 0) {
     for (int s = 0; s < QM_NST; ++s) {
       mbar_init(&full_x[s], 1);
@@ -432,7 +434,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1) qgemm_tc_kernel(const QgemmPara
           for (int i = 0; i < 32; ++i) {
             if (c0 + i >= nt) break;
             const int m = tt * QM_TN + c0 + i;
-            if (p.ksplit > 1) {  // fp32 scratch, zeroed: two halves add in either order to the same bits
+            if (KS > 1) {  // fp32 scratch, zeroed: two halves add in either order to the same bits
               atomicAdd(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + col, v[i]);
               continue;
             }
@@ -639,21 +641,18 @@ int run_qgemm(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t*
   const int ntiles = p.row_tiles * p.tok_groups * p.ksplit;
   const int grid = std::min(ntiles, sm_count());
   const size_t smem = (size_t)QM_NST * QM_STAGE_BYTES + 1024;
-  if (bits == 4) {
-    static bool cfg = false;
-    if (!cfg) {
-      cudaFuncSetAttribute(qgemm_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      cfg = true;
+  static bool cfg[2][2] = {};  // shared-memory opt-in, once per instantiation
+  auto go = [&](auto kern, int bi, int ki) {
+    if (!cfg[bi][ki]) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cfg[bi][ki] = true;
     }
-    launch(qgemm_tc_kernel<4>, dim3(grid), dim3(QM_THREADS), smem, stream, p, maps);
-  } else {
-    static bool cfg = false;
-    if (!cfg) {
-      cudaFuncSetAttribute(qgemm_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      cfg = true;
-    }
-    launch(qgemm_tc_kernel<8>, dim3(grid), dim3(QM_THREADS), smem, stream, p, maps);
-  }
+    launch(kern, dim3(grid), dim3(QM_THREADS), smem, stream, p, maps);
+  };
+  if (bits == 4)
+    p.ksplit == 2 ? go(qgemm_tc_kernel<4, 2>, 0, 1) : go(qgemm_tc_kernel<4, 1>, 0, 0);
+  else
+    p.ksplit == 2 ? go(qgemm_tc_kernel<8, 2>, 1, 1) : go(qgemm_tc_kernel<8, 1>, 1, 0);
   st = check_launch("qgemm_tc");
   if (st != SC_OK) return st;
   if (epi != SC_EPI_SWIGLU) {

@@ -232,10 +232,18 @@ __device__ __host__ __forceinline__ int owner_of(long long u, long long T, int n
 }
 __device__ __host__ __forceinline__ long long range_lo(int c, long long T, int n) { return (long long)c * T / n; }
 
-// CTAs a GEMV's T units are split over: every CTA of the split holds at least
-// one unit, so the CTAs between a tile's first and last owner all hold a piece
-// of it (the segment count below relies on that).
-__device__ __host__ __forceinline__ int gemv_ctas(long long T, int n) { return (int)std::min<long long>(T, n); }
+// CTAs a GEMV's T units (tiles of kq) are split over.  Every CTA of the split
+// holds at least one unit, so the CTAs between a tile's first and last owner
+// all hold a piece of it (the segment count below relies on that).  Each CTA
+// holds at least r = ceil((kq - 1) / (SP_MAXT - 1)) units, so a tile's kq
+// units cross at most ceil((kq - 1) / r) + 1 <= SP_MAXT CTAs: small GEMVs on
+// many SMs run on fewer CTAs rather than cut a tile into more segments.
+__device__ __host__ __forceinline__ int gemv_ctas(long long T, int kq, int n) {
+  long long c = std::min<long long>(T, n);
+  const long long r = (kq - 1 + SP_MAXT - 2) / (SP_MAXT - 1);
+  if (r > 1) c = std::min<long long>(c, std::max<long long>(1, T / r));
+  return (int)c;
+}
 
 // First CTA holding tile t (units [t*kq, (t+1)*kq)) and the tile's segment count.
 __device__ __host__ __forceinline__ int tile_first(int t, int kq, long long T, int n) {
@@ -693,7 +701,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const __grid
           continue;
         }
         // GEMV: this CTA's units, SP_STAGE_BOXES / nset per stage
-        const int nC = gemv_ctas(op.total, n);
+        const int nC = gemv_ctas(op.total, op.kq, n);
         const long long lo = c < nC ? range_lo(c, op.total, nC) : 0, hi = c < nC ? range_lo(c + 1, op.total, nC) : 0;
         // one bulk copy per stage: the CTA's units are contiguous in the op's image
         const int qps = SP_STAGE_BOXES / op.nset;
@@ -792,7 +800,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const __grid
     if (op.kind == SOP_ATTN) {
       if (c >= na) continue;
       const StepOp& qop = P.ops[oi - 1];  // this layer's q|k|v GEMV
-      const int nQ = gemv_ctas(qop.total, n);
+      const int nQ = gemv_ctas(qop.total, qop.kq, n);
       const long long lo = range_lo(c, TA, na), hi = range_lo(c + 1, TA, na);
       if (tid == 0 && !*abort && !wait_ctr(P, P.ctr + qop.grp_ctr, (gen + 1) * qop.seg_need, SPE_QKV, oi)) *abort = 1;
       stamp(oi, 1);
@@ -1018,7 +1026,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) decode_step_kernel(const __grid
     }
 
     // ---------------------------------------------------------------- GEMV
-    const int nC = gemv_ctas(op.total, n);
+    const int nC = gemv_ctas(op.total, op.kq, n);
     const long long lo = c < nC ? range_lo(c, op.total, nC) : 0, hi = c < nC ? range_lo(c + 1, op.total, nC) : 0;
     if (lo < hi) {
       // input complete, then staged into shared memory (plain loads: the
@@ -1779,7 +1787,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
     q.x_need = H / 64;
     q.part = reinterpret_cast<float*>(ws + L.part_qkv);
     q.grp_ctr = L.ctr_grp + oq * L.max_groups;
-    for (int tt = 0; tt < q.tiles; ++tt) q.seg_need += tile_nseg(tt, q.kq, q.total, gemv_ctas(q.total, n));
+    for (int tt = 0; tt < q.tiles; ++tt) q.seg_need += tile_nseg(tt, q.kq, q.total, gemv_ctas(q.total, q.kq, n));
     ops.push_back(q);
     StepOp a{};
     a.kind = SOP_ATTN;
@@ -1851,7 +1859,7 @@ int sc_step_finalize(void* step, void* workspace, size_t workspace_bytes, cudaSt
   for (const auto& o : ops) {
     if (o.kind == SOP_EMBED || o.kind == SOP_ATTN) continue;
     for (int tt = 0; tt < o.tiles; ++tt)
-      SC_REQUIRE(tile_nseg(tt, o.kq, o.total, gemv_ctas(o.total, n)) <= SP_MAXT, SC_ERR_UNSUPPORTED,
+      SC_REQUIRE(tile_nseg(tt, o.kq, o.total, gemv_ctas(o.total, o.kq, n)) <= SP_MAXT, SC_ERR_UNSUPPORTED,
                  "step_finalize: a tile of op kind %d spans more than %d CTAs", o.kind, SP_MAXT);
   }
   // ---- shared memory: staged x (or an attention merge), then as many ring stages as fit

@@ -25,6 +25,10 @@ SHAPES = {
     "tinyllama-dims-2L": synth.tiny_shape(vocab_size=32000, hidden_size=2048, num_layers=2, num_heads=32,
                                           num_kv_heads=4, intermediate_size=5632),
     "g1-hd128": synth.tiny_shape(hidden_size=1024, num_heads=8, num_kv_heads=8, intermediate_size=1536),
+    # a 512-row head over a 4096-deep input (as on a TP8 rank): that GEMV runs on fewer CTAs
+    # than SMs, so a tile's 16 units cross at most 4 CTAs
+    "head512-4096deep": synth.tiny_shape(vocab_size=512, hidden_size=4096, num_heads=32, num_kv_heads=8,
+                                         intermediate_size=512),
 }
 
 
