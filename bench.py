@@ -357,6 +357,11 @@ def dist_env():
 # replays of `python bench.py --steps 2 --warmup 3 --no-cpu-baseline`).
 NCU_GEMV_TRAFFIC = {("llama3-8b", 1, 1, 4, 64, 2048): 4235.6e6}
 
+# The first 8 greedy tokens of sequence 0 after the prompt, from a TP1 run of
+# the same command (synthetic weights are one model at TP 1/2/4/8, so every N
+# should reproduce them); keyed by (model, bits, group, ctx, batch, layers).
+TP1_FIRST_TOKENS = {("llama3-8b", 4, 64, 2048, 1, 32): [72726, 111630, 23418, 10603, 90257, 89492, 83690, 73369]}
+
 
 def probe_mlx() -> str:
     """Whether the reference's CPU backend (MLX) imports on this host."""
@@ -689,6 +694,9 @@ def main():
                 "config": workload_config(args, world), "clocks": clk, "e2e": e2e,
                 "gpu_launches": launches_per_step * args.steps, "roofline": roofline, "cpu_baseline": cpu,
                 "first_tokens": first,
+                "first_tokens_match_tp1": (None if (key := (args.model, args.bits, args.group, args.ctx, B,
+                                                            args.layers or cfg.num_layers)) not in TP1_FIRST_TOKENS
+                                           else first == TP1_FIRST_TOKENS[key]),
                 "prefill": {"tokens": B * args.ctx, "ms": prefill_ms, "tok_per_s": B * args.ctx / (prefill_ms / 1e3),
                             "note": "the prompt through every layer (tensor-core GEMM for more than 16 rows, "
                                     "flash attention), CUDA events, after one warm-up prefill"}}

@@ -138,40 +138,65 @@ class RankWeights:
 
         return cls.from_shard(cfg, load_rank_shard(shard_dir, rank, device), world, rank, bits, group, device)
 
+    SYNTH_SLICES = 8  # the finest tensor-parallel split the synthetic model is drawn for
+
     @classmethod
     def synthetic(cls, cfg: ModelConfig, world: int, rank: int, bits: int = 4, group: int = 64,
                   device: Optional[torch.device] = None, seed: int = 0, std: float = 0.02) -> "RankWeights":
-        """Random-init N(0, std) fp16 weights of this rank's shard, quantized on the GPU.
+        """Random-init N(0, std) fp16 weights of this rank's shard of ONE full
+        model, quantized on the GPU.
 
-        Each rank draws its own slices (seeded by rank and tensor), which is
-        statistically the same as sharding one full random model.
+        Every full tensor is drawn as 8 slices along the axis the sharder
+        splits it on (output rows of the column-parallel linears and of the
+        vocab-split embedding, input columns of the row-parallel o / down),
+        slice j from its own seed (tensor, j).  A rank of a world dividing 8
+        draws exactly its slices, so TP 1, 2, 4 and 8 hold shards of the same
+        model (their greedy tokens agree up to the reduction order).  Other
+        world sizes draw each rank's shard from seeds of (tensor, rank).
         """
         device = device or torch.device("cuda", torch.cuda.current_device())
         gen = torch.Generator(device=device)
         H, F, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
         Hq, Hkv = cfg.num_heads // world, cfg.kv_heads // world
-        counter = [seed * 1000003 + rank * 7919]
+        nsl = cls.SYNTH_SLICES
+        sliced = nsl % world == 0
+        per = nsl // world if sliced else 1
+        tensor_id = [0]
 
-        def q(rows: int, cols: int) -> QTriple:
-            counter[0] += 1
-            gen.manual_seed(counter[0])
+        def draw(rows: int, cols: int, sd: int) -> torch.Tensor:
+            gen.manual_seed(sd)
+            return (torch.randn(rows, cols, generator=gen, device=device) * std).to(torch.float16)
+
+        def q(rows: int, cols: int, split_cols: bool = False) -> QTriple:
+            """This rank's [rows, cols] shard; slices along cols for row-parallel tensors."""
+            tensor_id[0] += 1
+            base = (seed * 1000003 + tensor_id[0]) * 1009
             out_w = torch.empty(rows, cols * bits // 32, dtype=torch.int32, device=device)
             out_s = torch.empty(rows, cols // group, dtype=torch.float16, device=device)
             out_b = torch.empty_like(out_s)
-            step = max(1, (64 << 20) // max(cols, 1))  # quantize in ~64M-element slabs
-            for r0 in range(0, rows, step):
-                r1 = min(rows, r0 + step)
-                w = (torch.randn(r1 - r0, cols, generator=gen, device=device) * std).to(torch.float16)
-                a, b_, c = ops.quantize(w, group, bits)
-                out_w[r0:r1], out_s[r0:r1], out_b[r0:r1] = a, b_, c
+            even = (cols % (per * group) == 0) if split_cols else (rows % per == 0)
+            if not (sliced and even):  # one draw per rank
+                pieces = [(0, rows, 0, cols, base + 7919 * (rank + 1))]
+            elif split_cols:
+                c = cols // per
+                pieces = [(0, rows, j * c, c, base + rank * per + j) for j in range(per)]
+            else:
+                r = rows // per
+                pieces = [(j * r, r, 0, cols, base + rank * per + j) for j in range(per)]
+            for (r0, nr, c0, nc, sd) in pieces:
+                w = draw(nr, nc, sd)
+                a, b_, c_ = ops.quantize(w, group, bits)
                 del w
+                out_w[r0:r0 + nr, c0 * bits // 32:(c0 + nc) * bits // 32] = a
+                out_s[r0:r0 + nr, c0 // group:(c0 + nc) // group] = b_
+                out_b[r0:r0 + nr, c0 // group:(c0 + nc) // group] = c_
             return out_w, out_s, out_b
 
         ones = torch.ones(H, dtype=torch.float16, device=device)
         layers = []
         for _ in range(cfg.num_layers):
             layers.append(LayerWeights(ln1=ones.clone(), ln2=ones.clone(), q=q(Hq * hd, H), k=q(Hkv * hd, H),
-                                       v=q(Hkv * hd, H), o=q(H, Hq * hd), gate=q(F // world, H),
-                                       up=q(F // world, H), down=q(H, F // world)))
+                                       v=q(Hkv * hd, H), o=q(H, Hq * hd, True), gate=q(F // world, H),
+                                       up=q(F // world, H), down=q(H, F // world, True)))
         return cls(cfg=cfg, world=world, rank=rank, bits=bits, group=group,
                    embed=q(cfg.vocab_size // world, H), norm=ones.clone(), layers=layers)
