@@ -172,6 +172,28 @@ int sc_qlinear_fused_prefetch(const void* x, int x_dtype, int M, int K, int ldx,
                               const void* const* pf_ptrs, const size_t* pf_bytes, int pf_n,
                               size_t pf_max_bytes, cudaStream_t stream);
 
+/* Row-parallel quantized linear with its all-reduce in the GEMV epilogue:
+ * y[M, N] (fp32, ldy = N) = the sum over the transport's ranks, in rank
+ * order from zero, of each rank's x.W_r^T (+ bias) (+ residual where it is
+ * passed: rank 0 in tensor-parallel decode) -- the bits sc_qlinear_fused
+ * followed by sc_p2p_allreduce gives, on every rank.  Each CTA pushes its
+ * outputs to every peer as {value, epoch} half lines over NVLink and sums
+ * its rows from the ranks' lines, so no all-reduce launch follows.  y may
+ * alias residual.  Replaces QuantizedRowParallelLinear.forward's quantized
+ * matmul + all_reduce (parallel/quantized_linear.py:419-455, the all-reduce
+ * at 446-447).  p2p: a transport (sc_p2p_create + sc_p2p_open) reserved for
+ * these calls -- their per-CTA epochs live in its header -- whose max_bytes
+ * holds M * N * 4; every rank makes the same sequence of calls.  Returns
+ * SC_ERR_UNSUPPORTED before any launch when the shape does not run as one
+ * unsplit decode-GEMV pass with one output per consumer thread (batch 1-2
+ * at 4-bit g64, up to 4 at 8-bit); the caller then runs sc_qlinear_fused
+ * and sc_p2p_allreduce.  Polls are bounded like sc_p2p_allreduce's (the
+ * transport's error word, sc_p2p_status). */
+int sc_qlinear_allreduce(const void* x, int x_dtype, int M, int K, int ldx, const uint32_t* wq,
+                         const uint16_t* scales, const uint16_t* biases, int N, int group_size, int bits,
+                         const uint16_t* bias, float* y, const float* residual, void* p2p,
+                         cudaStream_t stream);
+
 /* Prefetch up to 12 device regions into L2 (at most max_bytes in total, 0 =
  * no cap) without waiting for them.  The decode step issues it right after a
  * GEMV for the next GEMV's weights, so HBM keeps streaming through kernel

@@ -43,6 +43,7 @@ SIGNATURES = {
                               _vp, _i, _i, _vp, _i, _vp, _sz, _vp]),
     "sc_qlinear_fused_prefetch": (_i, [_vp, _i, _i, _i, _i, _vp, _f, _i, _pp, _pp, _pp, C.POINTER(_i), _i, _i, _vp,
                                        _i, _vp, _i, _i, _vp, _i, _vp, _sz, _pp, C.POINTER(_sz), _i, _sz, _vp]),
+    "sc_qlinear_allreduce": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "sc_embed_gather_q": (_i, [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp]),
     "sc_embed_gather_f16": (_i, [_vp, _i, _vp, _i, _i, _i, _vp, _i, _vp]),
     "sc_dequantize": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),

@@ -228,6 +228,23 @@ class Communicator:
         self._extra_arenas.append((handle, pre))
         return [bases[q] for q in range(self.world_size)], size.value
 
+    def fused_transport(self, max_bytes: int, timeout: float = 60.0):
+        """Collective: a dedicated peer-memory transport (a handle for
+        ``sc_qlinear_allreduce``) carrying messages of up to ``max_bytes``
+        per rank, freed at shutdown; None on every rank when any rank failed
+        (the caller then keeps the GEMV + all-reduce pair).  Its per-CTA
+        epochs live in its own header, so no other collective shares it."""
+        self._require()
+        if self.world_size < 2 or self.world_size > 8 or self.backend != "nccl":
+            return None
+        gen = next(_P2P_GENERATION)
+        pre = f"shardcompute_b200/fused_ar/{gen}"
+        handle = self._open_arena(pre, max(8, int(max_bytes)), timeout)
+        if handle is None:
+            return None
+        self._extra_arenas.append((handle, pre))
+        return handle
+
     @property
     def p2p_enabled(self) -> bool:
         """True when small all-reduces / all-gathers go through NVLink peer memory."""
@@ -524,9 +541,11 @@ class Communicator:
             return 0
         from .. import _lib as L
 
-        if self._p2p is not None:
+        # the collectives' transport and those lent to kernels (the fused
+        # GEMV all-reduce raises the same sticky word on a timeout)
+        for h in ([self._p2p] if self._p2p is not None else []) + [a[0] for a in self._extra_arenas]:
             t = C.c_int(0)
-            L.check(L.load().sc_p2p_status(self._p2p, C.byref(t)), "sc_p2p_status")
+            L.check(L.load().sc_p2p_status(h, C.byref(t)), "sc_p2p_status")
             if t.value:
                 return P2P_TIMEOUT
         err = C.c_int(0)

@@ -33,15 +33,12 @@
 // back to NCCL or aborts.
 #include <string.h>
 
-#include "sc_common.cuh"
+#include "sc_p2p.cuh"
 
 namespace sc {
 
-constexpr int P2P_MAX_WORLD = 8;
 constexpr int P2P_CTAS = 16;       // fixed grid: every call runs the same blocks
 constexpr int P2P_THREADS = 256;
-constexpr size_t P2P_HDR = 4096;   // per-block counters [0, 64), error word at 2048
-constexpr size_t P2P_ERR_OFF = 2048;
 
 struct P2P {
   int world, rank, device;
@@ -54,30 +51,6 @@ struct P2P {
   int* host_err_dev;           // its device address
   uint64_t timeout_ns;
 };
-
-struct P2PArgs {
-  char* data[P2P_MAX_WORLD];  // LL regions of every rank's arena as mapped here
-  uint32_t* ctr;              // this rank's per-block call counters
-  int* err;                   // this rank's error word (device)
-  int* host_err;              // host-mapped copy
-  size_t region_bytes;
-  uint64_t timeout_ns;
-  int world, rank;
-};
-
-__device__ __forceinline__ void st_volatile_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
-               : "memory");
-}
-
-__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
-}
 
 // Payload word `wi` of a message of `count` elements of T (zero past the end).
 template <typename T>
@@ -148,9 +121,7 @@ __device__ __forceinline__ uint4 p2p_recv_line(const P2PArgs& a, int set, int sr
     if (v.y == ep && v.w == ep) return v;
     if ((i & 127) == 0) {
       if (*reinterpret_cast<volatile int*>(a.err) != 0 || globaltimer_ns() - *t0 > a.timeout_ns) {
-        atomicExch(a.err, 1);
-        *reinterpret_cast<volatile int*>(a.host_err) = 1;
-        __threadfence_system();
+        p2p_raise(a);
         *skip = true;
         return v;
       }
@@ -269,6 +240,16 @@ static int p2p_check_device(const P2P* h) {
   int dev = -1;
   cudaGetDevice(&dev);
   SC_REQUIRE(dev == h->device, SC_ERR_ARG, "p2p: current device %d, transport created on %d", dev, h->device);
+  return SC_OK;
+}
+
+int p2p_args_of(void* p2p, P2PArgs* out, size_t* max_bytes) {
+  SC_REQUIRE(p2p && out, SC_ERR_ARG, "p2p: null transport");
+  const P2P* h = static_cast<const P2P*>(p2p);
+  for (int q = 0; q < h->world; ++q) SC_REQUIRE(h->peer[q], SC_ERR_ARG, "p2p: rank %d not mapped", q);
+  if (int st = p2p_check_device(h)) return st;
+  *out = p2p_args(h);
+  if (max_bytes) *max_bytes = h->max_bytes;
   return SC_OK;
 }
 

@@ -35,7 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include "sc_common.cuh"
+#include "sc_p2p.cuh"
 
 namespace sc {
 
@@ -77,6 +77,10 @@ struct QGemvParams {
   int x_vec;             // x rows start on 16 bytes: 8 values load as one or two 16-byte vectors
   PrefetchList pf;       // the next kernel's weights, pulled into L2 by the decode kernel's producer
   unsigned long long* stamp;  // null, or {first consumer start after the dependency wait, last exit} (%globaltimer)
+  // Row-parallel all-reduce in the epilogue (world > 1): every CTA pushes its
+  // outputs to every peer as {value, epoch} half lines, then sums each output
+  // over the ranks in rank order into y (fp32).  world == 0: off.
+  P2PArgs ar;
 };
 
 // The stamp pointer the next sc_qlinear* launches of this host thread carry
@@ -1188,6 +1192,15 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   const int g = lane >> 2, t = lane & 3;
   pdl_wait();
   if (p.stamp && tid == 0) atomicMin(p.stamp, (unsigned long long)globaltimer_ns());
+  __shared__ uint32_t s_ep;    // this CTA's epoch of the fused all-reduce
+  __shared__ int s_ar_skip;    // the transport already failed: no waits
+  if (p.ar.world > 1 && tid == 0) {
+    // the previous fused call (an earlier kernel) is complete: its counter is final
+    const uint32_t e = p.ar.ctr[blockIdx.x] + 1;
+    p.ar.ctr[blockIdx.x] = e;
+    s_ep = e;
+    s_ar_skip = *reinterpret_cast<volatile int*>(p.ar.err) != 0;
+  }
   // The epilogue's global reads (residual, bias) do not depend on this
   // kernel's results: when every consumer thread owns at most one output of
   // the CTA, issue them now, beside the x loads, so the kernel ends in writes.
@@ -1470,6 +1483,32 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       for (int a = 0; a < NACC; ++a) v[a] = v[a] / r;
     }
     if (row >= p.N) continue;
+    if (p.ar.world > 1) {
+      // this rank's partial (the value the unfused path writes before its
+      // all-reduce) to every peer: half line e of region (set, this rank)
+      const float part = (v[0] + pre_bias) + pre_res;
+      const uint32_t ep = s_ep;
+      const size_t e = (size_t)mm * p.N + row;
+      for (int k = 1; k < p.ar.world; ++k) {
+        const int dst = (p.ar.rank + k) % p.ar.world;  // staggered: ranks do not all hit one peer first
+        char* reg = p.ar.data[dst] + (size_t)((ep & 1) * p.ar.world + p.ar.rank) * p.ar.region_bytes;
+        st_volatile_v2(reg + e * 8, __float_as_uint(part), ep);
+      }
+      // the sum over ranks in rank order from zero: the unfused all-reduce's order, so its bits
+      bool skip = s_ar_skip != 0;
+      uint64_t t0 = 0;
+      float acc = 0.f;
+      for (int q = 0; q < p.ar.world; ++q) {
+        if (q == p.ar.rank) {
+          acc += part;
+        } else {
+          const char* reg = p.ar.data[p.ar.rank] + (size_t)((ep & 1) * p.ar.world + q) * p.ar.region_bytes;
+          acc += __uint_as_float(p2p_recv_half(p.ar, reg + e * 8, ep, &skip, &t0));
+        }
+      }
+      reinterpret_cast<float*>(p.y)[(size_t)mm * p.ldy + row] = acc;
+      continue;
+    }
     if (pre_epi)  // bias / residual already read; same sums, same order as epilogue()
       reinterpret_cast<YT*>(p.y)[(size_t)mm * p.ldy + row] = from_f32<YT>((v[0] + pre_bias) + pre_res);
     else
@@ -1934,7 +1973,8 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
                        int nseg, const uint32_t* const* wq, const uint16_t* const* scales,
                        const uint16_t* const* biases, const int* seg_rows, int group, int bits,
                        const uint16_t* bias, int epi, void* y, int y_dtype, int ldy, const float* residual,
-                       int ldr, void* ws, size_t ws_bytes, const PrefetchList* pf, cudaStream_t stream) {
+                       int ldr, void* ws, size_t ws_bytes, const PrefetchList* pf, cudaStream_t stream,
+                       const P2PArgs* ar = nullptr, size_t ar_max_bytes = 0) {
   SC_REQUIRE(x && y && wq && scales && biases && seg_rows, SC_ERR_ARG, "qlinear: null pointer argument");
   SC_REQUIRE(bits == 4 || bits == 8, SC_ERR_SHAPE, "qlinear: bits must be 4 or 8 (got %d)", bits);
   SC_REQUIRE(group == 32 || group == 64 || group == 128, SC_ERR_SHAPE,
@@ -1984,9 +2024,25 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
   const bool atomic_ok = epi == SC_EPI_RESIDUAL && y_dtype == SC_F32 && (const void*)residual == (const void*)y &&
                          ldr == ldy;
 
+  if (ar) {
+    // the all-reduce runs in the epilogue of ONE decode-GEMV pass: the plan
+    // (a function of the shape only, so every rank decides alike) must be the
+    // factored kernel without split-K, one output per consumer thread
+    const RowPass rp = plan_rows(M, K, N, bits, group, nacc, tma_ok, atomic_ok);
+    const int max_tiles = rp.pp.tma ? (rp.pp.sp.tiles + rp.pp.tp.grid_x - 1) / rp.pp.tp.grid_x : 0;
+    const bool fits = nseg == 1 && epi != SC_EPI_SWIGLU && !norm_w && y_dtype == SC_F32 && ldy == N &&
+                      rp.mb == M && !rp.hilo && rp.pp.tma && rp.pp.fx && rp.pp.sp.splits == 1 &&
+                      max_tiles * 16 * M <= TC_NCW * 32 && rp.pp.tp.grid_x <= P2P_MAX_CTR &&
+                      (size_t)M * N * 4 <= ar_max_bytes;
+    SC_REQUIRE(fits, SC_ERR_UNSUPPORTED,
+               "qlinear_allreduce: M=%d K=%d N=%d does not run as one unsplit decode-GEMV pass with an fp32 "
+               "output of at most %zu bytes (run sc_qlinear_fused + sc_p2p_allreduce)", M, K, N, ar_max_bytes);
+    p.ar = *ar;
+  }
+
   // More than 16 rows: the tensor-core GEMM (exact weights, x to ~22 bits)
   // when the shape and the workspace allow it; up to 16, decode-GEMV passes.
-  if (M > 16 && !knobs().nok2 && tma_ok &&
+  if (!ar && M > 16 && !knobs().nok2 && tma_ok &&
       qgemm_eligible(M, K, nseg, seg_rows, epi, bits, group) && ws &&
       ws_bytes >= qgemm_workspace_bytes(M, K, N, epi))
     return run_qgemm(x, x_dtype, M, K, ldx, norm_w, eps, nseg, wq, scales, biases, seg_rows, group, bits, bias, epi,
@@ -2007,6 +2063,10 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
     const TmaPlan* tp = nullptr;
     if (pp.tma && encode_maps(p, bits, nacc, &pp.tp.geo, &maps)) {
       tp = &pp.tp;
+    } else if (ar) {
+      // every rank must take the same path: refuse rather than fall back alone
+      set_error("qlinear_allreduce: tensor maps refused by the driver");
+      return SC_ERR_UNSUPPORTED;
     } else if (pp.tma) {
       // tensor maps unavailable: plan this pass for the direct-load kernel
       // (hi / lo rows when they fit its 16-row B tile)
@@ -2131,6 +2191,22 @@ int sc_qlinear_fused(const void* x, int x_dtype, int M, int K, int ldx, const ui
   return sc::run_qlinear(x, x_dtype, M, K, ldx, norm_weight, norm_eps, nseg, wq, scales, biases, seg_rows,
                          group_size, bits, bias, epilogue, y, y_dtype, ldy, residual, ldr, workspace,
                          workspace_bytes, nullptr, stream);
+}
+
+int sc_qlinear_allreduce(const void* x, int x_dtype, int M, int K, int ldx, const uint32_t* wq,
+                         const uint16_t* scales, const uint16_t* biases, int N, int group_size, int bits,
+                         const uint16_t* bias, float* y, const float* residual, void* p2p, cudaStream_t stream) {
+  sc::P2PArgs a;
+  size_t max_bytes = 0;
+  if (int st = sc::p2p_args_of(p2p, &a, &max_bytes)) return st;
+  SC_REQUIRE(a.world >= 2, SC_ERR_ARG, "qlinear_allreduce: transport of %d ranks", a.world);
+  const uint32_t* W[1] = {wq};
+  const uint16_t* S[1] = {scales};
+  const uint16_t* B[1] = {biases};
+  const int R[1] = {N};
+  return sc::run_qlinear(x, x_dtype, M, K, ldx, nullptr, 0.f, 1, W, S, B, R, group_size, bits, bias,
+                         residual ? SC_EPI_RESIDUAL : SC_EPI_STORE, y, SC_F32, N, residual, N, nullptr, 0, nullptr,
+                         stream, &a, max_bytes);
 }
 
 int sc_qlinear_fused_prefetch(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_weight,

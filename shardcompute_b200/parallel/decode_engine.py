@@ -60,7 +60,8 @@ class DecodeEngine:
 
     def __init__(self, weights: RankWeights, comm=None, max_batch: int = 1, max_seq: int = 2048,
                  device: Optional[torch.device] = None, attn_splits: Optional[int] = None,
-                 prefetch_mb: Optional[float] = None, one_kernel_step: Optional[bool] = None):
+                 prefetch_mb: Optional[float] = None, one_kernel_step: Optional[bool] = None,
+                 fused_allreduce: Optional[bool] = None):
         cfg: ModelConfig = weights.cfg
         self.cfg = cfg
         self.w = weights
@@ -116,6 +117,16 @@ class DecodeEngine:
         self.use_step = (one_kernel_step and self.B == 1 and self.bits == 4 and self.group == 64
                          and cfg.hidden_size % 512 == 0 and (self.Hq * self.hd) % 512 == 0 and self.F % 256 == 0
                          and self.F >= 512 and self.hd in (64, 128) and (self.Hq // self.Hkv) in (1, 2, 4, 8))
+        # TP > 1: the o / down GEMVs run their all-reduce in the epilogue
+        # (sc_qlinear_allreduce, over a transport of their own) where the
+        # pass allows it (argument, or SC_FUSED_AR=0 to keep the pair)
+        if fused_allreduce is None:
+            fused_allreduce = os.environ.get("SC_FUSED_AR", "1") != "0"
+        self._ar_p2p = None
+        if (fused_allreduce and self.world > 1 and not self.use_step and getattr(comm, "backend", None) == "nccl"
+                and comm.p2p_enabled):
+            self._ar_p2p = comm.fused_transport(self.B * self.H * 4)
+        self.fused_ar_calls = 0  # row-parallel GEMVs that ran with the all-reduce in the epilogue
         self._step = None
         self._step_ws: Optional[torch.Tensor] = None
         self.step_trace: Optional[torch.Tensor] = None   # [L+1, H] hidden states of the last step (debug)
@@ -277,11 +288,39 @@ class DecodeEngine:
             if hidden is not None:
                 hidden.append(h.clone())
 
+    def _qlin_allreduce(self, x, tri, h) -> bool:
+        """h = sum over ranks (rank order) of x.W_r^T, + h on rank 0, by one
+        GEMV whose epilogue exchanges the partials over NVLink.  False (and
+        nothing launched, on every rank alike) when the pass does not allow it."""
+        M, K = x.shape
+        N = int(tri[0].shape[0])
+        if self._probe is not None:
+            slot = len(self._probe)
+            L.call("sc_qgemv_probe_stamps", self._stamps[slot].data_ptr())
+        st = L.load().sc_qlinear_allreduce(
+            x.data_ptr(), ops._dt(x), M, K, K, tri[0].data_ptr(), tri[1].data_ptr(), tri[2].data_ptr(), N,
+            self.group, self.bits, None, h.data_ptr(), h.data_ptr() if self.rank == 0 else None, self._ar_p2p,
+            ops.stream_handle(self.device))
+        if self._probe is not None:
+            L.call("sc_qgemv_probe_stamps", None)
+        if st == L.SC_ERR_UNSUPPORTED:
+            return False
+        L.check(st, "sc_qlinear_allreduce")
+        if self._probe is not None:
+            nbytes = (N * K * self.bits // 8 + N * (K // self.group) * 4 + M * K * x.element_size() +
+                      M * N * 4 + (M * N * 4 if self.rank == 0 else 0))
+            self._probe.append((slot, nbytes))
+        self.fused_ar_calls += 1
+        return True
+
     def _row_out(self, x, tri, h, part, prefetch_next=None):
         """Row-parallel linear + residual.  TP=1: h += x.W^T in place.  TP>1:
-        rank 0 writes h + x.W^T, others x.W^T, and the all-reduce of those
-        partials lands in h (the residual is added exactly once).  The next
-        GEMV's weights are prefetched by this GEMV's producer."""
+        one GEMV with the all-reduce in its epilogue where the pass allows it;
+        otherwise rank 0 writes h + x.W^T, others x.W^T, and the all-reduce of
+        those partials lands in h (the residual is added exactly once).  The
+        next GEMV's weights are prefetched by this GEMV's producer."""
+        if self.world > 1 and self._ar_p2p is not None and self._qlin_allreduce(x, tri, h):
+            return
         if self.world == 1:
             self._qlin(x, [tri], h, epilogue=L.SC_EPI_RESIDUAL, residual=h, prefetch=prefetch_next)
         elif self.rank == 0:

@@ -150,6 +150,78 @@ def _cfg1_rank_main(rank, world, port, q):
         q.put((rank, traceback.format_exc(), None))
 
 
+def _fused_ar_rank_main(rank, world, port, q):
+    """The row-parallel GEMVs with the all-reduce in their epilogue
+    (``sc_qlinear_allreduce``) against the GEMV + all-reduce pair on the same
+    ranks: the same bits of the final hidden state and of this rank's logits
+    after every decode step, the same greedy tokens (graph-captured too),
+    agreement with the oracle, and the pair kept where a pass cannot fuse."""
+    try:
+        sys.path.insert(0, ROOT)
+        import torch
+
+        from oracle import sharder as osh
+        from oracle import synth
+        from oracle.tp import TPModel
+        from shardcompute_b200.collectives import Communicator
+        from shardcompute_b200.model.config import ModelConfig
+        from shardcompute_b200.parallel import DecodeEngine, RankWeights
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        shape = (synth.tiny_shape(num_layers=2, num_heads=8, num_kv_heads=4) if world <= 4 else
+                 synth.tiny_shape(num_layers=2, hidden_size=1024, num_heads=16, num_kv_heads=8,
+                                  intermediate_size=2048))
+        full = synth.checkpoint(shape, seed=17)
+        shards = [osh.shard_weights(full, world, r) for r in range(world)]
+        comm = Communicator(rank, world, host="127.0.0.1", port=port, backend="nccl")
+        comm.initialize_sync(timeout=60)
+        assert comm.p2p_enabled
+        cfg = ModelConfig.from_dict(synth.model_config_dict(shape))
+        w = RankWeights.from_shard(cfg, shards[rank], world, rank, shape.bits, shape.group_size, dev)
+        prompt = torch.from_numpy(np.random.default_rng(5).integers(0, shape.vocab_size, size=(1, 7))).to(dev)
+        engs = [DecodeEngine(w, comm, max_batch=1, max_seq=64, device=dev, fused_allreduce=f) for f in (False, True)]
+        assert engs[0]._ar_p2p is None and engs[1]._ar_p2p is not None
+        traces = []
+        for eng in engs:
+            eng.reset()
+            eng.prefill(prompt)  # 7 rows: no fused pass, the pair runs
+            assert eng.fused_ar_calls == 0
+            tr = []
+            for _ in range(8):
+                eng.decode_step()
+                bf = eng._buffers(1, 1)
+                tr.append((bf["h"].clone(), bf["logits"].clone(), int(eng.tok[0])))
+            traces.append(tr)
+        # every step fuses the same GEMVs (a tiny o_proj K may plan as a pass the epilogue cannot take)
+        n_f = engs[1].fused_ar_calls
+        assert n_f > 0 and n_f % 8 == 0 and n_f <= 8 * 2 * shape.num_layers, n_f
+        for step, (a, b) in enumerate(zip(*traces)):
+            assert torch.equal(a[0], b[0]), f"rank {rank} step {step}: hidden state differs"
+            assert torch.equal(a[1], b[1]), f"rank {rank} step {step}: logits differ"
+            assert a[2] == b[2], f"rank {rank} step {step}: token differs"
+        gen = [eng.generate(prompt, 16).cpu().numpy() for eng in engs]  # graph-captured steps
+        assert np.array_equal(gen[0], gen[1]), f"rank {rank}: captured greedy tokens differ"
+        ref_toks = TPModel(shards, shape, max_len=64).generate(prompt.cpu().numpy(), 16)
+        agree = float(np.mean(gen[1] == ref_toks))
+        assert agree >= 0.99, f"rank {rank}: greedy agreement with the oracle {agree:.2f}"
+        # batch 4 at 4-bit g64 takes two GEMV passes: the pair stays
+        e4 = DecodeEngine(w, comm, max_batch=4, max_seq=64, device=dev, fused_allreduce=True)
+        e4.reset()
+        e4.prefill(prompt.repeat(4, 1))
+        e4.decode_step()
+        assert e4.fused_ar_calls == 0
+        torch.cuda.synchronize()
+        assert comm.poll() == 0
+        for eng in engs + [e4]:
+            eng.graph = None
+        torch.cuda.synchronize()
+        comm.shutdown_sync()
+        q.put((rank, "ok", gen[1].tolist()))
+    except BaseException:  # noqa: BLE001 - report to the parent
+        q.put((rank, traceback.format_exc(), None))
+
+
 def _pp_rank_main(rank, world, port, q):
     """NCCL point-to-point: Communicator.send / recv of CUDA tensors (shape
     and dtype through the store), then a two-stage pipeline transfer as the
@@ -266,6 +338,11 @@ def test_one_kernel_step_matches_oracle(world):
     """The persistent one-kernel step with its in-kernel NVLink exchange (row
     sums and the argmax) at TP ``world``."""
     _spawn(_rank_main_one_kernel, world)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_row_parallel_allreduce_matches_the_pair(world):
+    _spawn(_fused_ar_rank_main, world)
 
 
 def test_nccl_send_recv_and_pipeline_stage_transfer():
