@@ -243,13 +243,24 @@ static int p2p_check_device(const P2P* h) {
   return SC_OK;
 }
 
-int p2p_args_of(void* p2p, P2PArgs* out, size_t* max_bytes) {
+// Writes the transport's kernel-side view into its arena header (for kernels
+// that take it by address) once every peer is mapped.
+static int p2p_publish(const P2P* h) {
+  for (int q = 0; q < h->world; ++q)
+    if (!h->peer[q]) return SC_OK;
+  const P2PArgs a = p2p_args(h);
+  return cuda_status(cudaMemcpy(h->arena + P2P_ARGS_OFF, &a, sizeof(a), cudaMemcpyHostToDevice),
+                     "p2p: publishing the transport's arguments");
+}
+
+int p2p_args_of(void* p2p, P2PArgs* out, size_t* max_bytes, const P2PArgs** dev_args) {
   SC_REQUIRE(p2p && out, SC_ERR_ARG, "p2p: null transport");
   const P2P* h = static_cast<const P2P*>(p2p);
   for (int q = 0; q < h->world; ++q) SC_REQUIRE(h->peer[q], SC_ERR_ARG, "p2p: rank %d not mapped", q);
   if (int st = p2p_check_device(h)) return st;
   *out = p2p_args(h);
   if (max_bytes) *max_bytes = h->max_bytes;
+  if (dev_args) *dev_args = reinterpret_cast<const P2PArgs*>(h->arena + P2P_ARGS_OFF);
   return SC_OK;
 }
 
@@ -337,7 +348,7 @@ int sc_p2p_open(void* p2p, const void* handles, size_t handle_bytes) {
     h->peer[q] = static_cast<char*>(ptr);
     h->mapped[q] = true;
   }
-  return SC_OK;
+  return p2p_publish(h);
 }
 
 int sc_p2p_open_loopback(void* p2p) {
@@ -346,7 +357,7 @@ int sc_p2p_open_loopback(void* p2p) {
   P2P* h = static_cast<P2P*>(p2p);
   for (int q = 0; q < h->world; ++q)
     if (!h->peer[q]) h->peer[q] = h->arena;
-  return SC_OK;
+  return p2p_publish(h);
 }
 
 int sc_p2p_set_timeout(void* p2p, uint64_t timeout_ns) {
@@ -355,7 +366,7 @@ int sc_p2p_set_timeout(void* p2p, uint64_t timeout_ns) {
   SC_REQUIRE(timeout_ns >= 1000000ull && timeout_ns <= 60000000000ull, SC_ERR_ARG,
              "p2p_set_timeout: %llu ns outside [1 ms, 60 s]", (unsigned long long)timeout_ns);
   static_cast<P2P*>(p2p)->timeout_ns = timeout_ns;
-  return SC_OK;
+  return p2p_publish(static_cast<P2P*>(p2p));
 }
 
 int sc_p2p_status(void* p2p, int* timed_out) {

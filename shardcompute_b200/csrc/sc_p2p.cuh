@@ -10,8 +10,9 @@
 namespace sc {
 
 constexpr int P2P_MAX_WORLD = 8;
-constexpr size_t P2P_HDR = 4096;   // per-block counters (up to 512), error word at 2048
+constexpr size_t P2P_HDR = 4096;   // per-block counters (up to 512), error word at 2048, P2PArgs at 3072
 constexpr size_t P2P_ERR_OFF = 2048;
+constexpr size_t P2P_ARGS_OFF = 3072;  // a device copy of the transport's P2PArgs, written when it is opened
 constexpr int P2P_MAX_CTR = (int)(P2P_ERR_OFF / 4);
 
 // A transport as its kernels see it.
@@ -25,10 +26,13 @@ struct P2PArgs {
   int world, rank;
 };
 
+static_assert(sizeof(P2PArgs) <= P2P_HDR - P2P_ARGS_OFF, "P2PArgs must fit the arena header");
+
 // The kernel-side view of a transport made by sc_p2p_create / sc_p2p_open,
-// and its largest message; an error status for a null handle, a peer not
-// mapped or another current device.
-int p2p_args_of(void* p2p, P2PArgs* out, size_t* max_bytes);
+// its largest message and the device copy of that view (in the arena's
+// header); an error status for a null handle, a peer not mapped or another
+// current device.
+int p2p_args_of(void* p2p, P2PArgs* out, size_t* max_bytes, const P2PArgs** dev_args);
 
 __device__ __forceinline__ void st_volatile_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)

@@ -31,6 +31,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -77,10 +78,11 @@ struct QGemvParams {
   int x_vec;             // x rows start on 16 bytes: 8 values load as one or two 16-byte vectors
   PrefetchList pf;       // the next kernel's weights, pulled into L2 by the decode kernel's producer
   unsigned long long* stamp;  // null, or {first consumer start after the dependency wait, last exit} (%globaltimer)
-  // Row-parallel all-reduce in the epilogue (world > 1): every CTA pushes its
-  // outputs to every peer as {value, epoch} half lines, then sums each output
-  // over the ranks in rank order into y (fp32).  world == 0: off.
-  P2PArgs ar;
+  // Row-parallel all-reduce in the epilogue (the transport's device copy of
+  // its P2PArgs; null: off): every CTA pushes its outputs to every peer as
+  // {value, epoch} half lines, then sums each output over the ranks in rank
+  // order into y (fp32).  Only the kernel instances built with AR read it.
+  const P2PArgs* ar;
 };
 
 // The stamp pointer the next sc_qlinear* launches of this host thread carry
@@ -1074,7 +1076,9 @@ __device__ __forceinline__ void stage_x_fx_warp(const QGemvParams& p, unsigned c
   __syncwarp();
 }
 
-template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
+// AR: the epilogue runs the row-parallel all-reduce (p.ar); a template
+// parameter, so the other instances carry none of its code.
+template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT, bool AR = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ TmaMaps maps) {
   using TR = QTraits<BITS>;
@@ -1194,12 +1198,15 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
   if (p.stamp && tid == 0) atomicMin(p.stamp, (unsigned long long)globaltimer_ns());
   __shared__ uint32_t s_ep;    // this CTA's epoch of the fused all-reduce
   __shared__ int s_ar_skip;    // the transport already failed: no waits
-  if (p.ar.world > 1 && tid == 0) {
-    // the previous fused call (an earlier kernel) is complete: its counter is final
-    const uint32_t e = p.ar.ctr[blockIdx.x] + 1;
-    p.ar.ctr[blockIdx.x] = e;
-    s_ep = e;
-    s_ar_skip = *reinterpret_cast<volatile int*>(p.ar.err) != 0;
+  if constexpr (AR) {
+    if (tid == 0) {
+      // the previous fused call (an earlier kernel) is complete: its counter is final
+      const P2PArgs& A = *p.ar;
+      const uint32_t e = A.ctr[blockIdx.x] + 1;
+      A.ctr[blockIdx.x] = e;
+      s_ep = e;
+      s_ar_skip = *reinterpret_cast<volatile int*>(A.err) != 0;
+    }
   }
   // The epilogue's global reads (residual, bias) do not depend on this
   // kernel's results: when every consumer thread owns at most one output of
@@ -1483,27 +1490,28 @@ qgemv_fx_kernel(const QGemvParams p, const TmaGeo geo, const __grid_constant__ T
       for (int a = 0; a < NACC; ++a) v[a] = v[a] / r;
     }
     if (row >= p.N) continue;
-    if (p.ar.world > 1) {
+    if constexpr (AR) {
       // this rank's partial (the value the unfused path writes before its
       // all-reduce) to every peer: half line e of region (set, this rank)
+      const P2PArgs& A = *p.ar;
       const float part = (v[0] + pre_bias) + pre_res;
       const uint32_t ep = s_ep;
       const size_t e = (size_t)mm * p.N + row;
-      for (int k = 1; k < p.ar.world; ++k) {
-        const int dst = (p.ar.rank + k) % p.ar.world;  // staggered: ranks do not all hit one peer first
-        char* reg = p.ar.data[dst] + (size_t)((ep & 1) * p.ar.world + p.ar.rank) * p.ar.region_bytes;
+      for (int k = 1; k < A.world; ++k) {
+        const int dst = (A.rank + k) % A.world;  // staggered: ranks do not all hit one peer first
+        char* reg = A.data[dst] + (size_t)((ep & 1) * A.world + A.rank) * A.region_bytes;
         st_volatile_v2(reg + e * 8, __float_as_uint(part), ep);
       }
       // the sum over ranks in rank order from zero: the unfused all-reduce's order, so its bits
       bool skip = s_ar_skip != 0;
       uint64_t t0 = 0;
       float acc = 0.f;
-      for (int q = 0; q < p.ar.world; ++q) {
-        if (q == p.ar.rank) {
+      for (int q = 0; q < A.world; ++q) {
+        if (q == A.rank) {
           acc += part;
         } else {
-          const char* reg = p.ar.data[p.ar.rank] + (size_t)((ep & 1) * p.ar.world + q) * p.ar.region_bytes;
-          acc += __uint_as_float(p2p_recv_half(p.ar, reg + e * 8, ep, &skip, &t0));
+          const char* reg = A.data[A.rank] + (size_t)((ep & 1) * A.world + q) * A.region_bytes;
+          acc += __uint_as_float(p2p_recv_half(A, reg + e * 8, ep, &skip, &t0));
         }
       }
       reinterpret_cast<float*>(p.y)[(size_t)mm * p.ldy + row] = acc;
@@ -1821,9 +1829,9 @@ static int launch_qgemv(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, 
   return check_launch("qgemv_splitk_reduce");
 }
 
-template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
-static int launch_qgemv_fx(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, cudaStream_t stream) {
-  auto kern = qgemv_fx_kernel<BITS, NGC, EPI, NORM, XT, YT>;
+template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT, bool AR>
+static int launch_qgemv_fx_k(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, cudaStream_t stream) {
+  auto kern = qgemv_fx_kernel<BITS, NGC, EPI, NORM, XT, YT, AR>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM_BUDGET);
@@ -1837,6 +1845,20 @@ static int launch_qgemv_fx(QGemvParams& p, const TmaPlan* tp, const TmaMaps* map
   const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)4 * sm_count());
   ::sc::launch(qgemv_splitk_reduce<EPI, YT>, rb, 256, 0, stream, p);
   return check_launch("qgemv_splitk_reduce");
+}
+
+template <int BITS, int NGC, int EPI, bool NORM, typename XT, typename YT>
+static int launch_qgemv_fx(QGemvParams& p, const TmaPlan* tp, const TmaMaps* maps, cudaStream_t stream) {
+  // the all-reduce epilogue exists for the shapes the host admits to it:
+  // one weight set, no RMSNorm prologue, fp32 output
+  if constexpr (EPI != SC_EPI_SWIGLU && !NORM && std::is_same<YT, float>::value) {
+    if (p.ar) return launch_qgemv_fx_k<BITS, NGC, EPI, NORM, XT, YT, true>(p, tp, maps, stream);
+  }
+  if (p.ar) {
+    set_error("qlinear_allreduce: no all-reduce epilogue for this kernel instance");
+    return SC_ERR_UNSUPPORTED;
+  }
+  return launch_qgemv_fx_k<BITS, NGC, EPI, NORM, XT, YT, false>(p, tp, maps, stream);
 }
 
 template <int BITS, int NGC, int EPI, bool NORM>
@@ -1974,7 +1996,7 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
                        const uint16_t* const* biases, const int* seg_rows, int group, int bits,
                        const uint16_t* bias, int epi, void* y, int y_dtype, int ldy, const float* residual,
                        int ldr, void* ws, size_t ws_bytes, const PrefetchList* pf, cudaStream_t stream,
-                       const P2PArgs* ar = nullptr, size_t ar_max_bytes = 0) {
+                       const P2PArgs* ar = nullptr, size_t ar_max_bytes = 0, const P2PArgs* ar_dev = nullptr) {
   SC_REQUIRE(x && y && wq && scales && biases && seg_rows, SC_ERR_ARG, "qlinear: null pointer argument");
   SC_REQUIRE(bits == 4 || bits == 8, SC_ERR_SHAPE, "qlinear: bits must be 4 or 8 (got %d)", bits);
   SC_REQUIRE(group == 32 || group == 64 || group == 128, SC_ERR_SHAPE,
@@ -2037,7 +2059,7 @@ static int run_qlinear(const void* x, int x_dtype, int M, int K, int ldx, const 
     SC_REQUIRE(fits, SC_ERR_UNSUPPORTED,
                "qlinear_allreduce: M=%d K=%d N=%d does not run as one unsplit decode-GEMV pass with an fp32 "
                "output of at most %zu bytes (run sc_qlinear_fused + sc_p2p_allreduce)", M, K, N, ar_max_bytes);
-    p.ar = *ar;
+    p.ar = ar_dev;
   }
 
   // More than 16 rows: the tensor-core GEMM (exact weights, x to ~22 bits)
@@ -2198,7 +2220,8 @@ int sc_qlinear_allreduce(const void* x, int x_dtype, int M, int K, int ldx, cons
                          const uint16_t* bias, float* y, const float* residual, void* p2p, cudaStream_t stream) {
   sc::P2PArgs a;
   size_t max_bytes = 0;
-  if (int st = sc::p2p_args_of(p2p, &a, &max_bytes)) return st;
+  const sc::P2PArgs* a_dev = nullptr;
+  if (int st = sc::p2p_args_of(p2p, &a, &max_bytes, &a_dev)) return st;
   SC_REQUIRE(a.world >= 2, SC_ERR_ARG, "qlinear_allreduce: transport of %d ranks", a.world);
   const uint32_t* W[1] = {wq};
   const uint16_t* S[1] = {scales};
@@ -2206,7 +2229,7 @@ int sc_qlinear_allreduce(const void* x, int x_dtype, int M, int K, int ldx, cons
   const int R[1] = {N};
   return sc::run_qlinear(x, x_dtype, M, K, ldx, nullptr, 0.f, 1, W, S, B, R, group_size, bits, bias,
                          residual ? SC_EPI_RESIDUAL : SC_EPI_STORE, y, SC_F32, N, residual, N, nullptr, 0, nullptr,
-                         stream, &a, max_bytes);
+                         stream, &a, max_bytes, a_dev);
 }
 
 int sc_qlinear_fused_prefetch(const void* x, int x_dtype, int M, int K, int ldx, const uint16_t* norm_weight,
